@@ -1,0 +1,462 @@
+"""Benchmark of the B200 decode sparse-attention path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (config 2): batched decode, attention path only, all 43 layers;
+64 sequences per GPU at 32768 raw-token context (8192 compressed entries),
+indexer top-2048 plus a 128-token window, every layer with its own seeded
+caches, indexer weights and sinks.  One "step" = one decode step of all 43
+layers (act_quant + window write, indexer compressor, indexer score, top-k,
+attention compressor, sparse attention) for the 64 sequences, positions
+advancing on the device.  Inputs are synthetic (seeded ~N(0,1), indexer
+weights ~N(0,0.02)); the 29 GB of caches per GPU are far larger than L2, so
+no L2 flush is needed between steps.
+
+Multi-GPU (torchrun): batch split with no collective on the path - each rank
+runs its own 64 sequences ("scaling": "weak"); the step time is the max over
+ranks of the CUDA-event time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tt-deepseek-v4_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "sparse-attn decode µs/layer & tok/s; HBM GB/s % of peak at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=43)
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU")
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--topk", type=int, default=2048)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--breakdown", action="store_true", help="print per-kernel timings to stderr")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def read_traffic():
+    """Per-launch DRAM traffic of each kernel from the committed ncu summary
+    (profiles/roofline_traffic.txt: `kernel workload bytes_per_launch`)."""
+    out = {}
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.txt")
+    if os.path.exists(p):
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 3 and not line.startswith("#"):
+                try:
+                    out[(parts[0], parts[1])] = float(parts[2])
+                except ValueError:
+                    pass
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ workload
+
+def algorithmic_bytes(B, t_active, k, W, H=64, D=512, Hi=64, Di=128):
+    """Bytes the algorithm must move per layer-step for B sequences (gathered
+    rows, not the full cache), per kernel."""
+    K = W + k
+    attn = B * (K * D * 2 + H * D * 2 * 2 + K * 4)          # gather + q + o + indices
+    idx = B * (t_active * Di * 2 + Hi * Di * 2 + Hi * 4 + t_active * 4)  # keys + q + w + scores
+    topk = B * (t_active * 4 + k * 4)
+    cmp = B * (2 * (2 * D) * 2 + 2 * (2 * Di) * 2 + (2 * 8 * 2 * D * 4) // 4 + (2 * 8 * 2 * Di * 4) // 4 + 2 * D)
+    kvw = B * (D * 2 * 2)
+    return {"sparse_attn": attn, "indexer_score": idx, "indexer_topk": topk, "compressor": cmp,
+            "kv_window_write": kvw}
+
+
+def build_path(args, dev, seed):
+    import torch
+    from dsv4attn.layer import DecodeLayer, DecodePath, LayerInputs
+    from dsv4attn.tables import PathArgs
+    pa = PathArgs(index_topk=args.topk)
+    max_seq = args.ctx + 4096
+    g = torch.Generator(device=dev).manual_seed(seed)
+    layers = []
+    for li in range(args.layers):
+        L = DecodeLayer(pa, args.batch, max_seq, dev)
+        L.kv_cache.normal_(generator=g)
+        L.idx_cache.normal_(generator=g)
+        L.cmp_kv.normal_(generator=g)
+        L.cmp_sc.normal_(generator=g)
+        L.icmp_kv.normal_(generator=g)
+        L.icmp_sc.normal_(generator=g)
+        L.ape.normal_(generator=g)
+        L.iape.normal_(generator=g)
+        L.gamma.normal_(generator=g).mul_(0.02).add_(1.0)
+        L.igamma.normal_(generator=g).mul_(0.02).add_(1.0)
+        L.sink.normal_(generator=g)
+        layers.append(L)
+    path = DecodePath(layers, max_seq)
+    inputs = []
+    for li in range(args.layers):
+        x = LayerInputs.empty(pa, args.batch, dev)
+        for t in x.tensors():
+            t.normal_(generator=g)
+        x.iw.mul_(0.02)
+        inputs.append(x)
+    outs = [torch.empty(args.batch, 64, 512, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
+    return pa, path, inputs, outs
+
+
+def time_kernels(path, inputs, outs, reps=3):
+    """CUDA-event time per launch of each kernel kind, each looped over all
+    layers (distinct caches, so nothing stays in L2) on the launching stream."""
+    import torch
+    from dsv4attn import ops
+    st = torch.cuda.current_stream()
+    res = {}
+    a = path.args
+
+    def run(name, fn):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        best = None
+        for _ in range(reps):
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / len(path.layers)
+            best = ms if best is None else min(best, ms)
+        res[name] = best
+
+    run("sparse_attn", lambda: [ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, path.scale, out=o, ws=L.ws)
+                                for L, x, o in zip(path.layers, inputs, outs)])
+    run("indexer_score", lambda: [ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score,
+                                                    t_valid=path.t_active) for L, x in zip(path.layers, inputs)])
+    run("indexer_topk", lambda: [ops.indexer_topk(L.score, path.t_active, L.k, L.win, T=L.T_max, mask_mode=1,
+                                                  out=L.idx[:, L.win:], ws=L.ws) for L in path.layers])
+    return res
+
+
+def cpu_baseline_sample(args, seconds=12.0, n_seq=2):
+    """Time the CPU oracle (all host threads) on a bounded sample of the same
+    workload: n_seq sequences of one layer at full config-2 shapes; report
+    tok/s for the 43-layer step."""
+    import torch
+    import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    W, k, ctx = 128, args.topk, args.ctx
+    T = ctx // 4
+    B = n_seq
+    cos, sin = O.rope_tables(64, ctx + 8, compressed=True)
+    ckv, csc = O.compressor_init_state(B, 512, 4, True)
+    ikv, isc = O.compressor_init_state(B, 128, 4, True)
+    st = O.LayerState(kv_cache=torch.randn(B, W + T + 4, 512, generator=g).to(torch.bfloat16),
+                      idx_kv_cache=torch.randn(B, T + 4, 128, generator=g).to(torch.bfloat16),
+                      cmp_kv=ckv.normal_(generator=g), cmp_sc=csc.normal_(generator=g), icmp_kv=ikv.normal_(generator=g),
+                      icmp_sc=isc.normal_(generator=g), ape=torch.randn(4, 1024, generator=g),
+                      gamma=torch.ones(512), iape=torch.randn(4, 256, generator=g), igamma=torch.ones(128),
+                      sink=torch.randn(64, generator=g), cos=cos, sin=sin, win=W, ratio=4, index_topk=k,
+                      scale=512 ** -0.5)
+    bf = torch.bfloat16
+    x = [torch.randn(B, 1, 64, 512, generator=g).to(bf), torch.randn(B, 512, generator=g).to(bf),
+         torch.randn(B, 1024, generator=g), torch.randn(B, 1024, generator=g),
+         torch.randn(B, 64, 128, generator=g).to(bf), torch.randn(B, 256, generator=g),
+         torch.randn(B, 256, generator=g), 0.02 * torch.randn(B, 64, generator=g)]
+    pos = ctx - 1          # every repetition is the same decode step (state rewritten in place)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        O.decode_layer_step(st, pos, *x)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / n          # seconds per layer-step of n_seq sequences
+    tok_s = n_seq / (dt * args.layers)
+    return {"value": tok_s, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} decode steps of 1 layer x {n_seq} sequences at config-2 shapes (T=8192, k={k}, W=128), "
+                      f"{dt * 1e3:.1f} ms per layer-step, scaled to {args.layers} layers"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's own CPU path is not runnable here (it
+    needs ttnn/tt-lang on Tenstorrent hardware), so the oracle port stands in,
+    timed on the host cores; rank 0 only."""
+    if rank != 0:
+        return
+    cb = cpu_baseline_sample(args, seconds=max(8.0, 2.0 * args.steps))
+    line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.batch * 1e3 / cb["value"] if cb["value"] else None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) caches, indexer weights N(0,0.02))",
+            "config": {"workload": "cfg2 batched decode, 43 layers, 64 seq/GPU, ctx 32768, top-2048 + window 128",
+                       "global_batch": args.batch * world, "seq_len": args.ctx, "parallelism": f"dp{world}"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from dsv4attn import ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    pa, path, inputs, outs = build_path(args, dev, seed=1234 + rank)
+    path.set_positions(args.ctx - 1)
+    torch.cuda.synchronize()
+
+    graph = path.capture(inputs, outs, warmup=1)
+    path.set_positions(args.ctx - 1)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_total = e0.elapsed_time(e1)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    if int(path.status.item()) != 0:
+        raise RuntimeError("an attention index fell outside the cache during the bench")
+    ms_step = ms_total / args.steps
+    tok_s = world * args.batch * args.steps / (ms_total / 1e3)
+    us_layer = ms_step * 1e3 / args.layers
+
+    t_active = (args.ctx + args.warmup + args.steps) // 4
+    ab = algorithmic_bytes(args.batch, t_active, args.topk, 128)
+    bytes_step = sum(ab.values()) * args.layers
+    hbm, hbm_kind = peaks()
+
+    # per-kernel CUDA-event timings -> dominant kernel roofline
+    kt = time_kernels(path, inputs, outs)
+    dom = max(kt, key=kt.get)
+    achieved = ab[dom] / (kt[dom] * 1e-3) / 1e9
+    traffic = read_traffic().get((dom, "cfg2"))
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "traffic": traffic,
+                "peak_kind": f"{hbm_kind} (MEASURED_PEAKS.json hbm_gbs)" if hbm_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_launch": ab[dom], "us_per_launch": round(kt[dom] * 1e3, 2),
+                "kernels_us": {k: round(v * 1e3, 2) for k, v in kt.items()}}
+    step_gbs = bytes_step / (ms_step * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(args, path, inputs, outs, dev, world)
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "us_per_layer": round(us_layer, 2),
+            "step_hbm_gbs": round(step_gbs, 1), "step_hbm_frac": round(step_gbs / hbm, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) caches/inputs, indexer weights N(0,0.02), random-init layer params)",
+            "config": {"workload": "cfg2 batched decode: 43 layers, 64 seq/GPU, ctx 32768 (8192 compressed), "
+                                   "indexer top-2048 + window 128, H=64 D=512, Hi=64 Di=128",
+                       "global_batch": args.batch * world, "seq_len": args.ctx, "layers": args.layers,
+                       "parallelism": f"dp{world} (batch split, no collective)",
+                       "l2": "working set 29 GB/GPU >> 126 MB L2; no flush needed"},
+            "roofline": roofline, "clocks": clk, "gpu_launches": path.launches_per_step() * args.steps,
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+    if rank == 0 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline_sample(args)
+    if world > 1:
+        dist.barrier()
+        path.graph = None
+        del graph
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_e2e(args, path, inputs, outs, dev, world):
+    """Same metric through the public API with HOST buffers: every step copies
+    all 43 layers' inputs from pinned host memory and reads all outputs back.
+    Copies run on side streams, pipelined against the previous step's graph
+    (two input/output buffer sets, one captured graph each)."""
+    import torch
+    from dsv4attn.layer import LayerInputs
+    B, nl = args.batch, args.layers
+    host_in = []
+    for x in inputs:
+        h = LayerInputs.empty(path.args, B, dev, pin=True)
+        for a, b in zip(h.tensors(), x.tensors()):
+            a.copy_(b)
+        host_in.append(h)
+    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+    sets = [(inputs, outs)]
+    in2 = [LayerInputs(*[t.clone() for t in x.tensors()]) for x in inputs]
+    out2 = [torch.empty_like(o) for o in outs]
+    sets.append((in2, out2))
+    graphs = [path.graph]
+    path.graph = None
+    graphs.append(path.capture(in2, out2, warmup=0))
+    path.graph = graphs[0]
+    path.set_positions(args.ctx - 1)
+    torch.cuda.synchronize()
+    comp = torch.cuda.current_stream()
+    h2d = torch.cuda.Stream(dev)
+    d2h = torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    out_free = [torch.cuda.Event() for _ in range(2)]
+    h2d_bytes = sum(x.nbytes() for x in host_in)
+    d2h_bytes = sum(o.numel() * o.element_size() for o in outs)
+
+    def issue(step):
+        s = step & 1
+        ins, os_ = sets[s]
+        with torch.cuda.stream(h2d):
+            if step >= 2:
+                h2d.wait_event(done[s])          # graph of step-2 finished reading this set
+            for d, h in zip(ins, host_in):
+                d.copy_(h, non_blocking=True)
+            in_ready[s].record(h2d)
+        comp.wait_event(in_ready[s])
+        if step >= 2:
+            comp.wait_event(out_free[s])         # outputs of step-2 copied out
+        graphs[s].replay()
+        done[s].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(done[s])
+            for h, o in zip(host_out, os_):
+                h.copy_(o, non_blocking=True)
+            out_free[s].record(d2h)
+
+    for i in range(3):
+        issue(i)
+    torch.cuda.synchronize()
+    n = max(4, args.steps // 2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for i in range(n):
+        issue(3 + i)
+    comp.wait_stream(d2h)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    for g in graphs[1:]:
+        del g
+    return {"value": round(world * B * n / (ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": d2h_bytes, "steps": n, "ms_per_step": round(ms / n, 4),
+            "note": "pinned host inputs of all 43 layers H2D + all outputs D2H every step, pipelined with compute"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,217 @@
+/*
+ * dsv4attn.h - C ABI of the B200 (sm_100a) DeepSeek-V4-Flash decode
+ * sparse-attention path.
+ *
+ * Every entry point takes raw device pointers, element counts / strides and
+ * a CUDA stream, launches asynchronously on that stream and returns a
+ * status code (DSA_OK = 0, negative on error).  No entry point allocates
+ * device memory, synchronises the device or copies to or from the host:
+ * all buffers are owned by the caller, so every call can be captured in a
+ * CUDA graph.  Argument errors are detected on the host before any launch;
+ * dsa_last_error() returns a message for the calling thread.
+ *
+ * Each function names the reference interface it replaces
+ * (zoecarver/tt-deepseek-v4, file:line).  Tensor layouts are row-major;
+ * "bf16" is IEEE bfloat16, "e4m3" is OCP FP8 E4M3 (float8_e4m3fn).
+ */
+#ifndef DSV4ATTN_H
+#define DSV4ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* dsa_stream_t; /* == cudaStream_t */
+
+enum {
+  DSA_OK = 0,
+  DSA_ERR_ARG = -1,         /* bad shape / stride / alignment / null pointer */
+  DSA_ERR_CUDA = -2,        /* a CUDA launch or runtime call failed          */
+  DSA_ERR_UNSUPPORTED = -3, /* shape outside what the kernels are built for */
+  DSA_ERR_TIMEOUT = -4,     /* a bounded device-side wait expired            */
+  DSA_ERR_WORKSPACE = -5    /* caller-provided workspace too small           */
+};
+
+/* Library version (major*10000 + minor*100 + patch) and the last error
+ * message recorded on the calling host thread ("" if none). */
+int dsa_version(void);
+const char* dsa_last_error(void);
+
+/* ---------------------------------------------------------------- attn.kv */
+
+/* Block-wise max-abs FP8-E4M3 round trip of an [M, N] bf16 matrix along N.
+ * Per block of `block` columns: amax = max|x|; s = max(amax, eps) / fp8_max;
+ * q = e4m3_rn_satfinite(clamp(x / s, +-fp8_max)); out = bf16(float(q) * s).
+ * scales [M, N/block] fp32 (may be NULL); codes [M, N] e4m3 (may be NULL).
+ * Replaces the tt-lang factory
+ *   _compile_act_quant_block_kernel(M_pad, N, BLOCK, fp8_max, eps)(x, scaler, out)
+ *   inference.py:3383-3499, with the semantics of the ttnn chain
+ *   _device_act_quant_block inference.py:4578-4607 plus the e4m3 cast. */
+int dsa_act_quant_block(const void* x, void* out, float* scales, uint8_t* codes,
+                        int64_t M, int64_t N, int64_t ld_x, int64_t ld_out,
+                        int block, float fp8_max, float eps, dsa_stream_t stream);
+
+/* attn.kv + attn.kv_update for B sequences: act_quant_block on the first
+ * D - rope_dim dims of kv [B, D] bf16 (rope dims pass through) and write
+ * the row into the window ring kv_cache[b, pos[b] % win, :].
+ * kv_cache: bf16, batch stride cache_bstride elements, row stride D.
+ * pos: [B] int32 device array.  scales [B, (D-rope_dim)/block] (may be NULL).
+ * Replaces Lk-D1's act_quant stage + paged_update_cache:
+ *   inference.py:5997-6006 (_lk_d1_kernel), 6072-6079 (attn.kv_update). */
+int dsa_kv_window_write(const void* kv, void* kv_cache, float* scales,
+                        const int32_t* pos, int B, int D, int rope_dim,
+                        int64_t cache_bstride, int win, int block,
+                        dsa_stream_t stream);
+
+/* ---------------------------------------------------------- attn.compress */
+
+/* One compressor decode step for B sequences (one kernel):
+ *   state write: score_row += ape[pos % r]; kv/score rows stored at slot
+ *     (overlap ? r + pos % r : pos % r)               inference.py:4954-4991
+ *   if (pos + 1) % r == 0 (per sequence, read from device `pos`):
+ *     softmax over slots of the overlap view, weighted sum, RMSNorm(gamma,
+ *     eps), interleaved rotary of the last rope_dim dims with row
+ *     pos + 1 - r of cos/sin, optional orthonormal Hadamard (rotate != 0),
+ *     bf16 row written to kv_cache[b, slot_offset + pos / r], and (overlap)
+ *     slot shift rows [0,r) <- rows [r,2r)             inference.py:4997-5097
+ *       (cssn 3205-3364, fanout slot shift 3101-3186)
+ * kv_row/score_row: [B, coff*d] bf16 (row stride ld_row), coff = 1 + overlap.
+ * ape [r, coff*d] fp32.  kv_state/score_state: [B, coff*r, coff*d] fp32.
+ * gamma [d] fp32.  cos/sin [n_pos, rope_dim/2] fp32.  kv_cache bf16 rows
+ * of d, batch stride cache_bstride.  emitted (may be NULL): [B] int32 set
+ * to 1 where a row was emitted this step, 0 where not, -1 where the emit
+ * row or angle row fell outside kv_cache / the table (nothing written).
+ * write_state = 0 skips the state write (kv_row/score_row/ape unused):
+ * that is _emit_body alone.
+ * Replaces DeviceCompressor.forward_device (inference.py:4938) with its
+ * _emit_body (4997). */
+int dsa_compressor_step(const void* kv_row, const void* score_row, int64_t ld_row,
+                        const float* ape, float* kv_state, float* score_state,
+                        const float* gamma, const float* cos_tab, const float* sin_tab,
+                        int n_pos, void* kv_cache, int64_t cache_bstride,
+                        int64_t cache_rows, int slot_offset, const int32_t* pos,
+                        int32_t* emitted, int B, int d, int rope_dim, int ratio,
+                        int overlap, int rotate, int write_state, float eps,
+                        dsa_stream_t stream);
+
+/* ------------------------------------------------------------- attn.topk */
+
+/* Window ring indices for B sequences: idx[b, i] for i < win is the
+ * reference's per-position row of _build_window_topk_table (inference.py:
+ * 479-506, picked at 6020-6026): [0..p, -1...] while p < win, else
+ * [(p%win)+1 .. win-1, 0 .. p%win].  idx row stride ld_idx. */
+int dsa_window_indices(const int32_t* pos, int32_t* idx, int64_t ld_idx, int B,
+                       int win, dsa_stream_t stream);
+
+/* Indexer score s[b, t] = sum_h w[b, h] * relu(q[b, h, :] . k[b, t, :]),
+ * fp32 accumulation, for t < T.  q [B, H, Di] bf16; k bf16 rows of Di with
+ * batch stride k_bstride elements; w [B, H] fp32 (already scaled by
+ * Di^-1/2 * H^-1/2 when the caller follows the reference's fold);
+ * score [B, T] fp32 with row stride ld_score.  t_valid (may be NULL):
+ * device [B] int32; keys t >= t_valid[b] are neither read nor scored (their
+ * score entries are left untouched).  Requires H == 64, Di == 128.
+ * Replaces DeviceIndexer.forward_device_score's score stage
+ * (inference.py:5260-5275: matmul, relu*w, head sum). */
+int dsa_indexer_score(const void* q, const void* k, const float* w, float* score,
+                      const int32_t* t_valid, int B, int H, int Di, int T,
+                      int64_t k_bstride, int64_t ld_score, dsa_stream_t stream);
+
+/* Top-k of the masked indexer score, the reference's bucketed pad+mask
+ * path (inference.py:5823-5851): masked = s - 1e4 * (t >= t_active[b]);
+ * select the k largest of masked[b, 0:T]; out = t + win where
+ * masked >= -1000, else -1.  Ties at the k-th value are broken towards the
+ * lower index.  k <= T, k <= 4096.  Output order: descending score when
+ * sort_desc != 0 (the reference's sorted=True), else ascending position.
+ * out_idx [B, k] int32 (row stride ld_out); out_score (may be NULL) [B, k]
+ * fp32 masked scores in the same order.  mask_mode 0 is the reference's
+ * additive mask; mask_mode 1 treats positions t >= t_active[b] as -inf
+ * without reading them (identical output unless a score exceeds 9000, and
+ * lets the score buffer beyond t_active stay unwritten, see t_valid of
+ * dsa_indexer_score).  Rows with T > 16384 are selected
+ * in two levels and need caller workspace: use dsa_indexer_topk_ws with
+ * dsa_indexer_topk_workspace_size(B, T, k) bytes (dsa_indexer_topk returns
+ * DSA_ERR_WORKSPACE for them). */
+int dsa_indexer_topk(const float* score, int64_t ld_score, const int32_t* t_active,
+                     int32_t* out_idx, float* out_score, int64_t ld_out,
+                     int B, int T, int k, int win, int sort_desc, int mask_mode,
+                     dsa_stream_t stream);
+size_t dsa_indexer_topk_workspace_size(int B, int T, int k);
+int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_active,
+                        int32_t* out_idx, float* out_score, int64_t ld_out,
+                        int B, int T, int k, int win, int sort_desc, int mask_mode,
+                        void* workspace, size_t workspace_bytes, dsa_stream_t stream);
+
+/* Device-side position advance for graph-replayed decode: pos[b] += step;
+ * t_active[b] = (pos[b] + 1) / ratio (T_active of inference.py:6028; may
+ * be NULL).  Replaces the per-step host staging of pre_stage_decode
+ * (inference.py:5853-5885) when the step loop stays on the device. */
+int dsa_advance_positions(int32_t* pos, int32_t* t_active, int B, int ratio, int step,
+                          dsa_stream_t stream);
+
+/* Global top-k over candidate lists (sequence split): cand_score/cand_idx
+ * [B, n_cand] (fp32 masked score, int32 global compressed position, -1 =
+ * empty slot); selects the k best (ties: lower position), n_cand <= 16384,
+ * and writes out_idx = position + win (or -1 when the score is below -1000
+ * or the slot is empty) and out_score, [B, k], in descending-score order.
+ * This is the merge step of the per-shard top-k of the sequence split the
+ * reference plans in briefs/future_max_utilization.md:177-204; on one GPU
+ * it equals ttnn.topk over the full row (inference.py:5841-5842). */
+int dsa_topk_merge(const float* cand_score, const int32_t* cand_idx, int n_cand,
+                   int32_t* out_idx, float* out_score, int64_t ld_out, int B, int k,
+                   int win, dsa_stream_t stream);
+
+/* ------------------------------------------------------------ attn.sparse */
+
+/* Bytes of workspace dsa_sparse_attn needs for this shape (0 when it runs
+ * without splitting the key range). */
+size_t dsa_sparse_attn_workspace_size(int B, int S, int H, int D, int K);
+
+/* Sparse sink attention (DeviceSparseAttn.forward_device, inference.py:
+ * 4459-4501, with the index->mask conversion 4444-4457 folded in):
+ *   for query row m = b*S + s:  g = kv[b, max(idx[m, j], 0)];
+ *   z = (q[m] . g^T) * scale, -inf where idx[m, j] < 0;
+ *   m_h = max(max_j z, sink[h]);
+ *   p = e^{z - m_h} / (sum_j e^{z - m_h} + e^{sink[h] - m_h});  o = p . g.
+ * q [B*S, H, D] bf16; kv bf16 rows of D with batch stride kv_bstride and
+ * kv_rows rows per batch (indices >= kv_rows are an error the kernel
+ * clamps and reports through `status`); idx [B*S, K] int32 (row stride
+ * ld_idx); sink [H] fp32; out [B*S, H, D] bf16.  lse (may be NULL):
+ * [B*S, H] fp32 natural-log partition sum including the sink.
+ * workspace: >= dsa_sparse_attn_workspace_size() bytes (may be NULL when
+ * that is 0).  status (may be NULL): device int32, set non-zero if any
+ * index was >= kv_rows.  Requires H == 64, D == 512. */
+int dsa_sparse_attn(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,
+                    const int32_t* idx, int64_t ld_idx, const float* sink, void* out,
+                    float* lse, int B, int S, int H, int D, int K, float scale,
+                    void* workspace, size_t workspace_bytes, int32_t* status,
+                    dsa_stream_t stream);
+
+/* Un-normalised partial attention for a sequence split: like
+ * dsa_sparse_attn but without the sink and without normalisation; writes
+ * part_ml [B*S, H, 2] = (m, l) and part_o [B*S, H, D] fp32 with
+ * o = sum_j e^{z_j - m} g_j, l = sum_j e^{z_j - m} (m = -inf, l = 0, o = 0
+ * when every index is masked).  Partials of disjoint index sets combine
+ * with dsa_lse_combine.  (Per-shard step of the split planned in
+ * briefs/future_max_utilization.md:185-199.) */
+int dsa_sparse_attn_partial(const void* q, const void* kv, int64_t kv_bstride,
+                            int64_t kv_rows, const int32_t* idx, int64_t ld_idx,
+                            float* part_ml, float* part_o, int B, int S, int H, int D,
+                            int K, float scale, void* workspace, size_t workspace_bytes,
+                            int32_t* status, dsa_stream_t stream);
+
+/* Log-sum-exp merge of P partials with the sink counted once:
+ * part_ml [P, M, H, 2], part_o [P, M, H, D] fp32 (P-major, M = B*S rows);
+ * M_h = max(max_p m_p, sink_h); L = sum_p l_p e^{m_p - M_h} + e^{sink_h - M_h};
+ * out = sum_p o_p e^{m_p - M_h} / L as bf16 [M, H, D]. */
+int dsa_lse_combine(const float* part_ml, const float* part_o, const float* sink,
+                    void* out, int P, int M, int H, int D, dsa_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV4ATTN_H */

@@ -1,0 +1,217 @@
+"""GPU parity: attn.topk (window indices, indexer score, masked top-k,
+candidate merge) and attn.sparse (gather + sink-softmax attention) against
+the CPU oracle.
+
+Bars: top-k index sets identical except at documented
+near-ties - a position counts as a near-tie when its oracle score is within
+relative 1e-3 of the k-th oracle score; indexer scores within rtol 1e-3;
+attention outputs within rtol 2e-2 / atol 2e-2 of the fp32 oracle."""
+
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+NEAR_TIE_REL = 1e-3
+
+
+def assert_topk_sets(got_idx: torch.Tensor, want_idx: torch.Tensor, oracle_masked: torch.Tensor, win: int):
+    """Per row: the valid index sets match except for near-ties at the k-th
+    value of the oracle's masked scores."""
+    for b in range(got_idx.shape[0]):
+        g = set(int(v) for v in got_idx[b] if v >= 0)
+        w = set(int(v) for v in want_idx[b] if v >= 0)
+        if g == w:
+            continue
+        k = len(w)
+        kth = torch.topk(oracle_masked[b], k).values[-1]
+        tol = NEAR_TIE_REL * max(abs(float(kth)), 1e-6)
+        for v in g ^ w:
+            s = float(oracle_masked[b, v - win])
+            assert abs(s - float(kth)) <= tol, f"row {b}: index {v} score {s} vs k-th {float(kth)} is not a near-tie"
+        assert len(g) == len(w)
+
+
+def masked_scores(score, t_active):
+    T = score.shape[1]
+    ta = torch.as_tensor(t_active).reshape(-1, 1)
+    return score - 1e4 * (torch.arange(T).unsqueeze(0) >= ta).float()
+
+
+@pytest.mark.parametrize("pos", [0, 5, 127, 128, 200, 4095])
+def test_window_indices(cuda_dev, pos):
+    from dsv4attn import ops
+    got = ops.window_indices(torch.tensor([pos, pos + 1], dtype=torch.int32, device=cuda_dev), 128).cpu()
+    assert torch.equal(got[0], O.window_indices(pos, 128))
+    assert torch.equal(got[1], O.window_indices(pos + 1, 128))
+
+
+@pytest.mark.parametrize("B,T", [(1, 1024), (3, 1000), (2, 77), (64, 8192)])
+def test_indexer_score(cuda_dev, B, T):
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B * 100 + T)
+    q = torch.randn(B, 64, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, T + 5, 128, generator=g).to(torch.bfloat16)
+    w = 0.02 * torch.randn(B, 64, generator=g)
+    want = O.indexer_score(q, k[:, :T], w)
+    got = ops.indexer_score(q.to(cuda_dev), k.to(cuda_dev), w.to(cuda_dev), T).cpu()
+    torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-3 * float(want.abs().max()))
+
+
+def test_indexer_score_t_valid(cuda_dev):
+    from dsv4attn import ops
+    B, T = 2, 512
+    q = torch.randn(B, 64, 128).to(torch.bfloat16)
+    k = torch.randn(B, T, 128).to(torch.bfloat16)
+    w = 0.02 * torch.randn(B, 64)
+    out = torch.full((B, T), 123.0, device=cuda_dev)
+    tv = torch.tensor([100, 0], dtype=torch.int32, device=cuda_dev)
+    ops.indexer_score(q.to(cuda_dev), k.to(cuda_dev), w.to(cuda_dev), T, out=out, t_valid=tv)
+    want = O.indexer_score(q, k, w)
+    o = out.cpu()
+    torch.testing.assert_close(o[0, :100], want[0, :100], rtol=1e-3, atol=1e-4)
+    assert (o[0, 100:] == 123.0).all() and (o[1] == 123.0).all()
+
+
+def test_topk_reference_case(cuda_dev):
+    # T_PAD 128, bucket 128, k 64, T_active 50 (test_lk_d_topk.py:42-46, 219-224)
+    from dsv4attn import ops
+    torch.manual_seed(0)
+    score = torch.randn(1, 128).to(torch.bfloat16).float()
+    want = O.indexer_topk(score, 50, 64, 128)
+    for sort_desc in (False, True):
+        got = ops.indexer_topk(score.to(cuda_dev), torch.tensor([50], dtype=torch.int32, device=cuda_dev), 64, 128,
+                               sort_desc=sort_desc).cpu()
+        assert set(got[0].tolist()) == set(want[0].tolist())
+        assert int((got[0] == -1).sum()) == 14
+        if sort_desc:
+            # descending masked score, the -1 sentinels last (reference sorted=True)
+            valid = got[0][got[0] >= 0] - 128
+            vals = score[0, valid.long()]
+            assert (vals[:-1] >= vals[1:]).all()
+            assert (got[0, :50] >= 0).all() and (got[0, 50:] == -1).all()
+
+
+def test_topk_one_hot_and_ties(cuda_dev):
+    from dsv4attn import ops
+    score = torch.zeros(2, 300)
+    score[0, 17] = 5.0
+    score[1, :] = 1.0                        # all tied: lowest indices win
+    ta = torch.tensor([300, 300], dtype=torch.int32, device=cuda_dev)
+    got = ops.indexer_topk(score.to(cuda_dev), ta, 10, 0).cpu()
+    assert 17 in got[0].tolist()
+    assert sorted(got[1].tolist()) == list(range(10))
+
+
+@pytest.mark.parametrize("B,T,k,ta", [(1, 1024, 512, 1024), (4, 1024, 512, 700), (64, 8192, 2048, 8192),
+                                      (2, 8192, 2048, 1000), (1, 65536, 2048, 65536), (2, 40000, 2048, 30000)])
+def test_topk_random_sets(cuda_dev, B, T, k, ta):
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(T + k)
+    score = torch.randn(B, T, generator=g)
+    tact = torch.full((B,), ta, dtype=torch.int32)
+    want = O.indexer_topk(score, tact, k, 128)
+    got = ops.indexer_topk(score.to(cuda_dev), tact.to(cuda_dev), k, 128).cpu()
+    assert_topk_sets(got, want, masked_scores(score, tact), 128)
+    assert int((got == -1).sum()) == int((want == -1).sum())
+
+
+def test_topk_mask_mode_exclusion_equivalent(cuda_dev):
+    from dsv4attn import ops
+    B, T, k = 3, 4096, 512
+    score = torch.randn(B, T)
+    tact = torch.tensor([4096, 300, 0], dtype=torch.int32)
+    a = ops.indexer_topk(score.to(cuda_dev), tact.to(cuda_dev), k, 128, mask_mode=0).cpu()
+    poisoned = score.clone()
+    for b in range(B):
+        poisoned[b, int(tact[b]):] = float("nan")   # never read in mask_mode 1
+    bm = ops.indexer_topk(poisoned.to(cuda_dev), tact.to(cuda_dev), k, 128, mask_mode=1).cpu()
+    for b in range(B):
+        assert set(a[b].tolist()) == set(bm[b].tolist())
+
+
+def test_topk_merge_equals_global(cuda_dev):
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(11)
+    T, G, k = 65536, 8, 2048
+    score = torch.randn(1, T, generator=g)
+    want = O.indexer_topk(score, T, k, 128)
+    cs, ci = [], []
+    for r in range(G):
+        sub = score[:, r * T // G:(r + 1) * T // G]
+        v, i = torch.topk(sub, k)
+        cs.append(v)
+        ci.append((i + r * T // G).to(torch.int32))
+    got = ops.topk_merge(torch.cat(cs, 1).to(cuda_dev), torch.cat(ci, 1).to(cuda_dev), k, 128).cpu()
+    assert_topk_sets(got, want, score, 128)
+
+
+# --------------------------------------------------------------- attention
+
+def _attn_case(B, S, N, K, frac_masked=0.1, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, S, 64, 512, generator=g).to(torch.bfloat16)
+    kv = torch.randn(B, N, 512, generator=g).to(torch.bfloat16)
+    idx = torch.randint(0, N, (B, S, K), generator=g, dtype=torch.int32)
+    idx[torch.rand(B, S, K, generator=g) < frac_masked] = -1
+    sink = torch.randn(64, generator=g)
+    return q, kv, idx, sink
+
+
+@pytest.mark.parametrize("B,S,N,K", [(1, 1, 4224, 640), (2, 1, 1000, 200), (64, 1, 2048, 2176), (1, 1, 70000, 2176),
+                                     (2, 3, 600, 130), (1, 1, 300, 17)])
+def test_sparse_attn_matches_oracle(cuda_dev, B, S, N, K):
+    from dsv4attn import ops
+    q, kv, idx, sink = _attn_case(B, S, N, K, seed=N + K)
+    scale = 512 ** -0.5
+    want = O.sparse_attn(q, kv, idx, sink, scale)
+    lse = torch.empty(B * S, 64, device=cuda_dev)
+    got = ops.sparse_attn(q.to(cuda_dev), kv.to(cuda_dev), idx.to(cuda_dev), sink.to(cuda_dev), scale, lse=lse).cpu()
+    torch.testing.assert_close(got.float(), want.float(), rtol=2e-2, atol=2e-2)
+    err = (got.float() - want.float()).abs().max()
+    assert float(err) < 2e-2
+
+
+def test_sparse_attn_all_masked_and_single_index(cuda_dev):
+    from dsv4attn import ops
+    q, kv, idx, sink = _attn_case(1, 1, 64, 128, seed=5)
+    idx[:] = -1
+    got = ops.sparse_attn(q.to(cuda_dev), kv.to(cuda_dev), idx.to(cuda_dev), sink.to(cuda_dev), 0.05).cpu()
+    assert (got == 0).all()
+    idx[0, 0, 77] = 9
+    want = O.sparse_attn(q, kv, idx, sink, 0.05)
+    got = ops.sparse_attn(q.to(cuda_dev), kv.to(cuda_dev), idx.to(cuda_dev), sink.to(cuda_dev), 0.05).cpu()
+    torch.testing.assert_close(got.float(), want.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_sparse_attn_out_of_range_index_flags_status(cuda_dev):
+    from dsv4attn import ops
+    q, kv, idx, sink = _attn_case(1, 1, 100, 64, seed=6)
+    idx[0, 0, 3] = 100        # == kv_rows: clamped and reported, never read out of bounds
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    ops.sparse_attn(q.to(cuda_dev), kv.to(cuda_dev), idx.to(cuda_dev), sink.to(cuda_dev), 0.05, status=status)
+    assert int(status.item()) != 0
+
+
+def test_sparse_attn_partial_combine_equals_full(cuda_dev):
+    """Sequence-split building block: partials over disjoint index subsets
+    merged by lse_combine (sink once) equal the unsplit attention."""
+    from dsv4attn import ops
+    q, kv, idx, sink = _attn_case(1, 1, 5000, 2176, seed=8)
+    qd, kvd, sd = q.to(cuda_dev), kv.to(cuda_dev), sink.to(cuda_dev)
+    full = ops.sparse_attn(qd, kvd, idx.to(cuda_dev), sd, 0.044)
+    parts = []
+    G = 4
+    for r in range(G):
+        sub = idx.clone()
+        keep = (sub >= r * 1250) & (sub < (r + 1) * 1250)
+        sub[~keep] = -1
+        parts.append(ops.sparse_attn_partial(qd, kvd, sub.to(cuda_dev), 0.044))
+    ml = torch.stack([p[0] for p in parts])
+    po = torch.stack([p[1] for p in parts])
+    comb = ops.lse_combine(ml, po, sd).view(1, 1, 64, 512)
+    torch.testing.assert_close(comb.float().cpu(), full.float().cpu(), rtol=2e-2, atol=2e-2)
+    want = O.sparse_attn(q, kv, idx, sink, 0.044)
+    torch.testing.assert_close(comb.float().cpu(), want.float(), rtol=2e-2, atol=2e-2)

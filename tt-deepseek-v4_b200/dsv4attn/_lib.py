@@ -1,0 +1,98 @@
+"""ctypes binding of ``libdsv4attn.so`` (the C ABI declared in include/dsv4attn.h).
+
+The library is built in-tree by ``tt-deepseek-v4_b200/build.py``.  There is no
+fallback: if the library is missing or cannot be loaded every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdsv4attn.so")
+
+DSA_OK = 0
+DSA_ERR_ARG = -1
+DSA_ERR_CUDA = -2
+DSA_ERR_UNSUPPORTED = -3
+DSA_ERR_TIMEOUT = -4
+DSA_ERR_WORKSPACE = -5
+
+P = ctypes.c_void_p
+I32 = ctypes.c_int
+I64 = ctypes.c_int64
+F32 = ctypes.c_float
+SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/dsv4attn.h
+PROTOTYPES = {
+    "dsa_version": (I32, []),
+    "dsa_last_error": (ctypes.c_char_p, []),
+    "dsa_act_quant_block": (I32, [P, P, P, P, I64, I64, I64, I64, I32, F32, F32, P]),
+    "dsa_kv_window_write": (I32, [P, P, P, P, I32, I32, I32, I64, I32, I32, P]),
+    "dsa_compressor_step": (I32, [P, P, I64, P, P, P, P, P, P, I32, P, I64, I64, I32, P, P,
+                                  I32, I32, I32, I32, I32, I32, I32, F32, P]),
+    "dsa_window_indices": (I32, [P, P, I64, I32, I32, P]),
+    "dsa_indexer_score": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, P]),
+    "dsa_indexer_topk": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
+    "dsa_indexer_topk_workspace_size": (SZ, [I32, I32, I32]),
+    "dsa_indexer_topk_ws": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, SZ, P]),
+    "dsa_advance_positions": (I32, [P, P, I32, I32, I32, P]),
+    "dsa_topk_merge": (I32, [P, P, I32, P, P, I64, I32, I32, I32, P]),
+    "dsa_sparse_attn_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
+    "dsa_sparse_attn": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
+    "dsa_sparse_attn_partial": (I32, [P, P, I64, I64, P, I64, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
+    "dsa_lse_combine": (I32, [P, P, P, P, I32, I32, I32, I32, P]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class NativeLibraryError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load (once) and return the ctypes handle; raises if the .so is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise NativeLibraryError(
+                    f"dsv4attn native library not found at {LIB_PATH}; "
+                    "build it with `python tt-deepseek-v4_b200/build.py` (nvcc, sm_100a)")
+            h = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in PROTOTYPES.items():
+                fn = getattr(h, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = h
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().dsa_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    """Map a C status to the reference's Python error conventions:
+    ValueError for shape/argument problems (inference.py:3036-3044,
+    4394-4397), RuntimeError for device failures (4949-4952)."""
+    if rc == DSA_OK:
+        return
+    msg = last_error() or f"status {rc}"
+    if rc in (DSA_ERR_ARG, DSA_ERR_WORKSPACE, DSA_ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {msg}")
+    if rc == DSA_ERR_TIMEOUT:
+        raise TimeoutError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg}")
+
+
+def exported_symbols():
+    return sorted(PROTOTYPES)

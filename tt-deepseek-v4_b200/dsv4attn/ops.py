@@ -1,0 +1,317 @@
+"""Functional torch-tensor wrappers over the C ABI.
+
+Every function takes CUDA tensors, validates dtype / device / layout, calls
+the native entry point on ``torch.cuda.current_stream()`` and returns the
+output tensor(s).  Outputs may be passed in (``out=``) so a caller can keep
+all buffers persistent (CUDA-graph capture); nothing here synchronises.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import check, lib
+
+BF16 = torch.bfloat16
+I32 = torch.int32
+F32 = torch.float32
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtype=None, cuda=True):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if cuda and not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU fallback)")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _contig(t: torch.Tensor, name: str):
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+class Workspace:
+    """Grow-only per-device scratch buffer owned by the caller (allocate it
+    before CUDA-graph capture; the native calls never allocate)."""
+
+    def __init__(self, device, nbytes: int = 0):
+        self.device = torch.device(device)
+        self.buf = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=self.device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if nbytes > self.buf.numel():
+            self.buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+    @property
+    def nbytes(self) -> int:
+        return self.buf.numel()
+
+
+_default_ws: dict = {}
+
+
+def _ws(device, nbytes: int, ws: Workspace | None) -> Workspace:
+    if ws is None:
+        key = torch.device(device)
+        ws = _default_ws.get(key)
+        if ws is None:
+            ws = _default_ws[key] = Workspace(key)
+    ws.get(nbytes)
+    return ws
+
+
+# ------------------------------------------------------------------ attn.kv
+
+def act_quant_block(x: torch.Tensor, block: int = 64, fp8_max: float = 448.0, eps: float = 1e-4,
+                    out: torch.Tensor | None = None, scales: torch.Tensor | None = None,
+                    codes: torch.Tensor | None = None):
+    """Block-wise e4m3 round trip along the last dim (inference.py:3383-3499,
+    4578-4607).  Returns ``(out, scales, codes)``; scales/codes are filled only
+    when passed in or requested with ``scales=True`` / ``codes=True``."""
+    _need(x, "x", BF16)
+    if x.stride(-1) != 1:
+        raise ValueError("x must have a unit stride in the last dim")
+    N = x.shape[-1]
+    if N % block:
+        raise ValueError(f"last dim {N} must be divisible by block_size {block}")
+    x2 = x.reshape(-1, N)
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty_like(x)
+    out2 = out.view(-1, N)
+    if scales is True:
+        scales = torch.empty(*x.shape[:-1], N // block, dtype=F32, device=x.device)
+    if codes is True:
+        codes = torch.empty(*x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    check(lib().dsa_act_quant_block(x2.data_ptr(), out2.data_ptr(), _ptr(scales), _ptr(codes), M, N,
+                                    x2.stride(0), out2.stride(0), block, fp8_max, eps, _stream(x)),
+          "act_quant_block")
+    return out, scales, codes
+
+
+def kv_window_write(kv: torch.Tensor, kv_cache: torch.Tensor, pos: torch.Tensor, win: int,
+                    rope_dim: int = 64, scales: torch.Tensor | None = None) -> None:
+    """act_quant on the nope dims of ``kv [B, D]`` and ring write into
+    ``kv_cache[b, pos[b] % win]`` (inference.py:5997-6006, 6072-6079)."""
+    _need(kv, "kv", BF16)
+    _need(kv_cache, "kv_cache", BF16)
+    _need(pos, "pos", I32)
+    _contig(kv, "kv")
+    B, D = kv.shape
+    if kv_cache.dim() != 3 or kv_cache.shape[0] < B or kv_cache.shape[2] != D or kv_cache.stride(1) != D:
+        raise ValueError("kv_cache must be [B, rows, D] with contiguous rows")
+    check(lib().dsa_kv_window_write(kv.data_ptr(), kv_cache.data_ptr(), _ptr(scales), pos.data_ptr(), B, D,
+                                    rope_dim, kv_cache.stride(0), win, 64, _stream(kv)), "kv_window_write")
+
+
+# ------------------------------------------------------------ attn.compress
+
+def compressor_step(kv_row, score_row, ape, kv_state, score_state, gamma, cos, sin, kv_cache, slot_offset: int,
+                    pos, ratio: int, overlap: bool, rotate: bool = False, eps: float = 1e-6,
+                    rope_dim: int = 64, emitted=None, write_state: bool = True) -> None:
+    """One compressor decode step (state write + on-device emit decision,
+    inference.py:4938-5097).  kv_row/score_row [B, coff*d] bf16; state fp32
+    [B, coff*r, coff*d]; gamma [d] fp32; cos/sin [n_pos, rope/2] fp32;
+    kv_cache [B, rows, d] bf16."""
+    for t, n in ((kv_state, "kv_state"), (score_state, "score_state"), (gamma, "gamma"), (cos, "cos"),
+                 (sin, "sin")):
+        _need(t, n, F32)
+        _contig(t, n)
+    _need(kv_cache, "kv_cache", BF16)
+    _need(pos, "pos", I32)
+    B = kv_state.shape[0]
+    d = gamma.shape[0]
+    coff = 2 if overlap else 1
+    if tuple(kv_state.shape) != (B, coff * ratio, coff * d) or kv_state.shape != score_state.shape:
+        raise ValueError(f"state must be [B, {coff * ratio}, {coff * d}], got {tuple(kv_state.shape)}")
+    if kv_cache.dim() != 3 or kv_cache.shape[2] != d or kv_cache.stride(1) != d:
+        raise ValueError("kv_cache must be [B, rows, d] with contiguous rows")
+    ld_row = 0
+    if write_state:
+        _need(kv_row, "kv_row", BF16)
+        _need(score_row, "score_row", BF16)
+        _need(ape, "ape", F32)
+        _contig(ape, "ape")
+        if kv_row.shape[-1] != coff * d or kv_row.stride(-1) != 1 or score_row.stride() != kv_row.stride():
+            raise ValueError("kv_row/score_row must be [B, coff*d] with matching strides")
+        ld_row = kv_row.stride(0)
+    check(lib().dsa_compressor_step(_ptr(kv_row) if write_state else None, _ptr(score_row) if write_state else None,
+                                    ld_row, _ptr(ape) if write_state else None, kv_state.data_ptr(),
+                                    score_state.data_ptr(), gamma.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                    cos.shape[0], kv_cache.data_ptr(), kv_cache.stride(0), kv_cache.shape[1],
+                                    slot_offset, pos.data_ptr(), _ptr(emitted), B, d, rope_dim, ratio,
+                                    int(overlap), int(rotate), int(write_state), eps, _stream(kv_state)),
+          "compressor_step")
+
+
+# ---------------------------------------------------------------- attn.topk
+
+def window_indices(pos: torch.Tensor, win: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Window ring indices per sequence (inference.py:479-506, 6020-6026)."""
+    _need(pos, "pos", I32)
+    B = pos.shape[0]
+    if out is None:
+        out = torch.empty(B, win, dtype=I32, device=pos.device)
+    check(lib().dsa_window_indices(pos.data_ptr(), out.data_ptr(), out.stride(0), B, win, _stream(pos)),
+          "window_indices")
+    return out
+
+
+def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: int,
+                  out: torch.Tensor | None = None, t_valid: torch.Tensor | None = None) -> torch.Tensor:
+    """``s[b,t] = sum_h w[b,h] relu(q[b,h].k[b,t])`` for t < T
+    (inference.py:5260-5275).  q [B,64,128] bf16, k_cache [B, >=T, 128] bf16,
+    w [B,64] fp32 -> [B, T] fp32."""
+    _need(q, "q", BF16)
+    _need(k_cache, "k_cache", BF16)
+    _need(w, "w", F32)
+    _contig(q, "q")
+    _contig(w, "w")
+    B, H, Di = q.shape
+    if k_cache.shape[0] < B or k_cache.shape[1] < T or k_cache.shape[2] != Di or k_cache.stride(1) != Di:
+        raise ValueError("k_cache must be [B, >=T, Di] with contiguous rows")
+    if out is None:
+        out = torch.empty(B, T, dtype=F32, device=q.device)
+    check(lib().dsa_indexer_score(q.data_ptr(), k_cache.data_ptr(), w.data_ptr(), out.data_ptr(), _ptr(t_valid),
+                                  B, H, Di, T, k_cache.stride(0), out.stride(0), _stream(q)), "indexer_score")
+    return out
+
+
+def indexer_topk(score: torch.Tensor, t_active: torch.Tensor, k: int, win: int, T: int | None = None,
+                 sort_desc: bool = False, mask_mode: int = 0, out: torch.Tensor | None = None,
+                 out_score: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
+    """Masked top-k (inference.py:5823-5851) -> int32 [B, k] (idx + win, -1
+    for invalid)."""
+    _need(score, "score", F32)
+    _need(t_active, "t_active", I32)
+    B = score.shape[0]
+    T = score.shape[1] if T is None else T
+    if out is None:
+        out = torch.empty(B, k, dtype=I32, device=score.device)
+    L = lib()
+    need = L.dsa_indexer_topk_workspace_size(B, T, k)
+    if need:
+        w = _ws(score.device, need, ws)
+        rc = L.dsa_indexer_topk_ws(score.data_ptr(), score.stride(0), t_active.data_ptr(), out.data_ptr(),
+                                   _ptr(out_score), out.stride(0), B, T, k, win, int(sort_desc), mask_mode,
+                                   w.buf.data_ptr(), w.nbytes, _stream(score))
+    else:
+        rc = L.dsa_indexer_topk(score.data_ptr(), score.stride(0), t_active.data_ptr(), out.data_ptr(),
+                                _ptr(out_score), out.stride(0), B, T, k, win, int(sort_desc), mask_mode,
+                                _stream(score))
+    check(rc, "indexer_topk")
+    return out
+
+
+def topk_merge(cand_score: torch.Tensor, cand_idx: torch.Tensor, k: int, win: int,
+               out: torch.Tensor | None = None, out_score: torch.Tensor | None = None) -> torch.Tensor:
+    """Global top-k from concatenated per-shard candidate lists."""
+    _need(cand_score, "cand_score", F32)
+    _need(cand_idx, "cand_idx", I32)
+    _contig(cand_score, "cand_score")
+    _contig(cand_idx, "cand_idx")
+    B, n = cand_score.shape
+    if out is None:
+        out = torch.empty(B, k, dtype=I32, device=cand_score.device)
+    check(lib().dsa_topk_merge(cand_score.data_ptr(), cand_idx.data_ptr(), n, out.data_ptr(), _ptr(out_score),
+                               out.stride(0), B, k, win, _stream(cand_score)), "topk_merge")
+    return out
+
+
+def advance_positions(pos: torch.Tensor, t_active: torch.Tensor | None, ratio: int, step: int = 1) -> None:
+    _need(pos, "pos", I32)
+    check(lib().dsa_advance_positions(pos.data_ptr(), _ptr(t_active), pos.shape[0], ratio, step, _stream(pos)),
+          "advance_positions")
+
+
+# -------------------------------------------------------------- attn.sparse
+
+def _attn_shapes(q, kv, idx):
+    _need(q, "q", BF16)
+    _need(kv, "kv", BF16)
+    _need(idx, "idx", I32)
+    _contig(q, "q")
+    H, D = q.shape[-2], q.shape[-1]
+    if q.dim() == 4:
+        B, S = q.shape[0], q.shape[1]
+    elif q.dim() == 3:
+        B, S = q.shape[0], 1
+    else:
+        raise ValueError("q must be [B, S, H, D] or [B, H, D]")
+    if kv.dim() == 2:
+        kv = kv.unsqueeze(0)
+    if kv.shape[0] not in (1, B) or kv.shape[2] != D or kv.stride(1) != D:
+        raise ValueError("kv must be [N, D] or [B, N, D] with contiguous rows")
+    kv_bstride = 0 if kv.shape[0] == 1 else kv.stride(0)
+    if kv_bstride == 0:
+        kv_bstride = kv.shape[1] * D  # checked >= rows * D; batch 0 for all rows
+    K = idx.shape[-1]
+    idx2 = idx.reshape(B * S, K)
+    if idx2.stride(-1) != 1:
+        raise ValueError("idx must have a unit stride in the last dim")
+    return B, S, H, D, K, kv, kv_bstride, idx2
+
+
+def sparse_attn(q, kv, idx, sink, scale: float, out=None, lse=None, ws: Workspace | None = None,
+                status=None) -> torch.Tensor:
+    """Sink-softmax sparse attention (inference.py:4459-4501).  q [B,S,H,D] or
+    [B,H,D] bf16; kv [B,N,D] or [N,D] bf16; idx [B,S,K] / [B,K] int32 with -1
+    = masked; sink [H] fp32."""
+    B, S, H, D, K, kv3, kv_bstride, idx2 = _attn_shapes(q, kv, idx)
+    if kv3.shape[0] == 1 and B > 1:
+        raise ValueError("a shared [N, D] kv needs B == 1; pass [B, N, D]")
+    _need(sink, "sink", F32)
+    if out is None:
+        out = torch.empty_like(q)
+    L = lib()
+    need = L.dsa_sparse_attn_workspace_size(B, S, H, D, K)
+    w = _ws(q.device, need, ws) if need else None
+    check(L.dsa_sparse_attn(q.data_ptr(), kv3.data_ptr(), kv_bstride, kv3.shape[1], idx2.data_ptr(),
+                            idx2.stride(0), sink.data_ptr(), out.data_ptr(), _ptr(lse), B, S, H, D, K, scale,
+                            w.buf.data_ptr() if w else None, w.nbytes if w else 0, _ptr(status), _stream(q)),
+          "sparse_attn")
+    return out
+
+
+def sparse_attn_partial(q, kv, idx, scale: float, part_ml=None, part_o=None, ws: Workspace | None = None,
+                        status=None):
+    """Un-normalised partial (m, l, o) over the rows of ``idx`` (no sink)."""
+    B, S, H, D, K, kv3, kv_bstride, idx2 = _attn_shapes(q, kv, idx)
+    M = B * S
+    if part_ml is None:
+        part_ml = torch.empty(M, H, 2, dtype=F32, device=q.device)
+    if part_o is None:
+        part_o = torch.empty(M, H, D, dtype=F32, device=q.device)
+    L = lib()
+    need = L.dsa_sparse_attn_workspace_size(B, S, H, D, K)
+    w = _ws(q.device, need, ws) if need else None
+    check(L.dsa_sparse_attn_partial(q.data_ptr(), kv3.data_ptr(), kv_bstride, kv3.shape[1], idx2.data_ptr(),
+                                    idx2.stride(0), part_ml.data_ptr(), part_o.data_ptr(), B, S, H, D, K, scale,
+                                    w.buf.data_ptr() if w else None, w.nbytes if w else 0, _ptr(status),
+                                    _stream(q)), "sparse_attn_partial")
+    return part_ml, part_o
+
+
+def lse_combine(part_ml, part_o, sink, out=None) -> torch.Tensor:
+    """Merge P partials [P, M, H, 2] / [P, M, H, D] with the sink once -> bf16 [M, H, D]."""
+    _need(part_ml, "part_ml", F32)
+    _need(part_o, "part_o", F32)
+    _need(sink, "sink", F32)
+    _contig(part_ml, "part_ml")
+    _contig(part_o, "part_o")
+    Pn, M, H, D = part_o.shape
+    if out is None:
+        out = torch.empty(M, H, D, dtype=BF16, device=part_o.device)
+    check(lib().dsa_lse_combine(part_ml.data_ptr(), part_o.data_ptr(), sink.data_ptr(), out.data_ptr(), Pn, M, H, D,
+                                _stream(part_o)), "lse_combine")
+    return out
