@@ -273,6 +273,10 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def log(msg: str) -> None:
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -292,16 +296,20 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
+    log("building layers")
     pa, path, inputs, outs = build_path(args, dev, seed=1234 + rank)
     path.set_positions(args.ctx - 1)
     torch.cuda.synchronize()
-
+    log("capturing the step graph")
     graph = path.capture(inputs, outs, warmup=1)
     path.set_positions(args.ctx - 1)
     torch.cuda.synchronize()
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
+    if int(path.status.item()) != 0:
+        raise RuntimeError(f"device status {int(path.status.item())} after warm-up (1 = bad index, 2 = wait timeout)")
+    log("warm-up done; timing")
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
@@ -337,6 +345,7 @@ def main():
     hbm, hbm_kind = peaks()
 
     # per-kernel CUDA-event timings -> dominant kernel roofline
+    log(f"timed: {ms_step:.3f} ms/step; per-kernel timings")
     kt = time_kernels(path, inputs, outs)
     dom = max(kt, key=kt.get)
     achieved = ab[dom] / (kt[dom] * 1e-3) / 1e9
@@ -350,6 +359,7 @@ def main():
 
     e2e = None
     if not args.no_e2e:
+        log("end-to-end (host buffers)")
         e2e = measure_e2e(args, path, inputs, outs, dev, world)
 
     line = None
@@ -370,6 +380,7 @@ def main():
         if e2e is not None:
             line["e2e"] = e2e
     if rank == 0 and not args.no_cpu:
+        log("CPU baseline sample")
         line["cpu_baseline"] = cpu_baseline_sample(args)
     if world > 1:
         dist.barrier()

@@ -53,6 +53,9 @@ def _check_step(path, L, st, x, xd, pos, out):
         ws = set(int(v) for v in want_idx[b] if v >= 0)
         assert gs == ws, f"pos {pos} row {b}: index sets differ {sorted(gs ^ ws)}"
     torch.testing.assert_close(out.cpu().float(), want_o[:, 0].float(), rtol=2e-2, atol=2e-2)
+    o, w = out.cpu().float(), want_o[:, 0].float()
+    assert float((o - w).norm() / w.norm()) < 1e-2
+    assert int(path.status.item()) == 0
     torch.testing.assert_close(L.kv_cache.cpu().float(), st.kv_cache.float(), rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(L.idx_cache.cpu().float(), st.idx_kv_cache.float(), rtol=2e-2, atol=2e-2)
 

@@ -162,7 +162,7 @@ extern "C" int dsa_compressor_step(const void* kv_row, const void* score_row, in
                 kCmpMaxD);
   DSA_CHECK_ARG(rope_dim >= 0 && rope_dim <= d && rope_dim % 2 == 0, "compressor_step: bad rope_dim %d", rope_dim);
   DSA_CHECK_ARG(ratio > 0, "compressor_step: ratio must be positive");
-  DSA_CHECK_ARG(ld_row >= (overlap ? 2 : 1) * d, "compressor_step: ld_row too small");
+  DSA_CHECK_ARG(!write_state || ld_row >= (overlap ? 2 : 1) * d, "compressor_step: ld_row too small");
   DSA_CHECK_ARG(cache_rows > 0 && cache_bstride >= cache_rows * d, "compressor_step: bad cache shape");
   DSA_CHECK_ARG(n_pos > 0, "compressor_step: empty rotary table");
   DSA_CHECK_ARG(!rotate || (d & (d - 1)) == 0, "compressor_step: Hadamard needs power-of-two d (got %d)", d);

@@ -16,6 +16,8 @@
 // merged by lse_combine_kernel (sink counted once).  The kernel reads each
 // gathered row exactly once from HBM; its roofline is the gather stream.
 #include "common.cuh"
+#include "sparse_attn_tc.cuh"
+#include <stdlib.h>
 
 namespace dsa {
 
@@ -321,8 +323,20 @@ struct SplitPlan {
   int tiles_per_split;
 };
 
+static bool use_mma_v0() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV4_SPARSE_ATTN_MMA");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+static int split_tile() { return use_mma_v0() ? kSaTile : satc::TK; }
+
 static SplitPlan plan_splits(int M, int K) {
-  const int ntiles = std::max(1, (K + kSaTile - 1) / kSaTile);
+  const int tile = split_tile();
+  const int ntiles = std::max(1, (K + tile - 1) / tile);
   int want = std::max(1, num_sms() / std::max(1, M));
   want = std::min(want, ntiles);
   const int tps = (ntiles + want - 1) / want;
@@ -339,6 +353,7 @@ static void ensure_attr() {
   cudaGetDevice(&dev);
   if (done_dev != dev) {
     cudaFuncSetAttribute(sparse_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSaSmem);
+    cudaFuncSetAttribute(satc::sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, satc::kSmemBytes);
     done_dev = dev;
   }
 }
@@ -411,7 +426,30 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
     a.part_ml = part_ml_out;
     a.part_o = part_o_out;
   }
-  sparse_attn_mma_kernel<<<dim3(p.nsplit, M), kSaThreads, kSaSmem, st>>>(a);
+  if (use_mma_v0()) {
+    sparse_attn_mma_kernel<<<dim3(p.nsplit, M), kSaThreads, kSaSmem, st>>>(a);
+  } else {
+    satc::Args t{};
+    t.q = a.q;
+    t.kv = a.kv;
+    t.kv_bstride = a.kv_bstride;
+    t.kv_rows = a.kv_rows;
+    t.idx = a.idx;
+    t.ld_idx = a.ld_idx;
+    t.sink = a.sink;
+    t.out = a.out;
+    t.lse = a.lse;
+    t.part_ml = a.part_ml;
+    t.part_o = a.part_o;
+    t.status = a.status;
+    t.S = a.S;
+    t.M = a.M;
+    t.K = a.K;
+    t.tiles_per_split = a.tiles_per_split;
+    t.scale_log2 = a.scale_log2;
+    t.final_mode = a.final_mode;
+    satc::sparse_attn_tc_kernel<<<dim3(p.nsplit, M), satc::THREADS, satc::kSmemBytes, st>>>(t);
+  }
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {
     lse_combine_kernel<<<dim3(M, kSaH), 128, 0, st>>>(ws_ml, ws_o, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
