@@ -210,6 +210,16 @@ int dsa_sparse_attn_partial(const void* q, const void* kv, int64_t kv_bstride,
 int dsa_lse_combine(const float* part_ml, const float* part_o, const float* sink,
                     void* out, int P, int M, int H, int D, dsa_stream_t stream);
 
+/* --------------------------------------------------------------- tracing */
+
+/* Phase tracing (the device-side counterpart of the reference's _phase
+ * wall-clock timers, inference.py:174-266): while a device buffer of at
+ * least 8 * 256 int64 is set, sparse-attention launches record clock64()
+ * stamps of their first CTA per 32-row tile: slot 0 producer issued, 1 tile
+ * landed, 2 MMA warp got the tile, 3 S issued, 4 PV issued, 5 softmax got S,
+ * 6 P written; slot 7 holds kernel start / end.  NULL turns it off. */
+int dsa_set_trace(void* dev_buffer, size_t bytes);
+
 #ifdef __cplusplus
 }
 #endif

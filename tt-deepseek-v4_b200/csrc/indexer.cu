@@ -13,6 +13,8 @@
 // conflict-free); q (16 KB) stays resident in shared memory.  The kernel is
 // HBM-bound on the key stream: 256 B per key in, 4 B per key out.
 #include "common.cuh"
+#include "indexer_tc.cuh"
+#include <stdlib.h>
 
 namespace dsa {
 
@@ -142,22 +144,57 @@ extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, f
   DSA_CHECK_ARG(ld_score >= T, "indexer_score: ld_score < T");
   DSA_CHECK_ARG(aligned(q, 16) && aligned(k, 16), "indexer_score: q/k must be 16-byte aligned");
   if (B == 0 || T == 0) return DSA_OK;
-  const int smem = kIdxH * kIdxRowBytes + kIdxStages * kIdxTile * kIdxRowBytes;
+  static int use_mma = -1;
+  if (use_mma < 0) {
+    const char* e = getenv("DSV4_INDEXER_MMA");
+    use_mma = (e && e[0] == '1') ? 1 : 0;
+  }
   static int attr_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
+  const int smem = kIdxH * kIdxRowBytes + kIdxStages * kIdxTile * kIdxRowBytes;
   if (attr_dev != dev) {
     cudaFuncSetAttribute(indexer_score_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(idxtc::indexer_score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         idxtc::kSmemBytes);
     attr_dev = dev;
   }
-  // enough CTAs to cover the SMs ~2x; each CTA streams a contiguous key range
   const int nsm = num_sms();
-  int per = (int)((int64_t(T) * B + 2LL * nsm - 1) / (2LL * nsm));
-  per = std::max(kIdxTile * 2, ((per + kIdxTile - 1) / kIdxTile) * kIdxTile);
-  dim3 grid((T + per - 1) / per, B);
-  indexer_score_mma_kernel<<<grid, kIdxThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), w, score, t_valid, T, k_bstride,
-      ld_score, per);
+  if (use_mma) {
+    // enough CTAs to cover the SMs ~2x; each CTA streams a contiguous key range
+    int per = (int)((int64_t(T) * B + 2LL * nsm - 1) / (2LL * nsm));
+    per = std::max(kIdxTile * 2, ((per + kIdxTile - 1) / kIdxTile) * kIdxTile);
+    dim3 grid((T + per - 1) / per, B);
+    indexer_score_mma_kernel<<<grid, kIdxThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), w, score, t_valid, T, k_bstride,
+        ld_score, per);
+  } else {
+    DSA_CHECK_ARG(k_bstride % kIdxD == 0, "indexer_score: k batch stride must be a multiple of Di");
+    const int64_t row_stride = k_bstride / kIdxD;
+    const uint64_t k_rows = uint64_t(B - 1) * row_stride + uint64_t(T);
+    DSA_CHECK_ARG(k_rows < (1ull << 31), "indexer_score: key cache has more than 2^31 rows");
+    CUtensorMap tm_k, tm_q;
+    if (!tma::make_2d_bf16(&tm_k, k, kIdxD, k_rows, kIdxD * 2, 64, idxtc::TILE) ||
+        !tma::make_2d_bf16(&tm_q, q, kIdxD, uint64_t(B) * kIdxH, kIdxD * 2, 64, kIdxH)) {
+      set_error("indexer_score: cuTensorMapEncodeTiled failed");
+      return DSA_ERR_CUDA;
+    }
+    idxtc::Args a{};
+    a.w = w;
+    a.score = score;
+    a.t_valid = t_valid;
+    a.status = nullptr;
+    a.B = B;
+    a.T = T;
+    a.tiles_per_seq = (T + idxtc::TILE - 1) / idxtc::TILE;
+    const int total = B * a.tiles_per_seq;
+    a.items_per_cta = (total + nsm - 1) / nsm;
+    a.ld_score = ld_score;
+    a.k_row_stride = row_stride;
+    const int grid = (total + a.items_per_cta - 1) / a.items_per_cta;
+    idxtc::indexer_score_tc_kernel<<<grid, idxtc::THREADS, idxtc::kSmemBytes,
+                                     reinterpret_cast<cudaStream_t>(stream)>>>(a, tm_k, tm_q);
+  }
   DSA_CHECK_LAUNCH("indexer_score");
   return DSA_OK;
 }

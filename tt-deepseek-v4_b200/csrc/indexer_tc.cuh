@@ -1,0 +1,189 @@
+// attn.topk indexer score on the tcgen05 tensor cores.
+//
+// s[b, t] = sum_h w[b, h] * relu(q[b, h, :] . k[b, t, :])   (H = 64, Di = 128)
+//
+// Persistent kernel: one CTA per SM walks a contiguous range of
+// (sequence, 128-key tile) work items.  Roles:
+//   warp 0      TMA producer: per item a [128 keys x 128] tile of the key
+//               cache and the sequence's [64 x 128] q (two 128-B-swizzled
+//               k-blocks each) into a 4-stage ring (48 KB per stage).
+//   warp 1      MMA issuer: S^T = K_tile . Q^T, M = 128 keys, N = 64 heads,
+//               K = 128 (8 x K16), into one of two TMEM accumulators.
+//   warps 2-5   epilogue: thread = key row (TMEM lane), 64 head scores in
+//               registers -> sum_h w_h relu(s_h) -> one fp32 score, coalesced.
+// The [H, T] score matrix never exists; HBM traffic is the key stream
+// (256 B per key) plus 4 B of score per key.
+#pragma once
+
+#include "common.cuh"
+#include "tc05.cuh"
+#include "tma.cuh"
+
+namespace dsa {
+namespace idxtc {
+
+constexpr int H = 64;
+constexpr int DI = 128;
+constexpr int TILE = 128;         // keys per work item
+constexpr int NS = 4;
+constexpr int THREADS = 192;
+constexpr int kKeyBytes = TILE * DI * 2;   // 32 KB: 2 k-blocks of [128 rows x 128 B]
+constexpr int kQBytes = H * DI * 2;        // 16 KB: 2 k-blocks of [64 rows x 128 B]
+constexpr int kStageBytes = kKeyBytes + kQBytes;
+constexpr int kOffAux = NS * kStageBytes;
+constexpr int kSmemBytes = kOffAux + 256 + 1024;
+constexpr uint32_t kTmemCols = 128;        // 2 accumulators x 64 columns
+constexpr uint32_t kIdesc = tc::idesc_bf16(128, 64, false, false);
+
+struct Aux {
+  uint64_t full[NS];
+  uint64_t empty[NS];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+struct Args {
+  const float* w;
+  float* score;
+  const int32_t* t_valid;
+  int32_t* status;
+  int B, T, tiles_per_seq, items_per_cta;
+  int64_t ld_score;
+  int64_t k_row_stride;   // rows between consecutive sequences in the key map
+};
+
+__device__ __forceinline__ bool item_live(const Args& a, int item, int& b, int& t0, int& t_lim) {
+  b = item / a.tiles_per_seq;
+  t0 = (item - b * a.tiles_per_seq) * TILE;
+  t_lim = a.T;
+  if (a.t_valid) t_lim = min(a.T, max(0, a.t_valid[b]));
+  return t0 < t_lim;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args a,
+                                                                      const __grid_constant__ CUtensorMap tm_k,
+                                                                      const __grid_constant__ CUtensorMap tm_q) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Aux* aux = reinterpret_cast<Aux*>(smem + kOffAux);
+  const uint32_t sbase = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int total = a.B * a.tiles_per_seq;
+  const int i_begin = blockIdx.x * a.items_per_cta;
+  const int i_end = min(total, i_begin + a.items_per_cta);
+
+  if (warp == 1) {
+    tc::tmem_alloc(smem_u32(&aux->tmem_base), kTmemCols);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      tc::mbar_init(smem_u32(&aux->full[s]), 1);
+      tc::mbar_init(smem_u32(&aux->empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(smem_u32(&aux->acc_full[s]), 1);
+      tc::mbar_init(smem_u32(&aux->acc_empty[s]), 4);
+    }
+    tc::mbar_fence_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = aux->tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      tma::prefetch_map(&tm_k);
+      tma::prefetch_map(&tm_q);
+      int it = 0;
+      for (int item = i_begin; item < i_end; ++item) {
+        int b, t0, t_lim;
+        if (!item_live(a, item, b, t0, t_lim)) continue;
+        const int s = it % NS;
+        if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2);
+        const uint32_t st = sbase + s * kStageBytes;
+        const uint32_t fb = smem_u32(&aux->full[s]);
+        tma::mbar_arrive_expect_tx(fb, kStageBytes);
+        const int krow = int(int64_t(b) * a.k_row_stride + t0);
+        tma::load_2d(st, &tm_k, 0, krow, fb);
+        tma::load_2d(st + kKeyBytes / 2, &tm_k, 64, krow, fb);
+        tma::load_2d(st + kKeyBytes, &tm_q, 0, b * H, fb);
+        tma::load_2d(st + kKeyBytes + kQBytes / 2, &tm_q, 64, b * H, fb);
+        ++it;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int it = 0;
+      for (int item = i_begin; item < i_end; ++item) {
+        int b, t0, t_lim;
+        if (!item_live(a, item, b, t0, t_lim)) continue;
+        const int s = it % NS, acc = it & 1;
+        tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2);
+        if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2);
+        tc::fence_after_sync();
+        const uint32_t st = sbase + s * kStageBytes;
+#pragma unroll
+        for (int ks = 0; ks < DI / 16; ++ks) {
+          const uint64_t ad = tc::smem_desc(st + (ks >> 2) * (kKeyBytes / 2) + (ks & 3) * 32, 16, 1024,
+                                            tc::kLayoutSw128);
+          const uint64_t bd = tc::smem_desc(st + kKeyBytes + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32, 16, 1024,
+                                            tc::kLayoutSw128);
+          tc::mma_bf16(tmem + 64 * acc, ad, bd, kIdesc, ks > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(smem_u32(&aux->acc_full[acc]));
+        tc::mma_commit(smem_u32(&aux->empty[s]));
+        ++it;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2-5)
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    int it = 0;
+    int cur_b = -1;
+    float wv[H];
+    for (int item = i_begin; item < i_end; ++item) {
+      int b, t0, t_lim;
+      if (!item_live(a, item, b, t0, t_lim)) continue;
+      const int acc = it & 1;
+      if (b != cur_b) {
+#pragma unroll
+        for (int h = 0; h < H; ++h) wv[h] = __ldg(a.w + int64_t(b) * H + h);
+        cur_b = b;
+      }
+      tc::mbar_wait(smem_u32(&aux->acc_full[acc]), (it >> 1) & 1, a.status, 2);
+      tc::fence_after_sync();
+      float v0[32], v1[32];
+      tc::tmem_ld32(trow + 64 * acc, v0);
+      tc::tmem_ld32(trow + 64 * acc + 32, v1);
+      tc::tmem_wait_ld();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(smem_u32(&aux->acc_empty[acc]));
+      float s = 0.f;
+#pragma unroll
+      for (int h = 0; h < 32; ++h) s = fmaf(wv[h], fmaxf(v0[h], 0.f), s);
+#pragma unroll
+      for (int h = 0; h < 32; ++h) s = fmaf(wv[32 + h], fmaxf(v1[h], 0.f), s);
+      const int t = t0 + quarter * 32 + lane;
+      if (t < t_lim) a.score[int64_t(b) * a.ld_score + t] = s;
+      ++it;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace idxtc
+}  // namespace dsa

@@ -323,6 +323,8 @@ struct SplitPlan {
   int tiles_per_split;
 };
 
+static long long* g_trace = nullptr;
+
 static bool use_mma_v0() {
   static int v = -1;
   if (v < 0) {
@@ -332,14 +334,18 @@ static bool use_mma_v0() {
   return v == 1;
 }
 
-static int split_tile() { return use_mma_v0() ? kSaTile : satc::TK; }
+using TcSmall = satc::Cfg<64, 2>;  // 64-key tiles, 2-stage ring (tcgen05 issue cost favours N=64)
+
+static int split_tile() { return use_mma_v0() ? kSaTile : TcSmall::TK; }
+static int idx_cap() { return TcSmall::kIdxCap; }
 
 static SplitPlan plan_splits(int M, int K) {
   const int tile = split_tile();
   const int ntiles = std::max(1, (K + tile - 1) / tile);
   int want = std::max(1, num_sms() / std::max(1, M));
   want = std::min(want, ntiles);
-  const int tps = (ntiles + want - 1) / want;
+  int tps = (ntiles + want - 1) / want;
+  if (!use_mma_v0()) tps = std::min(tps, idx_cap() / tile);  // the tc kernel stages <= kIdxCap indices
   return {(ntiles + tps - 1) / tps, tps};
 }
 
@@ -353,7 +359,9 @@ static void ensure_attr() {
   cudaGetDevice(&dev);
   if (done_dev != dev) {
     cudaFuncSetAttribute(sparse_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSaSmem);
-    cudaFuncSetAttribute(satc::sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, satc::kSmemBytes);
+    cudaFuncSetAttribute(satc::sparse_attn_tc_kernel<TcSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         TcSmall::kSmemBytes);
+
     done_dev = dev;
   }
 }
@@ -448,7 +456,19 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
     t.tiles_per_split = a.tiles_per_split;
     t.scale_log2 = a.scale_log2;
     t.final_mode = a.final_mode;
-    satc::sparse_attn_tc_kernel<<<dim3(p.nsplit, M), satc::THREADS, satc::kSmemBytes, st>>>(t);
+    t.trace = g_trace;
+    CUtensorMap tm_kv, tm_q;
+    DSA_CHECK_ARG(kv_bstride % kSaD == 0, "sparse_attn: kv batch stride must be a multiple of D");
+    const int64_t row_stride = kv_bstride / kSaD;
+    const uint64_t kv_total_rows = uint64_t(B - 1) * row_stride + uint64_t(kv_rows);
+    DSA_CHECK_ARG(kv_total_rows < (1ull << 31), "sparse_attn: kv cache has more than 2^31 rows");
+    if (!tma::make_2d_bf16(&tm_kv, kv, kSaD, kv_total_rows, kSaD * 2, 64, 1) ||
+        !tma::make_2d_bf16(&tm_q, q, kSaD, uint64_t(M) * kSaH, kSaD * 2, 64, 64)) {
+      set_error("sparse_attn: cuTensorMapEncodeTiled failed");
+      return DSA_ERR_CUDA;
+    }
+    satc::sparse_attn_tc_kernel<TcSmall><<<dim3(p.nsplit, M), satc::THREADS, TcSmall::kSmemBytes, st>>>(
+        t, tm_kv, tm_q, row_stride);
   }
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {
@@ -491,5 +511,13 @@ extern "C" int dsa_lse_combine(const float* part_ml, const float* part_o, const 
   lse_combine_kernel<<<dim3(M, H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr, nullptr);
   DSA_CHECK_LAUNCH("lse_combine");
+  return DSA_OK;
+}
+
+extern "C" int dsa_set_trace(void* dev_buffer, size_t bytes) {
+  clear_error();
+  const size_t need = size_t(satc::kTrMisc + 1) * satc::kTrTiles * sizeof(long long);
+  DSA_CHECK_ARG(dev_buffer == nullptr || bytes >= need, "set_trace: buffer needs %zu bytes", need);
+  g_trace = static_cast<long long*>(dev_buffer);
   return DSA_OK;
 }

@@ -1,0 +1,61 @@
+// TMA (cp.async.bulk.tensor) helpers for sm_100a: tensor-map encoding on the
+// host and 2-D tile / 4-row gather loads that complete on an mbarrier.
+// Only non-multicast forms are used: every source is this GPU's own memory.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsa {
+namespace tma {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn();  // resolved once through cudaGetDriverEntryPoint
+
+// 2-D bf16 map over [rows, cols] (cols contiguous, rows at row_stride_bytes),
+// box [box_rows, box_cols], 128-B swizzle.  Returns false on failure.
+bool make_2d_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_bytes,
+                  uint32_t box_cols, uint32_t box_rows);
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// box load of the tile whose top-left element is (col x, row y)
+__device__ __forceinline__ void load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// four rows r0..r3, columns [x, x + box_cols): 4 x box_cols elements into dst
+__device__ __forceinline__ void gather4(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t r0, int32_t r1,
+                                        int32_t r2, int32_t r3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
+}
+
+// L2 prefetch of four rows (no shared-memory destination, no completion)
+__device__ __forceinline__ void prefetch_gather4(const CUtensorMap* map, int32_t x, int32_t r0, int32_t r1, int32_t r2,
+                                                 int32_t r3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile::gather4 [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace tma
+}  // namespace dsa

@@ -45,6 +45,7 @@ PROTOTYPES = {
     "dsa_sparse_attn": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
     "dsa_sparse_attn_partial": (I32, [P, P, I64, I64, P, I64, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
     "dsa_lse_combine": (I32, [P, P, P, P, I32, I32, I32, I32, P]),
+    "dsa_set_trace": (I32, [P, SZ]),
 }
 
 _lock = threading.Lock()
