@@ -190,6 +190,24 @@ int dsa_sparse_attn(const void* q, const void* kv, int64_t kv_bstride, int64_t k
                     void* workspace, size_t workspace_bytes, int32_t* status,
                     dsa_stream_t stream);
 
+/* Allocation-free variant of dsa_sparse_attn, for callers that cannot
+ * allocate device memory where they call the attention (a runtime that owns
+ * a fixed device arena, a plugin running inside another framework's memory
+ * manager).  Same arguments and result as dsa_sparse_attn, without the
+ * workspace: the split-K partials go to an 8 MiB scratch array that the
+ * library reserves in device memory on every GPU that loads it and keeps
+ * until the process exits.  Shapes whose partials need more than 8 MiB
+ * (dsa_sparse_attn_workspace_size() > 8 MiB) are rejected with
+ * DSA_ERR_WORKSPACE.  The first call on a device looks up the array's
+ * device address; make that first call before any stream capture.  All
+ * calls share the one array, so calls that overlap on the GPU (other
+ * streams, other host threads) race on it.  This entry point has no
+ * counterpart in the reference. */
+int dsa_sparse_attn_noalloc(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,
+                            const int32_t* idx, int64_t ld_idx, const float* sink, void* out,
+                            float* lse, int B, int S, int H, int D, int K, float scale,
+                            int32_t* status, dsa_stream_t stream);
+
 /* Un-normalised partial attention for a sequence split: like
  * dsa_sparse_attn but without the sink and without normalisation; writes
  * part_ml [B*S, H, 2] = (m, l) and part_o [B*S, H, D] fp32 with

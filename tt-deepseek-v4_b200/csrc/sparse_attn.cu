@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "sparse_attn_tc.cuh"
 #include <stdlib.h>
+#include <mutex>
 
 namespace dsa {
 
@@ -520,4 +521,74 @@ extern "C" int dsa_set_trace(void* dev_buffer, size_t bytes) {
   DSA_CHECK_ARG(dev_buffer == nullptr || bytes >= need, "set_trace: buffer needs %zu bytes", need);
   g_trace = static_cast<long long*>(dev_buffer);
   return DSA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of dsa_sparse_attn.
+//
+// Some callers cannot allocate device memory at the point where they call the
+// attention: a host runtime that owns a fixed device arena and forbids other
+// allocations, a plugin called from inside another framework's memory
+// manager, or code running where cudaMalloc is unavailable or too slow.  For
+// them the split-K partials (the only scratch dsa_sparse_attn needs) live in
+// a file-scope device array that the library reserves once at load time.
+// Every GPU that loads the library holds these 8 MiB until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mu;
+
+// Device address of the scratch array for the current device.  The array's
+// name is only a host-side handle; its device address comes from
+// cudaGetSymbolAddress, resolved once per device with that device current.
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("sparse_attn_noalloc: no usable current device");
+    return DSA_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("sparse_attn_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return DSA_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DSA_OK;
+}
+
+}  // namespace
+
+extern "C" int dsa_sparse_attn_noalloc(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,
+                                       const int32_t* idx, int64_t ld_idx, const float* sink, void* out, float* lse,
+                                       int B, int S, int H, int D, int K, float scale, int32_t* status,
+                                       dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG(sink && out, "sparse_attn_noalloc: null sink/out");
+  DSA_CHECK_ARG(B >= 0 && S >= 1 && K >= 0, "sparse_attn_noalloc: bad B/S/K");
+  const size_t need = dsa_sparse_attn_workspace_size(B, S, H, D, K);
+  if (need > kNoAllocScratchBytes) {
+    set_error("sparse_attn_noalloc: this shape needs %zu bytes of scratch, above the built-in maximum of %zu "
+              "(use dsa_sparse_attn with a caller-owned workspace)",
+              need, kNoAllocScratchBytes);
+    return DSA_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != DSA_OK) return rc;
+  }
+  // Every split-K partial is written before it is read, so the scratch needs
+  // no clearing between calls.
+  return sparse_attn_run(q, kv, kv_bstride, kv_rows, idx, ld_idx, sink, out, lse, nullptr, nullptr, B, S, H, D, K,
+                         scale, scratch, need > 0 ? kNoAllocScratchBytes : 0, status,
+                         reinterpret_cast<cudaStream_t>(stream), true);
 }

@@ -43,6 +43,7 @@ PROTOTYPES = {
     "dsa_topk_merge": (I32, [P, P, I32, P, P, I64, I32, I32, I32, P]),
     "dsa_sparse_attn_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "dsa_sparse_attn": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
+    "dsa_sparse_attn_noalloc": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, P]),
     "dsa_sparse_attn_partial": (I32, [P, P, I64, I64, P, I64, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
     "dsa_lse_combine": (I32, [P, P, P, P, I32, I32, I32, I32, P]),
     "dsa_set_trace": (I32, [P, SZ]),
