@@ -335,10 +335,8 @@ static bool use_mma_v0() {
   return v == 1;
 }
 
-using TcSmall = satc::Cfg<64, 2>;  // 64-key tiles, 2-stage ring (tcgen05 issue cost favours N=64)
-
-static int split_tile() { return use_mma_v0() ? kSaTile : TcSmall::TK; }
-static int idx_cap() { return TcSmall::kIdxCap; }
+static int split_tile() { return use_mma_v0() ? kSaTile : satc::TK; }
+static int idx_cap() { return satc::kIdxCap; }
 
 static SplitPlan plan_splits(int M, int K) {
   const int tile = split_tile();
@@ -360,8 +358,8 @@ static void ensure_attr() {
   cudaGetDevice(&dev);
   if (done_dev != dev) {
     cudaFuncSetAttribute(sparse_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSaSmem);
-    cudaFuncSetAttribute(satc::sparse_attn_tc_kernel<TcSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         TcSmall::kSmemBytes);
+    cudaFuncSetAttribute(satc::sparse_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         satc::kSmemBytes);
 
     done_dev = dev;
   }
@@ -458,18 +456,14 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
     t.scale_log2 = a.scale_log2;
     t.final_mode = a.final_mode;
     t.trace = g_trace;
-    CUtensorMap tm_kv, tm_q;
+    CUtensorMap tm_q;
     DSA_CHECK_ARG(kv_bstride % kSaD == 0, "sparse_attn: kv batch stride must be a multiple of D");
     const int64_t row_stride = kv_bstride / kSaD;
-    const uint64_t kv_total_rows = uint64_t(B - 1) * row_stride + uint64_t(kv_rows);
-    DSA_CHECK_ARG(kv_total_rows < (1ull << 31), "sparse_attn: kv cache has more than 2^31 rows");
-    if (!tma::make_2d_bf16(&tm_kv, kv, kSaD, kv_total_rows, kSaD * 2, 64, 1) ||
-        !tma::make_2d_bf16(&tm_q, q, kSaD, uint64_t(M) * kSaH, kSaD * 2, 64, 64)) {
+    if (!tma::make_2d_bf16(&tm_q, q, kSaD, uint64_t(M) * kSaH, kSaD * 2, 64, 64)) {
       set_error("sparse_attn: cuTensorMapEncodeTiled failed");
       return DSA_ERR_CUDA;
     }
-    satc::sparse_attn_tc_kernel<TcSmall><<<dim3(p.nsplit, M), satc::THREADS, TcSmall::kSmemBytes, st>>>(
-        t, tm_kv, tm_q, row_stride);
+    satc::sparse_attn_tc_kernel<<<dim3(p.nsplit, M), satc::THREADS, satc::kSmemBytes, st>>>(t, tm_q, row_stride);
   }
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {

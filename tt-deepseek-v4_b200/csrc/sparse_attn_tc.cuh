@@ -1,26 +1,45 @@
 // attn.sparse on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// One CTA per (query row, key split); 6 warps with fixed roles:
-//   warps 5-8   gather producers: 16-byte cp.async of the selected kv rows
-//               (each warp owns 8 rows of every 32-row tile) into a 4-stage
-//               ring (128-B swizzled, K-major), plus L2 prefetches of the rows
-//               a few tiles ahead.  Many LSU-issuing warps are what saturates
-//               HBM for random 1 KB rows on B200 (a single TMA gather4 issuer
-//               tops out near 1.8 TB/s); the query's 64 x 512 Q block comes
-//               in once by 2-D TMA.
-//   warp 4      MMA issuer (one thread): S(t) = Q K_t^T  (M=64 heads, N=32
-//               keys, K=512) into a double-buffered TMEM slot, then
-//               O^T += V_t^T P(t-1)^T  (M=128 dims x4, N=64 heads, K=32 keys)
-//               into a TMEM accumulator that lives for the whole split.
-//   warps 0-3   softmax: lane l < 16 of warp w owns head 16w+l (the M=64
-//               accumulator layout puts row 16w+l in TMEM lane 32w+l); online
-//               softmax with lazy rescaling (the running max only moves when a
-//               tile beats it by 2^8, so P <= 256 and O^T is rarely touched);
-//               writes P as bf16 8x16-B core matrices; epilogue reads O^T back
-//               (TMEM lane = output dim, column = head) and stores coalesced.
-// The same shared-memory kv tile is the K-major B operand of Q K^T and the
-// MN-major A operand of V^T P^T, so each gathered row is read from HBM once
-// and from shared memory twice by the tensor cores.
+// One CTA per (query row, key split), 16 warps with fixed roles, 64-key tiles
+// held in a two-slot ring (2 x 64 KB) next to the query block Q (64 KB):
+//
+//   warps 5-7, 9-11, 13-15  gather producers.  Each selected kv row (1 KB) is copied whole,
+//               one 512-B half per warp instruction (16-byte cp.async from 32
+//               lanes), and scattered into the tile's eight 64-dim k-block
+//               slabs (128-B swizzled).  Measured on B200: random 1 KB rows
+//               requested whole reach ~7 TB/s from HBM, the same rows fetched
+//               128 B at a time only ~4.7 TB/s, and L2 prefetches do not help
+//               (they lowered it), so each row is read once, whole.  A tile
+//               completes on its slot's mbarrier through
+//               cp.async.mbarrier.arrive.
+//   warp 4      MMA issuer (one thread), ready-first over two kinds of batch:
+//               S(t)  = K_t Q^T   (M=64 keys, N=64 heads, K=512 dims; both
+//                       operands K-major) into one of two TMEM buffers (keys
+//                       in the M=64 lane layout, heads in columns), issued
+//                       once tile t has landed;
+//               PV(t): O^T += V_t^T P_t^T  (M=128 dims per block, N=64 heads,
+//                       K=64 keys; A = two adjacent k-block slabs read
+//                       MN-major, B = P, MN-major) into a TMEM accumulator that
+//                       lives for the whole split (lane = dim, column = head),
+//                       issued once the softmax of tile t wrote P; it then
+//                       releases the tile's slot for the next copy.
+//               A wait between dependent batches drains the tensor pipe
+//               (about 700 cycles measured), so the issuer keeps whichever
+//               batch is ready queued.
+//   warps 0-3   softmax.  The 16x256b TMEM load spreads the 64 x 64 scores
+//               over 128 threads: thread i of warp w holds keys 16w + i/4 and
+//               16w + 8 + i/4, heads 8r + 2(i%4) + {0,1}, r = 0..7.  The
+//               running max per head lives in shared memory and moves only
+//               when some score beats it by 2^8 (one barrier with an OR tells
+//               all 128 threads), so O^T is rescaled rarely and P <= 256.  P
+//               goes to one of two buffers as 128-B swizzled rows per key,
+//               written by stmatrix (the 16x256b fragment is its 8x8 layout).
+//               The epilogue reads O^T back (lane = output dim) and stores
+//               coalesced rows.
+//
+// Every mbarrier wait is bounded (about a second); a wait that runs out sets
+// a status bit and an abort flag that makes all later waits of the CTA return
+// at once, so a lost arrival ends the launch with an error instead of a hang.
 #pragma once
 
 #include "common.cuh"
@@ -32,41 +51,42 @@ namespace satc {
 
 constexpr int H = 64;
 constexpr int D = 512;
-constexpr int kProducerWarps = 4;
-constexpr int THREADS = 32 * (5 + kProducerWarps);
+constexpr int TK = 64;                                // keys per tile
+constexpr int KB = D / 64;                            // 64-dim k-blocks per row
+constexpr int NT = 2;                                 // tile slots
+constexpr int kSlabBytes = TK * 128;                  // one k-block of a tile: 8 KB
+constexpr int kTileBytes = KB * kSlabBytes;           // 64 KB
+// 16 warps, four per scheduler (warp % 4): softmax 0-3, MMA issuer 4, and the
+// producers on the schedulers of warps 1-3 only (5-7, 9-11, 13-15), so the
+// MMA issuer shares its scheduler with one softmax warp; warps 8 and 12 idle.
+constexpr int kProducerWarps = 9;
+constexpr int kMmaWarp = 4;
+constexpr int THREADS = 512;
+__device__ __forceinline__ bool is_producer_warp(int w) { return w >= 5 && (w & 3) != 0; }
+__device__ __forceinline__ int producer_index(int w) { return w - 5 - ((w - 4) >> 2); }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int kQBytes = H * D * 2;          // 64 KB, 8 k-blocks of [64 rows x 128 B]
-constexpr int kKBlockQ = H * 128;           // 8 KB
-constexpr int kAuxBytes = 2048;
+constexpr float kRescaleThreshold = 8.0f;             // log2 units
+constexpr int kQBytes = H * D * 2;                    // 64 KB: 8 k-blocks of [64 heads x 128 B]
+constexpr int kQBlock = H * 128;                      // 8 KB
+constexpr int kPBytes = TK * H * 2;                   // 8 KB per buffer: [64 keys x 64 heads] bf16
+constexpr int kMaxTilesPerSplit = 36;
+constexpr int kIdxCap = kMaxTilesPerSplit * TK;       // indices staged per split
+constexpr int kAuxBytes = 4096;
+constexpr int kOffQ = 0;
+constexpr int kOffRing = kOffQ + kQBytes;
+constexpr int kOffP = kOffRing + NT * kTileBytes;
+constexpr int kOffAux = kOffP + 2 * kPBytes;
+constexpr int kOffIdx = kOffAux + kAuxBytes;
+constexpr int kSmemBytes = kOffIdx + kIdxCap * 4 + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0;     // O^T: 4 blocks x 64 columns
-constexpr uint32_t kColS = 256;   // S: 2 buffers x TK columns
-constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 64, true, false);
-constexpr int kL2Ahead = 4;       // tiles prefetched into L2 beyond the ones being loaded
-
-// Tile geometry: TK keys per tile, NS ring stages.
-template <int TK_, int NS_>
-struct Cfg {
-  static constexpr int TK = TK_;
-  static constexpr int NS = NS_;
-  static constexpr int kTileBytes = TK * D * 2;      // 8 k-blocks of [TK rows x 128 B]
-  static constexpr int kKBlockT = TK * 128;
-  static constexpr int kPBytes = H * TK * 2;         // per buffer, 8x16-B core matrices
-  static constexpr int kPSbo = TK * 16;              // stride between 8-head groups of P
-  static constexpr int kIdxCap = 2048;
-  static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
-  static constexpr int kOffP = kOffK + NS * kTileBytes;
-  static constexpr int kOffAux = kOffP + 2 * kPBytes;
-  static constexpr int kOffIdx = kOffAux + kAuxBytes;
-  static constexpr int kSmemBytes = kOffIdx + kIdxCap * 4 + 1024;
-  static constexpr uint32_t kIdescS = tc::idesc_bf16(64, TK, false, false);
-  static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert(TK == 64, "the softmax fragment mapping is written for 64-key tiles");
-  static_assert(kColS + 2 * TK <= kTmemCols, "TMEM columns");
-};
+constexpr uint32_t kColO = 0;                          // O^T: 4 blocks of [128 dims x 64 heads]
+constexpr uint32_t kColS = 256;                        // S: 2 buffers of [64 keys x 64 heads], M=64 layout
+constexpr uint32_t kIdescS = tc::idesc_bf16(64, 64, false, false);
+constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 64, true, true);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kColS + 2 * H <= kTmemCols, "TMEM columns");
+static_assert(TK % 16 == 0 && TK <= 64, "tile");
 
 enum : int { kStatusBadIndex = 1, kStatusTimeout = 2 };
 
@@ -89,8 +109,9 @@ struct Args {
   long long* trace;  // optional: per-tile clock64 stamps of CTA (0, 0), see kTr*
 };
 
-// trace slots (each kTrTiles long): producer issued / producer signalled /
-// MMA got tile / MMA issued S / MMA issued PV / softmax got S / softmax done P
+// trace slots (each kTrTiles long): producers issued tile t / MMA got tile t /
+// MMA issued S(t) / MMA issued PV(t) / softmax got S(t) / softmax wrote P(t) /
+// misc (0: start, 1: end)
 enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3, kTrPV = 4, kTrSGot = 5, kTrPDone = 6,
              kTrMisc = 7 };
 #define SA_TRACE(slot, t)                                                                         \
@@ -99,38 +120,38 @@ enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3,
   } while (0)
 
 struct Aux {
+  float m[H];        // running max per head (log2 units)
+  float alpha[H];    // rescale factor of the last max update
+  float f[H];        // epilogue scale per head
+  float red[4][H];   // per-warp partial reductions
   uint64_t q_full;
-  uint64_t full[4];
-  uint64_t empty[4];
+  uint64_t full[NT];
+  uint64_t empty[NT];
   uint64_t s_full[2];
   uint64_t s_free[2];
   uint64_t p_full[2];
-  uint64_t o_done[2];
+  uint64_t pv_done[2];
+  uint64_t mma_done;
   uint32_t tmem_base;
-  int any[4];
-  float alpha[H];
-  float m[H];
-  float l[H];
-  float f[H];
+  int abort;
 };
+static_assert(sizeof(Aux) <= kAuxBytes, "aux block");
 
-// byte offset of 16-B chunk c (0..63, 8 dims each) of row r in a [rows x 512]
-// bf16 tile stored as 8 k-blocks of [rows x 128 B] with the 128-B swizzle
-__device__ __forceinline__ uint32_t sw128_off(int r, int c, int kblock_bytes) {
-  return (c >> 3) * kblock_bytes + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+// byte offset of 16-B chunk c (0..63) of tile row r: k-block slab c / 8, then
+// the 128-B swizzle of row r inside the slab
+__device__ __forceinline__ uint32_t chunk_off(int r, int c) {
+  return (c >> 3) * kSlabBytes + r * 128 + ((((c & 7) ^ (r & 7))) << 4);
 }
 
-template <class C>
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a,
-                                                                    const __grid_constant__ CUtensorMap tm_kv,
                                                                     const __grid_constant__ CUtensorMap tm_q,
                                                                     int64_t kv_row_base_stride) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int TK = C::TK, NS = C::NS, kTileBytes = C::kTileBytes, kKBlockT = C::kKBlockT, kPBytes = C::kPBytes;
-  Aux* aux = reinterpret_cast<Aux*>(smem + C::kOffAux);
+  Aux* aux = reinterpret_cast<Aux*>(smem + kOffAux);
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t sQ = sbase + C::kOffQ, sK = sbase + C::kOffK, sP = sbase + C::kOffP;
+  const uint32_t sQ = sbase + kOffQ, sRing = sbase + kOffRing, sP = sbase + kOffP;
+  volatile int* abort_flag = &aux->abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m = blockIdx.y, split = blockIdx.x;
@@ -139,7 +160,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   const int j_end = min(a.K, j_begin + a.tiles_per_split * TK);
   const int n = j_end > j_begin ? (j_end - j_begin + TK - 1) / TK : 0;
   const int32_t* idxr = a.idx + int64_t(m) * a.ld_idx;
-  int32_t* s_idx = reinterpret_cast<int32_t*>(smem + C::kOffIdx);
+  int32_t* s_idx = reinterpret_cast<int32_t*>(smem + kOffIdx);
   long long* tr = (a.trace && blockIdx.x == 0 && blockIdx.y == 0) ? a.trace : nullptr;
   if (tid == 0) SA_TRACE(kTrMisc, 0);
 
@@ -152,8 +173,10 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       if (a.status) atomicOr(a.status, kStatusBadIndex);
       id = int(a.kv_rows - 1);
     }
-    s_idx[e] = id;
+    s_idx[e] = id < 0 ? -1 : id;
   }
+  if (tid < H) aux->m[tid] = -INFINITY;
+  if (tid == 0) aux->abort = 0;
 
   if (warp == 0) {
     tc::tmem_alloc(smem_u32(&aux->tmem_base), kTmemCols);
@@ -161,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   }
   if (tid == 32) {
     tc::mbar_init(smem_u32(&aux->q_full), 1);
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < NT; ++s) {
       tc::mbar_init(smem_u32(&aux->full[s]), 32 * kProducerWarps);  // one cp.async arrival per producer lane
       tc::mbar_init(smem_u32(&aux->empty[s]), 1);
     }
@@ -169,10 +192,11 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tc::mbar_init(smem_u32(&aux->s_full[s]), 1);
       tc::mbar_init(smem_u32(&aux->s_free[s]), 4);
     }
-    tc::mbar_init(smem_u32(&aux->p_full[0]), 1);
-    tc::mbar_init(smem_u32(&aux->p_full[1]), 1);
-    tc::mbar_init(smem_u32(&aux->o_done[0]), 1);
-    tc::mbar_init(smem_u32(&aux->o_done[1]), 1);
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(smem_u32(&aux->p_full[s]), 1);
+      tc::mbar_init(smem_u32(&aux->pv_done[s]), 1);
+    }
+    tc::mbar_init(smem_u32(&aux->mma_done), 1);
     tc::mbar_fence_init();
   }
   tc::fence_before_sync();
@@ -180,197 +204,235 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   tc::fence_after_sync();
   const uint32_t tmem = aux->tmem_base;
 
-  if (warp >= 5) {
-    // ------------------------------------------------------------ producers (warps 5..)
-    const int pw = warp - 5;  // rows [8 pw, 8 pw + 8) of every tile
+  auto wait = [&](const uint64_t* bar, uint32_t parity) {
+    if (*abort_flag) return;
+    if (!tc::mbar_wait(smem_u32(bar), parity, a.status, kStatusTimeout)) *abort_flag = 1;
+  };
+  // whole-warp wait with one polling lane
+  auto warp_wait = [&](const uint64_t* bar, uint32_t parity) {
+    if (lane == 0) wait(bar, parity);
+    __syncwarp();
+  };
+
+  if (is_producer_warp(warp)) {
+    // ------------------------------------------------------------ producers
+    const int pw = producer_index(warp);
     if (pw == 0 && lane == 0 && n > 0) {
       tma::prefetch_map(&tm_q);
       tma::mbar_arrive_expect_tx(smem_u32(&aux->q_full), kQBytes);
 #pragma unroll
-      for (int kb = 0; kb < 8; ++kb)
-        tma::load_2d(sQ + kb * kKBlockQ, &tm_q, kb * 64, m * H, smem_u32(&aux->q_full));
+      for (int kb = 0; kb < KB; ++kb) tma::load_2d(sQ + kb * kQBlock, &tm_q, kb * 64, m * H, smem_u32(&aux->q_full));
     }
     const __nv_bfloat16* kvb = a.kv + int64_t(b) * kv_row_base_stride * D;
-    constexpr int kRowsPerWarp = TK / kProducerWarps;      // 8
-    const int rr = lane >> 3, cc = lane & 7;
-    // L2 prefetch of this warp's rows of tile u: 8 rows x 8 lines of 128 B
-    auto prefetch_tile = [&](int u) {
-#pragma unroll
-      for (int i = 0; i < kRowsPerWarp * 8 / 32; ++i) {
-        const int e = i * 32 + lane, r = e >> 3, line = e & 7;
-        const int id = s_idx[u * TK + pw * kRowsPerWarp + r];
-        if (id >= 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(kvb + int64_t(id) * D + line * 64));
-      }
-    };
-    for (int u = 0; u < min(n, NS + kL2Ahead); ++u) prefetch_tile(u);
     for (int t = 0; t < n; ++t) {
-      const int stage = t % NS;
-      if (t + NS + kL2Ahead < n) prefetch_tile(t + NS + kL2Ahead);
-      if (t >= NS) tc::mbar_wait(smem_u32(&aux->empty[stage]), ((t / NS) - 1) & 1, a.status, kStatusTimeout);
-      const uint32_t dst = sK + stage * kTileBytes;
-#pragma unroll
-      for (int rg = 0; rg < kRowsPerWarp / 4; ++rg) {
-        const int r = pw * kRowsPerWarp + rg * 4 + rr;
+      const int slot = t % NT;
+      if (t >= NT) warp_wait(&aux->empty[slot], ((t / NT) - 1) & 1);
+      const uint32_t dst = sRing + slot * kTileBytes;
+      // rows pw, pw + P, ...: lane copies 16-B chunks lane and lane + 32
+      for (int r = pw; r < TK; r += kProducerWarps) {
         const int id = s_idx[t * TK + r];
         const bool ok = id >= 0;
-        const __nv_bfloat16* src = kvb + int64_t(ok ? id : 0) * D + cc * 8;
-#pragma unroll
-        for (int kb = 0; kb < 8; ++kb)
-          cp_async16(dst + sw128_off(r, kb * 8 + cc, kKBlockT), src + kb * 64, ok ? 16 : 0);
+        const __nv_bfloat16* src = kvb + int64_t(ok ? id : 0) * D;
+        cp_async16(dst + chunk_off(r, lane), src + lane * 8, ok ? 16 : 0);
+        cp_async16(dst + chunk_off(r, lane + 32), src + (lane + 32) * 8, ok ? 16 : 0);
       }
-      // each lane's arrival fires when its copies of this tile have landed
-      tc::cp_async_arrive_noinc(smem_u32(&aux->full[stage]));
+      // this lane's arrival fires when its copies of the tile have landed
+      tc::cp_async_arrive_noinc(smem_u32(&aux->full[slot]));
       if (pw == 0 && lane == 0) SA_TRACE(kTrIssue, t);
     }
     cp_async_wait<0>();
-  } else if (warp == 4) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n > 0) {
-      const uint32_t hi_sw128 = tc::desc_hi(1024, tc::kLayoutSw128);
-      const uint32_t hi_v = tc::desc_hi(1024, tc::kLayoutSw128);
-      const uint32_t hi_p = tc::desc_hi(C::kPSbo, tc::kLayoutNone);
+      const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
       const uint32_t q_lo = tc::desc_lo(sQ, 16);
-      tc::mbar_wait(smem_u32(&aux->q_full), 0, a.status, kStatusTimeout);
-      auto issue_pv = [&](int u) {
-        tc::mbar_wait(smem_u32(&aux->p_full[u & 1]), (u >> 1) & 1, a.status, kStatusTimeout);
-        tc::fence_after_sync();
-        const uint32_t v_lo = tc::desc_lo(sK + (u % NS) * kTileBytes, kKBlockT);
-        const uint32_t p_lo = tc::desc_lo(sP + (u & 1) * kPBytes, 128);
+      const uint32_t k_lo = tc::desc_lo(sRing, 16);          // K-major: LBO unused
+      const uint32_t v_lo = tc::desc_lo(sRing, kSlabBytes);  // MN-major: LBO = the next 64 dims (next slab)
+      const uint32_t p_lo = tc::desc_lo(sP, kPBytes);        // MN-major, one 64-head group
+      wait(&aux->q_full, 0);
+      // Ready-first issue: PV(np) as soon as P(np) is written (it frees the
+      // tile's slot for the next copy), else S(ns) as soon as tile ns has
+      // landed and its S buffer is free.  Keeping MMAs queued avoids the
+      // ~700-cycle drain and refill of the tensor pipe that a wait between
+      // dependent batches costs.
+      int ns = 0, np = 0;
+      long long last = clock64();
+      while (np < n) {
+        bool did = false;
+        if (np < ns && tc::mbar_try_wait(smem_u32(&aux->p_full[np & 1]), (np >> 1) & 1)) {
+          tc::fence_after_sync();
+          const uint32_t vs = v_lo + (np % NT) * (kTileBytes / 16);
+          const uint32_t ps = p_lo + (np & 1) * (kPBytes / 16);
+          // PV(np): 16 MMAs of M=128 dims x N=64 heads x K=16 keys
 #pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk) {
+          for (int jb = 0; jb < KB / 2; ++jb) {
 #pragma unroll
-          for (int jb = 0; jb < 4; ++jb) {
-            const uint64_t ad = tc::desc_pack(v_lo + ((2 * jb) * kKBlockT + kk * 16 * 128) / 16, hi_v);
-            const uint64_t bd = tc::desc_pack(p_lo + (kk * 256) / 16, hi_p);
-            tc::mma_bf16(tmem + kColO + 64 * jb, ad, bd, kIdescPV, (u > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < TK / 16; ++kk) {
+              const uint64_t ad = tc::desc_pack(vs + (2 * jb * kSlabBytes + kk * 2048) / 16, hi);
+              const uint64_t bd = tc::desc_pack(ps + (kk * 2048) / 16, hi);
+              tc::mma_bf16(tmem + kColO + H * jb, ad, bd, kIdescPV, (np > 0 || kk > 0) ? 1u : 0u);
+            }
           }
-        }
-        tc::mma_commit(smem_u32(&aux->o_done[u & 1]));
-        tc::mma_commit(smem_u32(&aux->empty[u % NS]));
-        SA_TRACE(kTrPV, u);
-      };
-      for (int t = 0; t < n; ++t) {
-        const int stage = t % NS;
-        tc::mbar_wait(smem_u32(&aux->full[stage]), (t / NS) & 1, a.status, kStatusTimeout);
-        SA_TRACE(kTrMmaGot, t);
-        if (t >= 2) tc::mbar_wait(smem_u32(&aux->s_free[t & 1]), ((t - 2) >> 1) & 1, a.status, kStatusTimeout);
-        tc::fence_after_sync();
-        const uint32_t kt = sK + stage * kTileBytes;
-        // S(t) = Q K_t^T: 32 MMAs of M=64 heads x N=64 keys x K=16 (an MMA costs
-        // ~47 cycles up to N=64, so a 64-key tile halves the per-key issue cost)
-        const uint32_t sbuf = tmem + kColS + (t & 1) * TK;
-        const uint32_t kt_lo = tc::desc_lo(kt, 16);
+          tc::mma_commit(smem_u32(&aux->empty[np % NT]));
+          tc::mma_commit(smem_u32(&aux->pv_done[np & 1]));
+          SA_TRACE(kTrPV, np);
+          ++np;
+          did = true;
+        } else if (ns < n && ns < np + NT && tc::mbar_try_wait(smem_u32(&aux->full[ns % NT]), (ns / NT) & 1) &&
+                   (ns < 2 || tc::mbar_try_wait(smem_u32(&aux->s_free[ns & 1]), ((ns - 2) >> 1) & 1))) {
+          tc::fence_after_sync();
+          SA_TRACE(kTrMmaGot, ns);
+          const uint32_t ks0 = k_lo + (ns % NT) * (kTileBytes / 16);
+          const uint32_t d = tmem + kColS + H * (ns & 1);
+          // S(ns): 32 MMAs of M=64 keys x N=64 heads x K=16 dims
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint64_t ad = tc::desc_pack(q_lo + ((ks >> 2) * kKBlockQ + (ks & 3) * 32) / 16, hi_sw128);
-          const uint64_t bd = tc::desc_pack(kt_lo + ((ks >> 2) * kKBlockT + (ks & 3) * 32) / 16, hi_sw128);
-          tc::mma_bf16(sbuf, ad, bd, C::kIdescS, ks > 0 ? 1u : 0u);
+          for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t ad = tc::desc_pack(ks0 + (kb * kSlabBytes + ks * 32) / 16, hi);
+              const uint64_t bd = tc::desc_pack(q_lo + (kb * kQBlock + ks * 32) / 16, hi);
+              tc::mma_bf16(d, ad, bd, kIdescS, (kb | ks) ? 1u : 0u);
+            }
+          }
+          tc::mma_commit(smem_u32(&aux->s_full[ns & 1]));
+          SA_TRACE(kTrS, ns);
+          ++ns;
+          did = true;
         }
-        tc::mma_commit(smem_u32(&aux->s_full[t & 1]));
-        SA_TRACE(kTrS, t);
-        if (t >= 1) issue_pv(t - 1);
+        if (did) {
+          last = clock64();
+        } else if (*abort_flag || clock64() - last > tc::kWaitCycles) {
+          if (!*abort_flag && a.status) atomicOr(a.status, kStatusTimeout);
+          *abort_flag = 1;
+          break;
+        }
       }
-      issue_pv(n - 1);
+      // every MMA of this CTA has completed before TMEM is released
+      tc::mma_commit(smem_u32(&aux->mma_done));
+      tc::mbar_wait(smem_u32(&aux->mma_done), 0, a.status, kStatusTimeout);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 4) {
     // ------------------------------------------------------------ softmax warps 0-3
-    // S rows (heads) 16w..16w+15 live in TMEM lanes 32w..32w+15 (M=64 layout);
-    // the 16x256b load spreads each row over a quad: thread i holds heads
-    // h0 = 16w + i/4 and h1 = h0 + 8, keys 8r + 2(i%4) + {0,1}, r = 0..7.
-    const int q4 = lane & 3, g = lane >> 2;
-    const int h0 = warp * 16 + g, h1 = h0 + 8;
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    // S rows (keys) 16w..16w+15 sit in TMEM lanes 32w..32w+15 (M=64 layout).
+    const int q4 = lane & 3, g8 = lane >> 2;
+    const int ka = warp * 16 + g8, kb2 = ka + 8;  // this thread's two keys
+    const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+    // [r][e] -> head 8r + 2 q4 + e: running max (a register copy of aux->m)
+    // and partial sums of p over this thread's keys
+    float mr[16], lp[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      mr[i] = -INFINITY;
+      lp[i] = 0.f;
+    }
+    // stmatrix x4 number j writes the 8x8 blocks (keys 16w + 8g.., heads
+    // 8r..) for (g, r) = (0, 2j), (1, 2j), (0, 2j+1), (1, 2j+1); lane l gives
+    // the address of row l % 8 of block l / 8: one 16-B chunk of a P row
+    const int sm_g = (lane >> 3) & 1, sm_r = lane >> 4, sm_key = warp * 16 + 8 * sm_g + (lane & 7);
     for (int t = 0; t < n; ++t) {
-      uint64_t vmask = __ballot_sync(0xffffffffu, s_idx[t * TK + lane] >= 0);
-      vmask |= uint64_t(__ballot_sync(0xffffffffu, s_idx[t * TK + 32 + lane] >= 0)) << 32;
-      tc::mbar_wait(smem_u32(&aux->s_full[t & 1]), (t >> 1) & 1, a.status, kStatusTimeout);
+      const bool va = s_idx[t * TK + ka] >= 0, vb = s_idx[t * TK + kb2] >= 0;
+      warp_wait(&aux->s_full[t & 1], (t >> 1) & 1);
       tc::fence_after_sync();
       if (tid == 0) SA_TRACE(kTrSGot, t);
       float v[32];
-      tc::tmem_ld16x256b_x8(trow + kColS + TK * (t & 1), v);
+      tc::tmem_ld16x256b_x8(tq + kColS + H * (t & 1), v);
       tc::tmem_wait_ld();
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(smem_u32(&aux->s_free[t & 1]));
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+      bool need = false;
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
+        v[4 * r + 0] = va ? v[4 * r + 0] * a.scale_log2 : -INFINITY;
+        v[4 * r + 1] = va ? v[4 * r + 1] * a.scale_log2 : -INFINITY;
+        v[4 * r + 2] = vb ? v[4 * r + 2] * a.scale_log2 : -INFINITY;
+        v[4 * r + 3] = vb ? v[4 * r + 3] * a.scale_log2 : -INFINITY;
+        need |= fmaxf(v[4 * r + 0], v[4 * r + 2]) > mr[2 * r] + kRescaleThreshold;
+        need |= fmaxf(v[4 * r + 1], v[4 * r + 3]) > mr[2 * r + 1] + kRescaleThreshold;
+      }
+      const bool any = tc::named_bar_red_or(1, 128, need);
+      if (any) {
+        // tile max per head: this thread's two keys, then the 8 lanes that
+        // share q4 (xor 4, 8, 16), then the 4 warps through shared memory
+        float mx[16];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const bool ok = (vmask >> (8 * r + 2 * q4 + e)) & 1ull;
-          v[4 * r + e] = ok ? v[4 * r + e] * a.scale_log2 : -INFINITY;
-          v[4 * r + 2 + e] = ok ? v[4 * r + 2 + e] * a.scale_log2 : -INFINITY;
-          mx0 = fmaxf(mx0, v[4 * r + e]);
-          mx1 = fmaxf(mx1, v[4 * r + 2 + e]);
+        for (int r = 0; r < 8; ++r) {
+          mx[2 * r] = fmaxf(v[4 * r + 0], v[4 * r + 2]);
+          mx[2 * r + 1] = fmaxf(v[4 * r + 1], v[4 * r + 3]);
         }
-      }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const bool need0 = mx0 > m0 + kRescaleThreshold, need1 = mx1 > m1 + kRescaleThreshold;
-      const float mn0 = need0 ? mx0 : m0, mn1 = need1 ? mx1 : m1;
-      const float al0 = need0 ? tc::ex2(m0 - mn0) : 1.f, al1 = need1 ? tc::ex2(m1 - mn1) : 1.f;
-      float rs0 = 0.f, rs1 = 0.f;
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
+        for (int off = 4; off < 32; off <<= 1)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          v[4 * r + e] = (v[4 * r + e] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + e] - mn0);
-          v[4 * r + 2 + e] = (v[4 * r + 2 + e] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 2 + e] - mn1);
-          rs0 += v[4 * r + e];
-          rs1 += v[4 * r + 2 + e];
+          for (int i = 0; i < 16; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], off));
+        if (g8 == 0) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            aux->red[warp][8 * r + 2 * q4] = mx[2 * r];
+            aux->red[warp][8 * r + 2 * q4 + 1] = mx[2 * r + 1];
+          }
         }
-      }
-      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
-      rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
-      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
-      rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
-      l0 = l0 * al0 + rs0;
-      l1 = l1 * al1 + rs1;
-      m0 = mn0;
-      m1 = mn1;
-      if (q4 == 0) {
-        aux->alpha[h0] = al0;
-        aux->alpha[h1] = al1;
-      }
-      // P(t) goes to buffer t&1, last read by PV(t-2); a rescale of O^T also
-      // needs PV(t-1) finished.  One o_done barrier per buffer keeps every
-      // wait within one phase of its barrier.
-      if (t >= 2) tc::mbar_wait(smem_u32(&aux->o_done[t & 1]), ((t - 2) >> 1) & 1, a.status, kStatusTimeout);
-      const bool any = tc::named_bar_red_or(1, 128, need0 || need1);
-      if (any && t >= 1) {
-        tc::mbar_wait(smem_u32(&aux->o_done[(t - 1) & 1]), ((t - 1) >> 1) & 1, a.status, kStatusTimeout);
-        tc::fence_after_sync();
+        tc::named_bar_sync(1, 128);
+        if (tid < H) {
+          const float tmax = fmaxf(fmaxf(aux->red[0][tid], aux->red[1][tid]), fmaxf(aux->red[2][tid], aux->red[3][tid]));
+          const float mo = aux->m[tid];
+          const float mn = fmaxf(mo, tmax);
+          aux->alpha[tid] = (mn == -INFINITY) ? 1.f : tc::ex2(mo - mn);
+          aux->m[tid] = mn;
+        }
+        tc::named_bar_sync(1, 128);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float2 al = *reinterpret_cast<const float2*>(&aux->alpha[8 * r + 2 * q4]);
+          const float2 mn = *reinterpret_cast<const float2*>(&aux->m[8 * r + 2 * q4]);
+          lp[2 * r] *= al.x;
+          lp[2 * r + 1] *= al.y;
+          mr[2 * r] = mn.x;
+          mr[2 * r + 1] = mn.y;
+        }
+        if (t >= 1) {
+          // (rare) O^T *= alpha per column, once PV(t-1) has completed
+          warp_wait(&aux->pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1);
+          tc::fence_after_sync();
+          const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+          const volatile float* alv = aux->alpha;
 #pragma unroll 1
-        for (int jb = 0; jb < 4; ++jb) {
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
+          for (int cb = 0; cb < 8; ++cb) {
             float o[32];
-            const uint32_t ta = trow + kColO + 64 * jb + 32 * hf;
+            const uint32_t ta = tl + kColO + 32 * cb;
             tc::tmem_ld32(ta, o);
             tc::tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= aux->alpha[32 * hf + i];
+            for (int i = 0; i < 32; ++i) o[i] *= alv[32 * (cb & 1) + i];
             tc::tmem_st32(ta, o);
           }
+          tc::tmem_wait_st();
         }
-        tc::tmem_wait_st();
       }
-      {
-        // P rows h0/h1: keys 8r + 2 q4 + {0,1} -> core matrix (h/8, r), row h%8, bytes 4 q4
-        const uint32_t pb = sP + (t & 1) * kPBytes + q4 * 4;
-        const uint32_t p0 = pb + (h0 >> 3) * C::kPSbo + (h0 & 7) * 16;
-        const uint32_t p1 = pb + (h1 >> 3) * C::kPSbo + (h1 & 7) * 16;
+      // p = 2^(x - m) <= 2^8, packed to bf16 pairs: pa[r] for key ka, pb[r]
+      // for key kb2, heads 8r + 2 q4 + {0, 1}
+      uint32_t pa[8], pb[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(p0 + r * 128), "r"(pack_bf16x2(v[4 * r], v[4 * r + 1]))
-                       : "memory");
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(p1 + r * 128), "r"(pack_bf16x2(v[4 * r + 2], v[4 * r + 3]))
-                       : "memory");
-        }
+      for (int r = 0; r < 8; ++r) {
+        const float p0 = (v[4 * r + 0] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 0] - mr[2 * r]);
+        const float p1 = (v[4 * r + 1] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 1] - mr[2 * r + 1]);
+        const float p2 = (v[4 * r + 2] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 2] - mr[2 * r]);
+        const float p3 = (v[4 * r + 3] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 3] - mr[2 * r + 1]);
+        lp[2 * r] += p0 + p2;
+        lp[2 * r + 1] += p1 + p3;
+        pa[r] = pack_bf16x2(p0, p1);
+        pb[r] = pack_bf16x2(p2, p3);
+      }
+      // P buffer t & 1 was last read by PV(t-2)
+      if (t >= 2) warp_wait(&aux->pv_done[t & 1], ((t - 2) >> 1) & 1);
+      const uint32_t pbuf = sP + (t & 1) * kPBytes;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = 2 * j + sm_r;
+        const uint32_t addr = pbuf + sm_key * 128 + ((r ^ (sm_key & 7)) << 4);
+        asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pa[2 * j]),
+                     "r"(pb[2 * j]), "r"(pa[2 * j + 1]), "r"(pb[2 * j + 1])
+                     : "memory");
       }
       tc::fence_proxy_async();
       tc::fence_before_sync();
@@ -379,17 +441,24 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       if (tid == 0) SA_TRACE(kTrPDone, t);
     }
     // ---------------------------------------------------------------- epilogue
-    if (n > 0) tc::mbar_wait(smem_u32(&aux->o_done[(n - 1) & 1]), ((n - 1) >> 1) & 1, a.status, kStatusTimeout);
+    if (n > 0) warp_wait(&aux->pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1);
     tc::fence_after_sync();
-    if (q4 == 0) {
-      aux->m[h0] = m0;
-      aux->l[h0] = l0;
-      aux->m[h1] = m1;
-      aux->l[h1] = l1;
+    // l per head: the 8 lanes sharing q4, then the 4 warps
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) lp[i] += __shfl_xor_sync(0xffffffffu, lp[i], off);
+    if (g8 == 0) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        aux->red[warp][8 * r + 2 * q4] = lp[2 * r];
+        aux->red[warp][8 * r + 2 * q4 + 1] = lp[2 * r + 1];
+      }
     }
     tc::named_bar_sync(1, 128);
     if (tid < H) {
-      const float mh = aux->m[tid], lh = aux->l[tid];
+      const float mh = aux->m[tid];
+      const float lh = (aux->red[0][tid] + aux->red[1][tid]) + (aux->red[2][tid] + aux->red[3][tid]);
       if (a.final_mode) {
         const float sk = a.sink[tid] * kLog2e;
         const float Mx = fmaxf(mh, sk);
@@ -405,28 +474,29 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       }
     }
     tc::named_bar_sync(1, 128);
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
     const int dloc = warp * 32 + lane;
 #pragma unroll 1
     for (int jb = 0; jb < 4; ++jb) {
       const int d = 128 * jb + dloc;
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        float v[32];
+        float o[32];
         if (n > 0) {
-          tc::tmem_ld32(trow + kColO + 64 * jb + 32 * hf, v);
+          tc::tmem_ld32(tl + kColO + H * jb + 32 * hf, o);
           tc::tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
         }
         if (a.final_mode) {
           __nv_bfloat16* om = a.out + int64_t(m) * H * D + d;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) om[(32 * hf + i) * D] = f2bf(v[i] * aux->f[32 * hf + i]);
+          for (int i = 0; i < 32; ++i) om[(32 * hf + i) * D] = f2bf(o[i] * aux->f[32 * hf + i]);
         } else {
           float* po = a.part_o + (int64_t(split) * a.M + m) * H * D + d;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) po[(32 * hf + i) * D] = v[i];
+          for (int i = 0; i < 32; ++i) po[(32 * hf + i) * D] = o[i];
         }
       }
     }

@@ -158,14 +158,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each poll may itself block for a
-// hardware-defined interval), records `code` in *status and returns false.
+// Bounded wait: polls until the phase completes or `limit_cycles` SM clocks
+// (default about one second at B200 clocks) have passed; then records `code`
+// in *status and returns false, so a lost arrival ends the kernel with an
+// error status instead of hanging the GPU.
+constexpr long long kWaitCycles = 2000000000ll;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status, int code,
-                                          uint32_t limit = (1u << 24)) {
-  for (uint32_t i = 0; i < limit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  if (status) atomicOr(status, code);
-  return false;
+                                          long long limit_cycles = kWaitCycles) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > limit_cycles) {
+      if (status) atomicOr(status, code);
+      return false;
+    }
+  }
+  return true;
 }
 
 // barrier over `nthreads` threads that also ORs a predicate across them
