@@ -183,27 +183,38 @@ def build_path(args, dev, seed):
 
 
 def time_kernels(path, inputs, outs, reps=3):
-    """CUDA-event time per launch of each kernel kind, each looped over all
-    layers (distinct caches, so nothing stays in L2) on the launching stream."""
+    """Device time per launch of each kernel kind: the op is captured over all
+    layers (distinct caches, so nothing stays in L2) in one CUDA graph and the
+    graph is timed with CUDA events on the replaying stream, so host launch
+    overhead does not enter the figure."""
     import torch
     from dsv4attn import ops
-    st = torch.cuda.current_stream()
     res = {}
-    a = path.args
 
     def run(name, fn):
-        fn()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            fn()
+        torch.cuda.current_stream().wait_stream(st)
         torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        cur = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         best = None
         for _ in range(reps):
-            e0.record(st)
-            fn()
-            e1.record(st)
+            e0.record(cur)
+            g.replay()
+            e1.record(cur)
             e1.synchronize()
             ms = e0.elapsed_time(e1) / len(path.layers)
             best = ms if best is None else min(best, ms)
         res[name] = best
+        del g
 
     run("sparse_attn", lambda: [ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, path.scale, out=o, ws=L.ws)
                                 for L, x, o in zip(path.layers, inputs, outs)])

@@ -126,6 +126,58 @@ def test_topk_random_sets(cuda_dev, B, T, k, ta):
     assert int((got == -1).sum()) == int((want == -1).sum())
 
 
+def _exact_topk_rows(score, tact, k, win):
+    """Deterministic top-k with -inf masking (mask_mode 1): every position
+    above the k-th value, then the lowest positions equal to it; -1 for picks
+    that are masked."""
+    out = []
+    for b in range(score.shape[0]):
+        row = score[b].clone()
+        row[int(tact[b]):] = float("-inf")
+        thr = torch.sort(row, descending=True).values[k - 1]
+        above = torch.nonzero(row > thr).flatten().tolist()
+        eq = torch.nonzero(row == thr).flatten().tolist()
+        pick = above + eq[:k - len(above)]
+        out.append(sorted((i + win) if row[i] >= -1000 else -1 for i in pick))
+    return out
+
+
+@pytest.mark.parametrize("kind", ["quantized", "cluster", "lognormal", "floor", "equal", "few", "prod"])
+def test_topk_exact_distributions(cuda_dev, kind):
+    """Exact sets (ties to the lowest position) on score distributions that
+    drive every branch of the selection: quantized and clustered values
+    (several levels, exact-value exit), very wide dynamic range, thresholds at
+    the masked floor, all-equal rows, short rows, and the production shape."""
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(sum(map(ord, kind)))
+    B, T, k, ta = 3, 9216, 2048, 8192
+    if kind == "quantized":
+        score = torch.randint(0, 40, (B, T), generator=g).float() * 0.25
+    elif kind == "cluster":
+        score = torch.ones(B, T)
+        hot = torch.rand(B, T, generator=g) < 0.01
+        score[hot] = 1.0 + torch.rand(int(hot.sum()), generator=g)
+        score[:, ::7] = 1.0 - 1e-7 * torch.arange(0, T, 7).float()
+    elif kind == "lognormal":
+        score = torch.exp(20.0 * torch.randn(B, T, generator=g))
+    elif kind == "floor":
+        score = torch.randn(B, T, generator=g)
+        ta = 1500  # fewer live positions than k
+    elif kind == "equal":
+        score = torch.full((B, T), -3.5)
+    elif kind == "few":
+        T, k, ta = 300, 64, 250
+        score = torch.randn(B, T, generator=g)
+    else:
+        B = 64
+        score = 0.02 * torch.randn(B, T, generator=g).abs()
+    tact = torch.full((B,), ta, dtype=torch.int32)
+    got = ops.indexer_topk(score.to(cuda_dev), tact.to(cuda_dev), k, 128, T=T, mask_mode=1).cpu()
+    want = _exact_topk_rows(score, tact, k, 128)
+    for b in range(B):
+        assert sorted(got[b].tolist()) == want[b], f"{kind} row {b}"
+
+
 def test_topk_mask_mode_exclusion_equivalent(cuda_dev):
     from dsv4attn import ops
     B, T, k = 3, 4096, 512

@@ -5,11 +5,16 @@
 //   out = idx + win where val >= -1000 else -1
 // and the window table rows (479-506, picked at 6020-6026).
 //
-// Selection is an exact block-level radix select over order-preserving
-// uint32 keys of the fp32 masked scores: four 8-bit digit passes over the
-// candidates held in shared memory, each a warp-aggregated (match_any)
-// histogram plus a one-warp suffix scan, find the k-th key; a final
-// deterministic compaction emits every key above it and the lowest-index
+// Selection is exact and deterministic.  Each thread keeps its keys (the
+// order-preserving uint32 of the masked fp32 scores) in registers.  The first
+// level histograms the live scores linearly in value between their min and
+// max into 256 bins (a monotone map, so exact; masked -inf positions are left
+// out when at least k keys lie above them), a one-warp suffix scan finds the
+// bin holding the k-th largest, and only that bin's keys are kept.  Heavily
+// clustered rows go through further levels that bin the survivors' keys over
+// their own range (each narrows it by 2^8).  Once at most 512 keys are left,
+// one warp bisects over their key bits with ballot counts.  A deterministic
+// compaction then emits every key above the threshold and the lowest-index
 // keys equal to it.  Rows longer than one CTA's shared-memory budget are cut
 // into chunks whose local top-k lists are merged by the same select
 // (dsa_topk_merge), which is also the cross-GPU merge of the sequence split.
@@ -20,68 +25,236 @@ namespace dsa {
 constexpr int kTopkThreads = 1024;
 constexpr int kTopkMaxN = 16384;   // elements one CTA selects from (64 KB keys + 64 KB idx)
 constexpr int kTopkMaxK = 4096;
+constexpr int kKeysPerThread = kTopkMaxN / kTopkThreads;  // 16
+// per-CTA scratch after keys and ids: the survivors of a level during the
+// select, then the (key, id) pairs of the optional descending sort
+constexpr int kScratchBytes = (kTopkMaxN * 4 > kTopkMaxK * 8) ? kTopkMaxN * 4 : kTopkMaxK * 8;
+constexpr uint32_t kNoBin = 0xffffffffu;
 
 struct SelectScratch {
   uint32_t hist[256];
   uint32_t prefix;
-  uint32_t kgt;        // elements strictly above the threshold found so far
+  uint32_t kgt;        // keys in bins above the chosen one
+  uint32_t ncand;
   uint32_t warp_cnt[2][32];
+  uint32_t part[32][4];
 };
 
-// Finds the threshold key of the k largest among keys[0, n) (k <= n).
-// Returns (threshold, n_above) in s->prefix / s->kgt.
-__device__ void radix_select(const uint32_t* keys, int n, int k, SelectScratch* s) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t prefix = 0, pmask = 0;
-  int krem = k;
-  int kgt = 0;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int i = tid; i < 256; i += blockDim.x) s->hist[i] = 0;
-    __syncthreads();
-    for (int base = 0; base < n; base += blockDim.x) {
-      const int i = base + tid;
-      uint32_t bin = 256;
-      if (i < n) {
-        const uint32_t key = keys[i];
-        if ((key & pmask) == prefix) bin = (key >> shift) & 255u;
-      }
-      const unsigned peers = __match_any_sync(0xffffffffu, bin);
-      if (bin < 256 && lane == __ffs(peers) - 1) atomicAdd(&s->hist[bin], (uint32_t)__popc(peers));
-    }
-    __syncthreads();
-    if (warp == 0) {
-      // lane l owns bins [8l, 8l+8); suffix counts from the top bin down
-      uint32_t h[8], tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        h[j] = s->hist[8 * lane + j];
-        tot += h[j];
-      }
-      uint32_t incl = tot;  // inclusive suffix sum over lanes >= l
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_down_sync(0xffffffffu, incl, o);
-        if (lane + o < 32) incl += v;
-      }
-      uint32_t run = incl - tot;  // count in bins above this lane's range
-#pragma unroll
-      for (int j = 7; j >= 0; --j) {
-        if (run < (uint32_t)krem && run + h[j] >= (uint32_t)krem) {
-          s->prefix = prefix | ((uint32_t)(8 * lane + j) << shift);
-          s->kgt = run;
-        }
-        run += h[j];
-      }
-    }
-    __syncthreads();
-    prefix = s->prefix;
-    pmask |= 0xffu << shift;
-    krem -= (int)s->kgt;
-    kgt += (int)s->kgt;
-    __syncthreads();
+// Block-wide min / max / sum of one value each per thread; every thread
+// receives the results.
+__device__ __forceinline__ void block_minmax_sum(uint32_t lo, uint32_t hi, uint32_t cnt, SelectScratch* s,
+                                                 uint32_t& mn, uint32_t& mx, uint32_t& sum) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  lo = __reduce_min_sync(0xffffffffu, lo);
+  hi = __reduce_max_sync(0xffffffffu, hi);
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  if (lane == 0) {
+    s->part[warp][0] = lo;
+    s->part[warp][1] = hi;
+    s->part[warp][2] = cnt;
   }
-  if (tid == 0) s->kgt = (uint32_t)kgt;
+  __syncthreads();
+  mn = __reduce_min_sync(0xffffffffu, lane < nw ? s->part[lane][0] : 0xffffffffu);
+  mx = __reduce_max_sync(0xffffffffu, lane < nw ? s->part[lane][1] : 0u);
+  sum = __reduce_add_sync(0xffffffffu, lane < nw ? s->part[lane][2] : 0u);
+  __syncthreads();
+}
+
+// Histogram of the live keys (bin_of(key) != kNoBin for index < nl) and the
+// bin holding the kl-th largest: s->prefix = bin, s->kgt = keys above it.
+// Lanes sharing lane 0's bin add with one atomic (clustered scores would
+// otherwise serialise on a few bins).
+template <class BinOf>
+__device__ __forceinline__ void hist_pick(const uint32_t (&r)[kKeysPerThread], int nj, int nl, int kl, BinOf bin_of,
+                                          SelectScratch* s) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 256; i += blockDim.x) s->hist[i] = 0;
+  if (tid == 0) s->ncand = 0;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= nj) break;  // uniform across the block
+    const uint32_t bin = tid + j * kTopkThreads < nl ? bin_of(r[j]) : kNoBin;
+    const uint32_t lead = __shfl_sync(0xffffffffu, bin, 0);
+    const unsigned same = __ballot_sync(0xffffffffu, bin == lead);
+    if (bin == lead) {
+      if (lane == __ffs(same) - 1 && lead != kNoBin) atomicAdd(&s->hist[lead], (uint32_t)__popc(same));
+    } else if (bin != kNoBin) {
+      atomicAdd(&s->hist[bin], 1u);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // lane l owns bins [8l, 8l+8); find the bin of the kl-th largest from the top
+    uint32_t h[8], tot = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      h[j] = s->hist[8 * lane + j];
+      tot += h[j];
+    }
+    uint32_t incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_down_sync(0xffffffffu, incl, o);
+      if (lane + o < 32) incl += v;
+    }
+    uint32_t run = incl - tot;
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+      if (run < (uint32_t)kl && run + h[j] >= (uint32_t)kl) {
+        s->prefix = (uint32_t)(8 * lane + j);
+        s->kgt = run;
+      }
+      run += h[j];
+    }
+  }
+  __syncthreads();
+}
+
+// Copies the live keys of bin `bin` to cand (one atomic per warp and key slot;
+// their order is irrelevant, only the threshold value is sought) and returns
+// how many there are.
+template <class BinOf>
+__device__ __forceinline__ int gather_bin(const uint32_t (&r)[kKeysPerThread], int nj, int nl, uint32_t bin,
+                                          BinOf bin_of, uint32_t* cand, SelectScratch* s) {
+  const int tid = threadIdx.x, lane = tid & 31;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= nj) break;
+    const bool hit = tid + j * kTopkThreads < nl && bin_of(r[j]) == bin;
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    if (m) {
+      uint32_t o = 0;
+      if (lane == 0) o = atomicAdd(&s->ncand, (uint32_t)__popc(m));
+      o = __shfl_sync(0xffffffffu, o, 0);
+      if (hit) cand[o + __popc(m & ((1u << lane) - 1u))] = r[j];
+    }
+  }
+  __syncthreads();
+  return (int)s->ncand;
+}
+
+// Finds the k-th largest of keys[0, n) (1 <= k <= n <= kTopkMaxN, blockDim.x
+// == kTopkThreads) and leaves it in s->prefix.  `cand` holds up to n keys.
+__device__ void kth_key_select(const uint32_t* keys, int n, int k, SelectScratch* s, uint32_t* cand) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int nj = (n + kTopkThreads - 1) / kTopkThreads;
+  uint32_t r[kKeysPerThread];
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    const int i = tid + j * kTopkThreads;
+    r[j] = i < n ? keys[i] : 0u;
+  }
+  // level 0 over the keys above the floor (the key of -inf: masked positions
+  // and padding sit at or below it), binned by score value
+  const uint32_t kfloor = float_key(-INFINITY);
+  uint32_t lo = 0xffffffffu, hi = 0u, cnt = 0;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= nj) break;
+    if (tid + j * kTopkThreads < n && r[j] > kfloor) {
+      ++cnt;
+      lo = min(lo, r[j]);
+      hi = max(hi, r[j]);
+    }
+  }
+  uint32_t mn, mx, n_live;
+  block_minmax_sum(lo, hi, cnt, s, mn, mx, n_live);
+  int nl = n, kl = k, nc = -1;
+  uint32_t thr = 0;
+  bool done = false;
+  if (n_live >= (uint32_t)k) {
+    const float vmin = key_float(mn), vmax = key_float(mx);
+    if (mx == mn) {
+      thr = mn;  // every live key is equal
+      done = true;
+    } else if (isfinite(vmin) && isfinite(vmax)) {
+      const float scale = 255.99f / (vmax - vmin);
+      auto vbin = [&](uint32_t key) -> uint32_t {
+        if (key <= kfloor) return kNoBin;
+        return min((uint32_t)((key_float(key) - vmin) * scale), 255u);
+      };
+      hist_pick(r, nj, nl, kl, vbin, s);
+      const uint32_t bin = s->prefix;
+      kl -= (int)s->kgt;
+      nc = gather_bin(r, nj, nl, bin, vbin, cand, s);
+    }
+  }
+  // otherwise (threshold at or below the floor, or non-finite scores) the
+  // key levels below start from all keys
+  for (int level = 0; level < 6 && !done; ++level) {
+    if (nc >= 0) {
+#pragma unroll
+      for (int j = 0; j < kKeysPerThread; ++j) {
+        const int i = tid + j * kTopkThreads;
+        r[j] = i < nc ? cand[i] : 0u;
+      }
+      nl = nc;
+      nj = (nc + kTopkThreads - 1) / kTopkThreads;
+    }
+    lo = 0xffffffffu;
+    hi = 0u;
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      if (j >= nj) break;
+      if (tid + j * kTopkThreads < nl) {
+        lo = min(lo, r[j]);
+        hi = max(hi, r[j]);
+      }
+    }
+    block_minmax_sum(lo, hi, 0u, s, mn, mx, cnt);  // also orders the reload before cand is rewritten
+    const uint32_t range = mx - mn;
+    if (range == 0) {
+      thr = mn;
+      break;
+    }
+    if (nl <= 32 * kKeysPerThread) {
+      // few keys left: warp 0 bisects over their offsets above mn, two bits
+      // per pass, counting with ballots (no block barrier per pass)
+      if (warp == 0) {
+        uint32_t c[kKeysPerThread];
+#pragma unroll
+        for (int j = 0; j < kKeysPerThread; ++j) {
+          const int i = lane + 32 * j;
+          c[j] = i < nl ? (nc >= 0 ? cand[i] : keys[i]) - mn : 0u;
+        }
+        const int ncj = (nl + 31) / 32;
+        uint32_t pre = 0;
+        for (int b2 = (32 - __clz(range) + 1) & ~1; b2 > 0; b2 -= 2) {
+          const int sh = b2 - 2;
+          const uint32_t p1 = pre | (1u << sh), p2 = pre | (2u << sh), p3 = pre | (3u << sh);
+          uint32_t t1 = 0, t2 = 0, t3 = 0;
+#pragma unroll
+          for (int j = 0; j < kKeysPerThread; ++j) {
+            if (j >= ncj) break;
+            const bool ok = lane + 32 * j < nl;
+            t1 += __popc(__ballot_sync(0xffffffffu, ok && c[j] >= p1));
+            t2 += __popc(__ballot_sync(0xffffffffu, ok && c[j] >= p2));
+            t3 += __popc(__ballot_sync(0xffffffffu, ok && c[j] >= p3));
+          }
+          pre = t3 >= (uint32_t)kl ? p3 : t2 >= (uint32_t)kl ? p2 : t1 >= (uint32_t)kl ? p1 : pre;
+        }
+        if (lane == 0) s->prefix = mn + pre;
+      }
+      __syncthreads();
+      thr = s->prefix;
+      break;
+    }
+    // key level: 256 bins over [mn, mx], each narrowing the range by 2^8
+    const int shift = range < 256u ? 0 : 32 - __clz(range) - 8;
+    const uint32_t mn0 = mn;
+    auto kbin = [&](uint32_t key) -> uint32_t { return (key - mn0) >> shift; };
+    hist_pick(r, nj, nl, kl, kbin, s);
+    const uint32_t bin = s->prefix;
+    kl -= (int)s->kgt;
+    if (shift == 0) {
+      thr = mn0 + bin;
+      break;
+    }
+    nc = gather_bin(r, nj, nl, bin, kbin, cand, s);
+  }
+  __syncthreads();
+  if (tid == 0) s->prefix = thr;
   __syncthreads();
 }
 
@@ -155,13 +328,14 @@ __device__ void bitonic_desc(uint64_t* v, int n_pow2) {
 // Selects the k best of (keys[i], ids[i]) for i < n and writes them out.
 // mode_final: out index = id + win when the masked score >= -1000, else -1;
 // otherwise the raw id is written (intermediate candidate lists).
+// `scratch` (kScratchBytes) holds a level's survivors during the select and the
+// (key, id) pairs of the optional descending sort afterwards.
 __device__ void select_and_emit(uint32_t* keys, const int32_t* ids, int n, int k, bool sort_desc, bool mode_final,
-                                int win, int32_t* out_idx, float* out_score, uint64_t* sort_buf,
+                                int win, int32_t* out_idx, float* out_score, uint8_t* scratch,
                                 SelectScratch* s) {
-  radix_select(keys, n, k, s);
+  kth_key_select(keys, n, k, s, reinterpret_cast<uint32_t*>(scratch));
+  uint64_t* sort_buf = reinterpret_cast<uint64_t*>(scratch);
   const uint32_t thr = s->prefix;
-  const int n_above = (int)s->kgt;
-  const int n_eq_take = k - n_above;
   // contiguous per-thread ranges keep the output in ascending position order
   const int per = (n + blockDim.x - 1) / blockDim.x;
   const int i0 = threadIdx.x * per, i1 = min(n, i0 + per);
@@ -173,8 +347,9 @@ __device__ void select_and_emit(uint32_t* keys, const int32_t* ids, int n, int k
   }
   uint32_t oa, oe, ta, te;
   block_scan2(ca, ce, oa, oe, s, ta, te);
-  (void)ta;
   (void)te;
+  const int n_above = (int)ta;  // < k by the choice of thr
+  const int n_eq_take = k - n_above;
   for (int i = i0; i < i1; ++i) {
     const uint32_t key = keys[i];
     int slot = -1;
@@ -225,32 +400,38 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ SelectScratch s;
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
-  uint64_t* sort_buf = reinterpret_cast<uint64_t*>(smem + kTopkMaxN * 4);
+  int32_t* ids = reinterpret_cast<int32_t*>(smem + kTopkMaxN * 4);
+  uint8_t* scratch = smem + kTopkMaxN * 8;
   const int b = blockIdx.y, c = blockIdx.x, n_chunks = gridDim.x;
   const int t0 = c * chunk;
   const int n = min(T, t0 + chunk) - t0;
   const int ta = t_active[b];
   const float* row = score + int64_t(b) * ld_score + t0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float m;
-    if (t0 + i < ta) m = row[i];
-    else m = mask_mode ? -INFINITY : __fsub_rn(row[i], 1.0e4f);
-    keys[i] = float_key(m);
+  // every load of a thread in flight before any use (n <= 16 x 1024)
+  float v[kKeysPerThread];
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    const int i = threadIdx.x + j * kTopkThreads;
+    v[j] = i < n ? __ldg(row + i) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    const int i = threadIdx.x + j * kTopkThreads;
+    if (i < n) keys[i] = float_key((t0 + i < ta) ? v[j] : (mask_mode ? -INFINITY : __fsub_rn(v[j], 1.0e4f)));
   }
   __syncthreads();
   if (n_chunks == 1) {
     select_and_emit(keys, nullptr, n, k, sort_desc != 0, true, win, out_idx + int64_t(b) * ld_out,
-                    out_score ? out_score + int64_t(b) * ld_out : nullptr, sort_buf, &s);
+                    out_score ? out_score + int64_t(b) * ld_out : nullptr, scratch, &s);
     return;
   }
   // intermediate: ids are global positions
   const int kk = min(k, n);
-  int32_t* ids = reinterpret_cast<int32_t*>(smem + kTopkMaxN * 4);
   for (int i = threadIdx.x; i < n; i += blockDim.x) ids[i] = t0 + i;
   __syncthreads();
   const int64_t base = (int64_t(b) * n_chunks + c) * k;
   // write keys of the selected candidates: emit ids into cand_id, then keys
-  select_and_emit(keys, ids, n, kk, false, false, 0, cand_id + base, nullptr, nullptr, &s);
+  select_and_emit(keys, ids, n, kk, false, false, 0, cand_id + base, nullptr, scratch, &s);
   __syncthreads();
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     if (i < kk) {
@@ -273,7 +454,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(
   __shared__ SelectScratch s;
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
   int32_t* ids = reinterpret_cast<int32_t*>(smem + kTopkMaxN * 4);
-  uint64_t* sort_buf = reinterpret_cast<uint64_t*>(smem + kTopkMaxN * 8);
+  uint8_t* scratch = smem + kTopkMaxN * 8;
   const int b = blockIdx.x;
   for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
     const int32_t id = cand_id[int64_t(b) * n_cand + i];
@@ -285,7 +466,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(
   }
   __syncthreads();
   select_and_emit(keys, ids, n_cand, k, sort_desc != 0, final_mode != 0, win, out_idx + int64_t(b) * ld_out,
-                  out_score ? out_score + int64_t(b) * ld_out : nullptr, sort_buf, &s);
+                  out_score ? out_score + int64_t(b) * ld_out : nullptr, scratch, &s);
 }
 
 __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ idx, int64_t ld,
@@ -305,8 +486,9 @@ __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* 
 using namespace dsa;
 
 namespace {
-int chunk_smem() { return kTopkMaxN * 4 + std::max(kTopkMaxN * 4, kTopkMaxK * 8); }
-int merge_smem() { return kTopkMaxN * 8 + kTopkMaxK * 8; }
+// keys | ids | scratch
+int chunk_smem() { return kTopkMaxN * 8 + kScratchBytes; }
+int merge_smem() { return kTopkMaxN * 8 + kScratchBytes; }
 }  // namespace
 
 extern "C" int dsa_window_indices(const int32_t* pos, int32_t* idx, int64_t ld_idx, int B, int win,
