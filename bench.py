@@ -405,26 +405,29 @@ def main():
 def measure_e2e(args, path, inputs, outs, dev, world):
     """Same metric through the public API with HOST buffers: every step copies
     all 43 layers' inputs from pinned host memory and reads all outputs back.
-    Copies run on side streams, pipelined against the previous step's graph
-    (two input/output buffer sets, one captured graph each)."""
+    Inputs and outputs of the whole step are packed (LayerInputs.packed, one
+    flat output tensor) so each direction is one copy per step; the copies run
+    on side streams, pipelined against the previous step's graph (two
+    input/output buffer sets, one captured graph each)."""
     import torch
     from dsv4attn.layer import LayerInputs
     B, nl = args.batch, args.layers
-    host_in = []
-    for x in inputs:
-        h = LayerInputs.empty(path.args, B, dev, pin=True)
+    host_flat, host_in = LayerInputs.packed(path.args, B, nl, pin=True)
+    for h, x in zip(host_in, inputs):
         for a, b in zip(h.tensors(), x.tensors()):
             a.copy_(b)
-        host_in.append(h)
-    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
-    sets = [(inputs, outs)]
-    in2 = [LayerInputs(*[t.clone() for t in x.tensors()]) for x in inputs]
-    out2 = [torch.empty_like(o) for o in outs]
-    sets.append((in2, out2))
-    graphs = [path.graph]
-    path.graph = None
-    graphs.append(path.capture(in2, out2, warmup=0))
-    path.graph = graphs[0]
+    out_shape = (nl,) + tuple(outs[0].shape)
+    host_out = torch.empty(out_shape, dtype=outs[0].dtype, pin_memory=True)
+    sets, graphs = [], []
+    saved = path.graph
+    for _ in range(2):
+        dflat, dins = LayerInputs.packed(path.args, B, nl, device=dev)
+        dflat.copy_(host_flat)
+        dout = torch.empty(out_shape, dtype=outs[0].dtype, device=dev)
+        sets.append((dflat, dout))
+        path.graph = None
+        graphs.append(path.capture(dins, list(dout.unbind(0)), warmup=0))
+    path.graph = saved
     path.set_positions(args.ctx - 1)
     torch.cuda.synchronize()
     comp = torch.cuda.current_stream()
@@ -433,17 +436,16 @@ def measure_e2e(args, path, inputs, outs, dev, world):
     in_ready = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
     out_free = [torch.cuda.Event() for _ in range(2)]
-    h2d_bytes = sum(x.nbytes() for x in host_in)
-    d2h_bytes = sum(o.numel() * o.element_size() for o in outs)
+    h2d_bytes = host_flat.numel()
+    d2h_bytes = host_out.numel() * host_out.element_size()
 
     def issue(step):
         s = step & 1
-        ins, os_ = sets[s]
+        dflat, dout = sets[s]
         with torch.cuda.stream(h2d):
             if step >= 2:
                 h2d.wait_event(done[s])          # graph of step-2 finished reading this set
-            for d, h in zip(ins, host_in):
-                d.copy_(h, non_blocking=True)
+            dflat.copy_(host_flat, non_blocking=True)
             in_ready[s].record(h2d)
         comp.wait_event(in_ready[s])
         if step >= 2:
@@ -452,8 +454,7 @@ def measure_e2e(args, path, inputs, outs, dev, world):
         done[s].record(comp)
         with torch.cuda.stream(d2h):
             d2h.wait_event(done[s])
-            for h, o in zip(host_out, os_):
-                h.copy_(o, non_blocking=True)
+            host_out.copy_(dout, non_blocking=True)
             out_free[s].record(d2h)
 
     for i in range(3):

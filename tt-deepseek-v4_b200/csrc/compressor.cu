@@ -36,6 +36,56 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
+// Softmax over the slot axis of the (overlap) view and the weighted sum for
+// this thread's columns; returns the thread's sum of squares.  With NS > 0
+// the slot count is a compile-time constant, so each column's NS scores and
+// values are loaded together instead of as a chain of dependent loads.
+template <int NS>
+__device__ __forceinline__ float emit_columns(const float* kvs, const float* scs, float* s_row, int d, int cd,
+                                              int ratio, int overlap, int nslots_rt = 0) {
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float v;
+    if constexpr (NS > 0) {
+      float sc[NS], kv[NS];
+#pragma unroll
+      for (int i = 0; i < NS; ++i) {
+        const int col = (overlap && i >= ratio) ? d + c : c;
+        sc[i] = scs[int64_t(i) * cd + col];
+        kv[i] = kvs[int64_t(i) * cd + col];
+      }
+      float m = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < NS; ++i) m = fmaxf(m, sc[i]);
+      float den = 0.f, num = 0.f;
+#pragma unroll
+      for (int i = 0; i < NS; ++i) {
+        const float e = expf(sc[i] - m);
+        den += e;
+        num = fmaf(e, kv[i], num);
+      }
+      v = __fdiv_rn(num, den);
+    } else {
+      float m = -INFINITY;
+      for (int i = 0; i < nslots_rt; ++i) {
+        const int col = (overlap && i >= ratio) ? d + c : c;
+        m = fmaxf(m, scs[int64_t(i) * cd + col]);
+      }
+      float den = 0.f, num = 0.f;
+      for (int i = 0; i < nslots_rt; ++i) {
+        const int col = (overlap && i >= ratio) ? d + c : c;
+        const float e = expf(scs[int64_t(i) * cd + col] - m);
+        den += e;
+        num = fmaf(e, kvs[int64_t(i) * cd + col], num);
+      }
+      v = __fdiv_rn(num, den);
+    }
+    s_row[c] = v;
+    ss = fmaf(v, v, ss);
+  }
+  return ss;
+}
+
 __global__ void __launch_bounds__(kCmpThreads) compressor_step_kernel(
     const __nv_bfloat16* __restrict__ kv_row, const __nv_bfloat16* __restrict__ score_row, int64_t ld_row,
     const float* __restrict__ ape, float* __restrict__ kv_state, float* __restrict__ score_state,
@@ -76,23 +126,9 @@ __global__ void __launch_bounds__(kCmpThreads) compressor_step_kernel(
 
   // ---- softmax over the slot axis of the (overlap) view, weighted sum
   float ss = 0.f;
-  for (int c = tid; c < d; c += blockDim.x) {
-    float m = -INFINITY;
-    for (int i = 0; i < nslots; ++i) {
-      const int col = (overlap && i >= ratio) ? d + c : c;
-      m = fmaxf(m, scs[int64_t(i) * cd + col]);
-    }
-    float den = 0.f, num = 0.f;
-    for (int i = 0; i < nslots; ++i) {
-      const int col = (overlap && i >= ratio) ? d + c : c;
-      const float e = expf(scs[int64_t(i) * cd + col] - m);
-      den += e;
-      num = fmaf(e, kvs[int64_t(i) * cd + col], num);
-    }
-    const float v = __fdiv_rn(num, den);
-    s_row[c] = v;
-    ss = fmaf(v, v, ss);
-  }
+  if (nslots == 8) ss = emit_columns<8>(kvs, scs, s_row, d, cd, ratio, overlap);
+  else if (nslots == 4) ss = emit_columns<4>(kvs, scs, s_row, d, cd, ratio, overlap);
+  else ss = emit_columns<0>(kvs, scs, s_row, d, cd, ratio, overlap, nslots);
   const float tot = block_sum(ss, s_red);
   const float rms = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, float(d)), eps)));
 
@@ -134,12 +170,31 @@ __global__ void __launch_bounds__(kCmpThreads) compressor_step_kernel(
   __nv_bfloat16* dst = cache + int64_t(b) * cache_bstride + out_row * d;
   for (int c = tid; c < d; c += blockDim.x) dst[c] = f2bf(s_row[c]);
 
-  // ---- slot shift (overlap): rows [0, r) <- rows [r, 2r)
+  // ---- slot shift (overlap): rows [0, r) <- rows [r, 2r), staged through
+  // registers 8 elements per thread and array at a time so the loads of a
+  // batch are all in flight before its stores
   if (overlap) {
     __syncthreads();
-    for (int e = tid; e < ratio * cd; e += blockDim.x) {
-      kvs[e] = kvs[int64_t(ratio) * cd + e];
-      scs[e] = scs[int64_t(ratio) * cd + e];
+    constexpr int kBatch = 8;
+    const int n = ratio * cd;
+    for (int e0 = 0; e0 < n; e0 += kBatch * kCmpThreads) {
+      float a[kBatch], c[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int e = e0 + j * kCmpThreads + tid;
+        if (e < n) {
+          a[j] = kvs[int64_t(ratio) * cd + e];
+          c[j] = scs[int64_t(ratio) * cd + e];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int e = e0 + j * kCmpThreads + tid;
+        if (e < n) {
+          kvs[e] = a[j];
+          scs[e] = c[j];
+        }
+      }
     }
   }
 }

@@ -274,42 +274,72 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_mma_kernel(SaArgs a
 
 // grid (M, H); 128 threads x 4 dims.  final: o = sum_p o_p e^{m_p-M} / L with
 // the sink in L; partial: (M, L, sum_p o_p e^{m_p-M}) without the sink.
-__global__ void __launch_bounds__(128) lse_combine_kernel(const float* __restrict__ part_ml,
-                                                          const float* __restrict__ part_o,
-                                                          const float* __restrict__ sink, int P, int M, int H, int D,
-                                                          int final_mode, __nv_bfloat16* __restrict__ out,
-                                                          float* __restrict__ lse, float* __restrict__ out_ml,
-                                                          float* __restrict__ out_o) {
-  const int m = blockIdx.x, h = blockIdx.y;
+// One warp per (query row, head): the split statistics are reduced across
+// lanes (any number of splits), then lane l combines output dims
+// [16 l, 16 l + 16) of every split with all of a split's loads in flight.
+constexpr int kCombineWarps = 8;
+__global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
+    const float* __restrict__ part_ml, const float* __restrict__ part_o, const float* __restrict__ sink, int P, int M,
+    int H, int D, int final_mode, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, float* __restrict__ out_ml,
+    float* __restrict__ out_o) {
+  const int m = blockIdx.x, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * kCombineWarps + (threadIdx.x >> 5);
+  if (h >= H) return;
+  auto ml = [&](int p, int j) { return part_ml[((int64_t(p) * M + m) * H + h) * 2 + j]; };
   float Mx = final_mode ? sink[h] : -INFINITY;
-  for (int p = 0; p < P; ++p) Mx = fmaxf(Mx, part_ml[((int64_t(p) * M + m) * H + h) * 2]);
-  float L = (final_mode && Mx != -INFINITY) ? expf(sink[h] - Mx) : 0.f;
+  for (int p0 = 0; p0 < P; p0 += 32) {
+    const float mp = p0 + lane < P ? ml(p0 + lane, 0) : -INFINITY;
+    Mx = fmaxf(Mx, warp_max(mp));
+  }
+  float lsum = 0.f;
+  for (int p0 = 0; p0 < P; p0 += 32) {
+    if (p0 + lane < P) {
+      const float mp = ml(p0 + lane, 0);
+      if (mp != -INFINITY) lsum += ml(p0 + lane, 1) * expf(mp - Mx);
+    }
+  }
+  float L = warp_sum(lsum);
+  if (final_mode && Mx != -INFINITY) L += expf(sink[h] - Mx);
+  const int d0 = 16 * lane;  // D = 512: 16 dims per lane
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
   for (int p = 0; p < P; ++p) {
-    const float mp = part_ml[((int64_t(p) * M + m) * H + h) * 2];
-    if (mp != -INFINITY) L += part_ml[((int64_t(p) * M + m) * H + h) * 2 + 1] * expf(mp - Mx);
+    const float mp = ml(p, 0);
+    if (mp == -INFINITY) continue;
+    const float w = expf(mp - Mx);
+    const float4* src = reinterpret_cast<const float4*>(part_o + ((int64_t(p) * M + m) * H + h) * D + d0);
+    const float4 v0 = __ldg(src), v1 = __ldg(src + 1), v2 = __ldg(src + 2), v3 = __ldg(src + 3);
+    acc[0] = fmaf(w, v0.x, acc[0]);
+    acc[1] = fmaf(w, v0.y, acc[1]);
+    acc[2] = fmaf(w, v0.z, acc[2]);
+    acc[3] = fmaf(w, v0.w, acc[3]);
+    acc[4] = fmaf(w, v1.x, acc[4]);
+    acc[5] = fmaf(w, v1.y, acc[5]);
+    acc[6] = fmaf(w, v1.z, acc[6]);
+    acc[7] = fmaf(w, v1.w, acc[7]);
+    acc[8] = fmaf(w, v2.x, acc[8]);
+    acc[9] = fmaf(w, v2.y, acc[9]);
+    acc[10] = fmaf(w, v2.z, acc[10]);
+    acc[11] = fmaf(w, v2.w, acc[11]);
+    acc[12] = fmaf(w, v3.x, acc[12]);
+    acc[13] = fmaf(w, v3.y, acc[13]);
+    acc[14] = fmaf(w, v3.z, acc[14]);
+    acc[15] = fmaf(w, v3.w, acc[15]);
   }
-  for (int d = threadIdx.x * 4; d < D; d += blockDim.x * 4) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < P; ++p) {
-      const float mp = part_ml[((int64_t(p) * M + m) * H + h) * 2];
-      if (mp == -INFINITY) continue;
-      const float w = expf(mp - Mx);
-      const float4 v = *reinterpret_cast<const float4*>(part_o + ((int64_t(p) * M + m) * H + h) * D + d);
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    }
-    if (final_mode) {
-      const float inv = 1.f / L;
-      __nv_bfloat16* op = out + (int64_t(m) * H + h) * D + d;
-      *reinterpret_cast<uint32_t*>(op) = pack_bf16x2(acc.x * inv, acc.y * inv);
-      *reinterpret_cast<uint32_t*>(op + 2) = pack_bf16x2(acc.z * inv, acc.w * inv);
-    } else {
-      *reinterpret_cast<float4*>(out_o + (int64_t(m) * H + h) * D + d) = acc;
-    }
+  if (final_mode) {
+    const float inv = 1.f / L;
+    uint4* op = reinterpret_cast<uint4*>(out + (int64_t(m) * H + h) * D + d0);
+    op[0] = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                       pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
+    op[1] = make_uint4(pack_bf16x2(acc[8] * inv, acc[9] * inv), pack_bf16x2(acc[10] * inv, acc[11] * inv),
+                       pack_bf16x2(acc[12] * inv, acc[13] * inv), pack_bf16x2(acc[14] * inv, acc[15] * inv));
+  } else {
+    float4* op = reinterpret_cast<float4*>(out_o + (int64_t(m) * H + h) * D + d0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) op[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
   }
-  if (threadIdx.x == 0) {
+  if (lane == 0) {
     if (final_mode) {
       if (lse) lse[int64_t(m) * H + h] = Mx + logf(L);
     } else {
@@ -397,6 +427,9 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   if (M == 0) return DSA_OK;
   ensure_attr();
   const SplitPlan p = plan_splits(M, K);
+  // the split-K combine writes 16-byte vectors
+  DSA_CHECK_ARG(p.nsplit <= 1 || (final_mode ? aligned(out, 16) : aligned(part_o_out, 16)),
+                "sparse_attn: out / part_o must be 16-byte aligned");
   SaArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.kv = static_cast<const __nv_bfloat16*>(kv);
@@ -467,7 +500,8 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   }
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {
-    lse_combine_kernel<<<dim3(M, kSaH), 128, 0, st>>>(ws_ml, ws_o, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
+    lse_combine_kernel<<<dim3(M, kSaH / kCombineWarps), 32 * kCombineWarps, 0, st>>>(
+        ws_ml, ws_o, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
                                                       static_cast<__nv_bfloat16*>(out), lse, part_ml_out,
                                                       part_o_out);
     DSA_CHECK_LAUNCH("sparse_attn(combine)");
@@ -500,10 +534,12 @@ extern "C" int dsa_lse_combine(const float* part_ml, const float* part_o, const 
                                int H, int D, dsa_stream_t stream) {
   clear_error();
   DSA_CHECK_ARG(part_ml && part_o && sink && out, "lse_combine: null pointer");
-  DSA_CHECK_ARG(P > 0 && M >= 0 && H > 0 && D > 0 && D % 4 == 0, "lse_combine: bad P/M/H/D");
-  DSA_CHECK_ARG(aligned(part_o, 16) && aligned(out, 4), "lse_combine: misaligned buffers");
+  DSA_CHECK_ARG(P > 0 && M >= 0 && H > 0, "lse_combine: bad P/M/H");
+  DSA_CHECK_ARG(D == kSaD, "lse_combine: built for D=%d (got %d)", kSaD, D);
+  DSA_CHECK_ARG(aligned(part_o, 16) && aligned(out, 16), "lse_combine: part_o / out must be 16-byte aligned");
   if (M == 0) return DSA_OK;
-  lse_combine_kernel<<<dim3(M, H), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  lse_combine_kernel<<<dim3(M, (H + kCombineWarps - 1) / kCombineWarps), 32 * kCombineWarps, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(
       part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr, nullptr);
   DSA_CHECK_LAUNCH("lse_combine");
   return DSA_OK;

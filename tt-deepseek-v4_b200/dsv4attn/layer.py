@@ -76,6 +76,42 @@ class LayerInputs:
             icmp_score=torch.empty(B, 2 * Di, dtype=BF16, **kw),
             iw=torch.empty(B, args.index_n_heads, dtype=F32, **kw))
 
+    @staticmethod
+    def shapes(args: PathArgs, B: int):
+        """(shape, dtype) of each input tensor, in field order."""
+        D, Di, H, Hi = args.head_dim, args.index_head_dim, args.n_heads, args.index_n_heads
+        return [((B, H, D), BF16), ((B, D), BF16), ((B, 2 * D), BF16), ((B, 2 * D), BF16),
+                ((B, Hi, Di), BF16), ((B, 2 * Di), BF16), ((B, 2 * Di), BF16), ((B, Hi), F32)]
+
+    @staticmethod
+    def packed(args: PathArgs, B: int, n_layers: int, device=None, pin: bool = False):
+        """Inputs of n_layers layers as views of ONE flat byte buffer (so a
+        host->device refresh of a whole step is a single copy).  Returns
+        (flat uint8 tensor, [LayerInputs] views)."""
+        sh = LayerInputs.shapes(args, B)
+        sizes = []
+        for shape, dt in sh:
+            n = 1
+            for x in shape:
+                n *= x
+            sizes.append(-(-n * torch.tensor([], dtype=dt).element_size() // 256) * 256)
+        per_layer = sum(sizes)
+        kw = dict(pin_memory=True) if pin else dict(device=device)
+        flat = torch.empty(n_layers * per_layer, dtype=torch.uint8, **kw)
+        layers = []
+        for li in range(n_layers):
+            off = li * per_layer
+            ts = []
+            for (shape, dt), nb in zip(sh, sizes):
+                esz = torch.tensor([], dtype=dt).element_size()
+                n = 1
+                for x in shape:
+                    n *= x
+                ts.append(flat[off:off + n * esz].view(dt).view(shape))
+                off += nb
+            layers.append(LayerInputs(*ts))
+        return flat, layers
+
     def tensors(self):
         return [self.q, self.kv, self.cmp_kv, self.cmp_score, self.iq, self.icmp_kv, self.icmp_score, self.iw]
 
