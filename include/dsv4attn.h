@@ -67,6 +67,48 @@ int dsa_kv_window_write(const void* kv, void* kv_cache, float* scales,
                         int64_t cache_bstride, int win, int block,
                         dsa_stream_t stream);
 
+/* The whole Lk-D1 zone plus attn.kv_update in one launch, for B sequences:
+ * kv [B, D] bf16 (the wkv output, row stride ld_kv) -> RMSNorm(gamma, eps)
+ * rounded to bf16 -> interleaved rotary of the last rope_dim dims with row
+ * pos[b] of cos/sin [n_pos, rope_dim/2] fp32 -> act_quant_block (block 64,
+ * e4m3, fp8_max 448, eps 1e-4) on the first D - rope_dim dims -> ring write
+ * kv_cache[b, pos[b] % win]; also stored to kv_out [B, D] when non-NULL.
+ * D and rope_dim multiples of 64, D <= 2048.  A position outside the table
+ * is clamped and flags *status (may be NULL).
+ * Replaces _lk_d1_kernel(kv, cos_full, sin_full, start_pos, kv_out)
+ *   inference.py:5997-6006 (kv_norm + rotary + act_quant) followed by the
+ *   paged_update_cache of attn.kv_update, inference.py:6072-6079. */
+int dsa_kv_norm_rope_window_write(const void* kv, int64_t ld_kv, const float* gamma,
+                                  float eps, const float* cos_tab, const float* sin_tab,
+                                  int n_pos, const int32_t* pos, void* kv_cache,
+                                  int64_t cache_bstride, int win, void* kv_out,
+                                  int64_t ld_out, float* scales, int B, int D,
+                                  int rope_dim, int32_t* status, dsa_stream_t stream);
+
+/* Per-head RMSNorm and/or interleaved rotary of x [B, H*Dh] bf16 (row
+ * stride ld_x) into out (may alias x).  do_norm: y = w * x * rsqrt(mean(x^2)
+ * + eps) with w = gamma[Dh] fp32, or the scalar `weight` when gamma is NULL,
+ * rounded to bf16 (the reference RMSNorm returns the input dtype).  Then,
+ * when rope_dim > 0, the last rope_dim dims of each head are rotated with
+ * row pos[b] of cos/sin (inverse != 0: by the conjugate).
+ * Replaces the q path rms_norm(q, q_rsqrt_ones) + _lk_c_q_rotary_kernel
+ *   inference.py:5982-5993, the q_norm rms_norm inference.py:6032-6034, the
+ *   indexer q rotary of _lk_d_idx_q_kernel inference.py:5242, and the
+ *   inverse rotary _lk_o_rotary_kernel inference.py:6100-6102. */
+int dsa_head_norm_rope(const void* x, int64_t ld_x, void* out, int64_t ld_out,
+                       int B, int H, int Dh, int rope_dim, const float* gamma,
+                       float weight, int do_norm, float eps, const float* cos_tab,
+                       const float* sin_tab, int n_pos, const int32_t* pos,
+                       int inverse, int32_t* status, dsa_stream_t stream);
+
+/* out[i] = (valid[i] < 0 ? -1 : idx[i]) for i < n: folds the additive
+ * {0, -inf} bf16 mask of the reference's (indices, mask) pair back into -1
+ * sentinels, which is what dsa_sparse_attn reads.
+ * Inverse of DeviceSparseAttn._idxs_int_tile_to_idxs_and_mask
+ *   inference.py:4444-4457. */
+int dsa_fold_index_mask(const int32_t* idx, const void* valid, int64_t n,
+                        int32_t* out, dsa_stream_t stream);
+
 /* ---------------------------------------------------------- attn.compress */
 
 /* One compressor decode step for B sequences (one kernel):

@@ -29,7 +29,8 @@ __all__ = [
     "compressor_init_state", "compressor_state_write", "compressor_emit",
     "compressor_step", "shift_matrix_apply", "indexer_score", "indexer_topk",
     "sparse_attn", "sparse_attn_partial", "lse_combine", "topk_merge",
-    "hadamard_rotate", "LayerState", "decode_layer_step",
+    "hadamard_rotate", "LayerState", "decode_layer_step", "linear_bf16",
+    "head_norm_rope", "kv_norm_rope_quant", "BlockWeights", "attention_decode_block",
 ]
 
 FP8_MAX = 448.0
@@ -416,3 +417,99 @@ def decode_layer_step(st: LayerState, pos: int, q, kv_row, cmp_kv_row, cmp_sc_ro
                     st.cos, st.sin, pos, r, True, kv_cache=st.kv_cache, slot_offset=W)
     o = sparse_attn(q, st.kv_cache, idx, st.sink, st.scale)
     return o, idx
+
+
+# --------------------------------------------------------------------------
+# around the path: q path, Lk-D1 kv path, output side, the whole block
+# --------------------------------------------------------------------------
+
+def linear_bf16(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """bf16 projection with fp32 accumulation, rounded to bf16 (the device
+    matmuls of inference.py:5934-5960; the CPU Linear is F.linear, 390-396)."""
+    return (x.to(torch.bfloat16).float() @ w.to(torch.bfloat16).float().t()).to(torch.bfloat16)
+
+
+def head_norm_rope(x: torch.Tensor, n_heads: int, head_dim: int, cos_row=None, sin_row=None,
+                   rope_dim: int = 0, gamma=None, weight: float = 1.0, norm: bool = True,
+                   eps: float = 1e-6, inverse: bool = False) -> torch.Tensor:
+    """Per-head RMSNorm (result rounded to bf16 as RMSNorm returns the input
+    dtype, inference.py:436-450) with weight ``gamma`` or the scalar
+    ``weight`` (q_rsqrt_ones = softmax_scale, 5348-5350, 5982-5983), then
+    interleaved rotary of the last ``rope_dim`` dims (5990; inverse for the
+    output side, 6102).  x [B, n_heads*head_dim] -> bf16 same shape.
+    cos_row/sin_row: [B, rope_dim/2]."""
+    B = x.shape[0]
+    xs = x.float().reshape(B, n_heads, head_dim)
+    if norm:
+        w = gamma.float() if gamma is not None else torch.full((head_dim,), float(weight))
+        xs = rmsnorm(xs, w, eps).to(torch.bfloat16).float()
+    if rope_dim:
+        c = cos_row.float().reshape(B, 1, -1)
+        s = sin_row.float().reshape(B, 1, -1)
+        xs = torch.cat([xs[..., :head_dim - rope_dim],
+                        rotary_interleaved(xs[..., head_dim - rope_dim:], c, s, inverse)], dim=-1)
+    return xs.to(torch.bfloat16).reshape(x.shape)
+
+
+def kv_norm_rope_quant(kv: torch.Tensor, gamma: torch.Tensor, cos_row, sin_row,
+                       eps: float = 1e-6, rope_dim: int = 64):
+    """The Lk-D1 zone (inference.py:5997-6006, test_lk_d1.py:498-594):
+    kv_norm -> bf16 -> rotary on the rope dims -> act_quant on the nope dims.
+    Returns (row bf16 [B, D], scales, codes)."""
+    D = kv.shape[-1]
+    y = head_norm_rope(kv, 1, D, cos_row, sin_row, rope_dim, gamma=gamma, eps=eps)
+    return kv_quant_row(y, rope_dim)
+
+
+@dataclass
+class BlockWeights:
+    """Weights of one compressed attention block (the CPU Attention,
+    inference.py:576-623; Compressor 523-552; Indexer 554-574)."""
+    wq_a: torch.Tensor          # [q_lora, dim]
+    q_norm: torch.Tensor        # [q_lora]
+    wq_b: torch.Tensor          # [H*D, q_lora]
+    wkv: torch.Tensor           # [D, dim]
+    kv_norm: torch.Tensor       # [D]
+    wo_a: torch.Tensor          # [G*R, H*D/G]
+    wo_b: torch.Tensor          # [dim, G*R]
+    c_wkv: torch.Tensor         # [2D, dim]  attention compressor
+    c_wgate: torch.Tensor       # [2D, dim]
+    i_wq_b: torch.Tensor        # [Hi*Di, q_lora]
+    i_wproj: torch.Tensor       # [Hi, dim]
+    i_wkv: torch.Tensor         # [2Di, dim] indexer compressor
+    i_wgate: torch.Tensor       # [2Di, dim]
+    n_groups: int = 8
+    eps: float = 1e-6
+
+
+def attention_decode_block(bw: BlockWeights, st: LayerState, x: torch.Tensor, pos: int,
+                           n_heads: int = 64, head_dim: int = 512, rope_dim: int = 64,
+                           index_n_heads: int = 64, index_head_dim: int = 128) -> torch.Tensor:
+    """DeviceAttention.forward_device for one token per sequence
+    (inference.py:5888-6127): q path (wq_a, q_norm, wq_b, per-head rms with
+    weight softmax_scale, rotary), kv path (wkv, Lk-D1, window write), the
+    indexer (wq_b + rotary on q, its compressor, weights_proj scaled by
+    softmax_scale * Hi^-1/2, 5175-5185), top-k, the attention compressor,
+    sparse attention with q pre-scaled, inverse rotary, grouped wo_a, wo_b.
+    x [B, 1, dim] -> [B, 1, dim] bf16; st.scale must be 1.0 (q carries it)."""
+    B = x.shape[0]
+    x2 = x.reshape(B, -1)
+    H, D, Hi, Di = n_heads, head_dim, index_n_heads, index_head_dim
+    cr, sr = st.cos[pos].expand(B, -1), st.sin[pos].expand(B, -1)
+    q_lora = linear_bf16(x2, bw.wq_a)
+    qr = head_norm_rope(q_lora, 1, q_lora.shape[-1], gamma=bw.q_norm, eps=bw.eps)
+    q = linear_bf16(qr, bw.wq_b)
+    q = head_norm_rope(q, H, D, cr, sr, rope_dim, weight=D ** -0.5, eps=bw.eps).view(B, H, D)
+    kv = head_norm_rope(linear_bf16(x2, bw.wkv), 1, D, cr, sr, rope_dim, gamma=bw.kv_norm, eps=bw.eps)
+    iq = linear_bf16(qr, bw.i_wq_b)
+    iq = head_norm_rope(iq, Hi, Di, cr, sr, rope_dim, norm=False).view(B, Hi, Di)
+    iw = linear_bf16(x2, (bw.i_wproj.float() * (Di ** -0.5 * Hi ** -0.5)).to(torch.bfloat16)).float()
+    o, idx = decode_layer_step(st, pos, q, kv, linear_bf16(x2, bw.c_wkv), linear_bf16(x2, bw.c_wgate),
+                               iq, linear_bf16(x2, bw.i_wkv), linear_bf16(x2, bw.i_wgate), iw)
+    o = head_norm_rope(o.reshape(B, H * D), H, D, cr, sr, rope_dim, norm=False, inverse=True)
+    G = bw.n_groups
+    R = bw.wo_a.shape[0] // G
+    og = o.view(B, G, H * D // G).float()
+    wa = bw.wo_a.to(torch.bfloat16).float().view(G, R, H * D // G)
+    a = torch.einsum("bgi,gri->bgr", og, wa).to(torch.bfloat16).reshape(B, G * R)
+    return linear_bf16(a, bw.wo_b).view(B, 1, -1)

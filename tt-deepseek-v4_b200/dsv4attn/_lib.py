@@ -32,6 +32,10 @@ PROTOTYPES = {
     "dsa_last_error": (ctypes.c_char_p, []),
     "dsa_act_quant_block": (I32, [P, P, P, P, I64, I64, I64, I64, I32, F32, F32, P]),
     "dsa_kv_window_write": (I32, [P, P, P, P, I32, I32, I32, I64, I32, I32, P]),
+    "dsa_kv_norm_rope_window_write": (I32, [P, I64, P, F32, P, P, I32, P, P, I64, I32, P, I64, P, I32, I32,
+                                            I32, P, P]),
+    "dsa_head_norm_rope": (I32, [P, I64, P, I64, I32, I32, I32, I32, P, F32, I32, F32, P, P, I32, P, I32, P, P]),
+    "dsa_fold_index_mask": (I32, [P, P, I64, P, P]),
     "dsa_compressor_step": (I32, [P, P, I64, P, P, P, P, P, P, I32, P, I64, I64, I32, P, P,
                                   I32, I32, I32, I32, I32, I32, I32, F32, P]),
     "dsa_window_indices": (I32, [P, P, I64, I32, I32, P]),

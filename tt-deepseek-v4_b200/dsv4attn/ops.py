@@ -114,6 +114,95 @@ def kv_window_write(kv: torch.Tensor, kv_cache: torch.Tensor, pos: torch.Tensor,
                                     rope_dim, kv_cache.stride(0), win, 64, _stream(kv)), "kv_window_write")
 
 
+def kv_norm_rope_window_write(kv: torch.Tensor, gamma: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                              pos: torch.Tensor, kv_cache: torch.Tensor, win: int, eps: float = 1e-6,
+                              rope_dim: int = 64, kv_out: torch.Tensor | None = None,
+                              scales: torch.Tensor | None = None, status: torch.Tensor | None = None) -> None:
+    """kv_norm -> rotary -> act_quant(nope) -> ring write at ``pos % win``
+    in one launch (Lk-D1 + attn.kv_update, inference.py:5997-6006,
+    6072-6079).  kv [B, D] bf16 (wkv output); gamma [D] fp32; cos/sin
+    [n_pos, rope/2] fp32; kv_cache [B, rows, D] bf16."""
+    _need(kv, "kv", BF16)
+    _need(gamma, "gamma", F32)
+    _need(cos, "cos", F32)
+    _need(sin, "sin", F32)
+    _need(pos, "pos", I32)
+    _need(kv_cache, "kv_cache", BF16)
+    for t, n in ((gamma, "gamma"), (cos, "cos"), (sin, "sin"), (pos, "pos")):
+        _contig(t, n)
+    if kv.dim() != 2 or kv.stride(-1) != 1:
+        raise ValueError("kv must be [B, D] with a unit stride in the last dim")
+    B, D = kv.shape
+    if gamma.numel() != D:
+        raise ValueError(f"gamma has {gamma.numel()} elements, expected {D}")
+    if kv_cache.dim() != 3 or kv_cache.shape[0] < B or kv_cache.shape[2] != D or kv_cache.stride(1) != D:
+        raise ValueError("kv_cache must be [B, rows, D] with contiguous rows")
+    if cos.shape != sin.shape or cos.shape[-1] * 2 != rope_dim:
+        raise ValueError(f"cos/sin must be [n_pos, {rope_dim // 2}]")
+    ld_out = 0
+    if kv_out is not None:
+        _need(kv_out, "kv_out", BF16)
+        ld_out = kv_out.stride(0)
+    check(lib().dsa_kv_norm_rope_window_write(kv.data_ptr(), kv.stride(0), gamma.data_ptr(), eps, cos.data_ptr(),
+                                              sin.data_ptr(), cos.shape[0], pos.data_ptr(), kv_cache.data_ptr(),
+                                              kv_cache.stride(0), win, _ptr(kv_out), ld_out, _ptr(scales), B, D,
+                                              rope_dim, _ptr(status), _stream(kv)), "kv_norm_rope_window_write")
+
+
+def head_norm_rope(x: torch.Tensor, n_heads: int, head_dim: int, cos=None, sin=None, pos=None, rope_dim: int = 0,
+                   gamma: torch.Tensor | None = None, weight: float = 1.0, norm: bool = True, eps: float = 1e-6,
+                   inverse: bool = False, out: torch.Tensor | None = None,
+                   status: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-head RMSNorm (gamma [head_dim] or scalar ``weight``) and/or
+    interleaved rotary of the last ``rope_dim`` dims at ``pos[b]`` for x
+    [B, ..., n_heads*head_dim] bf16 (inference.py:5982-5991, 6032-6034,
+    6100-6102).  ``out`` may be ``x`` (in place)."""
+    _need(x, "x", BF16)
+    if x.stride(-1) != 1:
+        raise ValueError("x must have a unit stride in the last dim")
+    B = x.numel() // (n_heads * head_dim)
+    x2 = x.reshape(B, n_heads * head_dim)
+    if out is None:
+        out = torch.empty_like(x)
+    o2 = out.view(B, n_heads * head_dim) if out.is_contiguous() else out.reshape(B, n_heads * head_dim)
+    if o2.data_ptr() != out.data_ptr():
+        raise ValueError("out must be viewable as [B, n_heads*head_dim]")
+    if gamma is not None:
+        _need(gamma, "gamma", F32)
+        _contig(gamma, "gamma")
+        if gamma.numel() != head_dim:
+            raise ValueError(f"gamma has {gamma.numel()} elements, expected {head_dim}")
+    n_pos = 0
+    if rope_dim:
+        for t, n in ((cos, "cos"), (sin, "sin")):
+            _need(t, n, F32)
+            _contig(t, n)
+        _need(pos, "pos", I32)
+        if cos.shape[-1] * 2 != rope_dim:
+            raise ValueError(f"cos/sin must be [n_pos, {rope_dim // 2}]")
+        n_pos = cos.shape[0]
+    check(lib().dsa_head_norm_rope(x2.data_ptr(), x2.stride(0), o2.data_ptr(), o2.stride(0), B, n_heads, head_dim,
+                                   rope_dim, _ptr(gamma), float(weight), int(norm), eps, _ptr(cos), _ptr(sin),
+                                   n_pos, _ptr(pos), int(inverse), _ptr(status), _stream(x)), "head_norm_rope")
+    return out
+
+
+def fold_index_mask(idx: torch.Tensor, valid: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """-1 where the additive bf16 mask is negative, else idx (inverse of
+    inference.py:4444-4457)."""
+    _need(idx, "idx", I32)
+    _need(valid, "valid", BF16)
+    _contig(idx, "idx")
+    _contig(valid, "valid")
+    if valid.numel() != idx.numel():
+        raise ValueError(f"valid has {valid.numel()} elements, idx {idx.numel()}")
+    if out is None:
+        out = torch.empty_like(idx)
+    check(lib().dsa_fold_index_mask(idx.data_ptr(), valid.data_ptr(), idx.numel(), out.data_ptr(), _stream(idx)),
+          "fold_index_mask")
+    return out
+
+
 # ------------------------------------------------------------ attn.compress
 
 def compressor_step(kv_row, score_row, ape, kv_state, score_state, gamma, cos, sin, kv_cache, slot_offset: int,
