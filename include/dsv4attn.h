@@ -206,6 +206,23 @@ int dsa_topk_merge(const float* cand_score, const int32_t* cand_idx, int n_cand,
                    int32_t* out_idx, float* out_score, int64_t ld_out, int B, int k,
                    int win, dsa_stream_t stream);
 
+/* Sequence split helpers (one context's compressed entries cut into
+ * contiguous shards [lo, hi), one per GPU; the split the reference plans in
+ * briefs/future_max_utilization.md:177-204).
+ * dsa_shard_active: t_local[b] = clamp(t_active[b] - lo, 0, n_local), the
+ * shard's share of T_active (inference.py:6028).
+ * dsa_shard_local_indices: from the merged global selection sel [B, k]
+ * (compressed positions, -1 = none) build this shard's attention index
+ * list out [B, W + k]: window slots win_idx[b, j] + win_base (win_idx NULL:
+ * this shard does not attend the window, all -1), then sel - lo +
+ * local_base for positions in [lo, hi), else -1.  The local list is what
+ * dsa_sparse_attn_partial reads over the shard's [B, rows, D] cache. */
+int dsa_shard_active(const int32_t* t_active, int32_t* t_local, int B, int lo, int n_local,
+                     dsa_stream_t stream);
+int dsa_shard_local_indices(const int32_t* sel, int64_t ld_sel, int k, const int32_t* win_idx,
+                            int64_t ld_win, int W, int lo, int hi, int local_base, int win_base,
+                            int32_t* out, int64_t ld_out, int B, dsa_stream_t stream);
+
 /* ------------------------------------------------------------ attn.sparse */
 
 /* Bytes of workspace dsa_sparse_attn needs for this shape (0 when it runs

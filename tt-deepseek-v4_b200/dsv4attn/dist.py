@@ -1,0 +1,263 @@
+"""The path across GPUs: batch split and sequence split.
+
+Batch split (config 2): the sequences are independent, so each rank owns
+B / world of them with their caches and runs ``layer.DecodePath`` unchanged;
+there is no collective on the data path (``batch_shard``).
+
+Sequence split (config 3): one long context, its compressed KV rows and
+indexer keys cut into ``world`` contiguous shards [lo, hi).  One decode step
+of one layer on every rank:
+
+  local    window ring write (replicated; attended by the last rank, which
+           holds the newest tokens), both compressors (state replicated,
+           the emitted row stored only by the rank that owns its position),
+           indexer score over the shard, local top-k' candidates
+           (k' = min(k, shard rows)) with global positions
+  exchange all-gather of the candidates (G x k' x 8 bytes)
+  attend   global merge (identical on every rank), this shard's rows of the
+           selection, partial attention (m, l, o) without the sink
+  exchange all-gather of the partials (G x H x (D + 2) x 4 bytes)
+  combine  log-sum-exp merge with the sink counted once -> bf16 o
+
+Any global top-k entry is in its shard's top-k', and both selections break
+ties towards the lower position, so the merged index set is exactly the
+unsplit one (inference.py:5823-5851); the combine is exact up to fp32
+rounding.  The reference plans this split (briefs/future_max_utilization.md:
+177-204) but does not implement it.
+
+``SeqShard`` holds one rank's buffers and runs the three compute phases;
+``SeqSplitPath`` drives it with a ``Comm`` (torch.distributed all-gathers,
+NCCL on GPUs).  The phases are separate methods so that G shards can also be
+driven inside one process (the exchanges become copies), which is how the
+single-GPU tests check the split against the unsplit path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops as native_ops
+from .layer import LayerInputs
+from .tables import PathArgs, rope_cos_sin
+
+BF16 = torch.bfloat16
+F32 = torch.float32
+I32 = torch.int32
+
+
+def batch_shard(B_total: int, rank: int, world: int):
+    """Contiguous [start, stop) of the sequences rank ``rank`` owns."""
+    if B_total % world:
+        raise ValueError(f"batch {B_total} not divisible by {world} ranks")
+    per = B_total // world
+    return rank * per, (rank + 1) * per
+
+
+def seq_shard(T_total: int, rank: int, world: int):
+    """Contiguous [lo, hi) of the compressed positions rank ``rank`` owns."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    per = -(-T_total // world)
+    lo = min(rank * per, T_total)
+    return lo, min(lo + per, T_total)
+
+
+class TorchDistComm:
+    """All-gathers over a torch.distributed process group."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        """out [world, *inp.shape] <- every rank's inp."""
+        try:
+            self.dist.all_gather_into_tensor(out, inp, group=self.group)
+        except (RuntimeError, NotImplementedError):
+            self.dist.all_gather(list(out.unbind(0)), inp, group=self.group)
+
+
+class SeqShardLayer:
+    """One layer's shard: compressed rows [lo, hi) + the window ring."""
+
+    def __init__(self, args: PathArgs, B: int, n_local: int, k: int, kc: int, world: int, device):
+        D, Di, H, W, r = args.head_dim, args.index_head_dim, args.n_heads, args.window_size, args.compress_ratio
+        dev = device
+        # rows [0, n_local) compressed entries of this shard, then the W-row window ring
+        self.kv = torch.zeros(B, n_local + W, D, dtype=BF16, device=dev)
+        self.keys = torch.zeros(B, max(n_local, 1), Di, dtype=BF16, device=dev)
+        self.cmp_kv = torch.zeros(B, 2 * r, 2 * D, dtype=F32, device=dev)
+        self.cmp_sc = torch.full((B, 2 * r, 2 * D), float("-inf"), dtype=F32, device=dev)
+        self.icmp_kv = torch.zeros(B, 2 * r, 2 * Di, dtype=F32, device=dev)
+        self.icmp_sc = torch.full((B, 2 * r, 2 * Di), float("-inf"), dtype=F32, device=dev)
+        self.ape = torch.zeros(r, 2 * D, dtype=F32, device=dev)
+        self.gamma = torch.ones(D, dtype=F32, device=dev)
+        self.iape = torch.zeros(r, 2 * Di, dtype=F32, device=dev)
+        self.igamma = torch.ones(Di, dtype=F32, device=dev)
+        self.sink = torch.zeros(H, dtype=F32, device=dev)
+        # per-step scratch
+        self.score = torch.zeros(B, max(n_local, 1), dtype=F32, device=dev)
+        self.cand_idx = torch.full((B, kc), -1, dtype=I32, device=dev)
+        self.cand_score = torch.full((B, kc), float("-inf"), dtype=F32, device=dev)
+        self.cand_idx_all = torch.full((world, B, kc), -1, dtype=I32, device=dev)
+        self.cand_score_all = torch.full((world, B, kc), float("-inf"), dtype=F32, device=dev)
+        self.sel = torch.full((B, k), -1, dtype=I32, device=dev)
+        self.win_idx = torch.full((B, W), -1, dtype=I32, device=dev)
+        self.lidx = torch.full((B, W + k), -1, dtype=I32, device=dev)
+        self.pml = torch.zeros(B, H, 2, dtype=F32, device=dev)
+        self.po = torch.zeros(B, H, D, dtype=F32, device=dev)
+        self.pml_all = torch.zeros(world, B, H, 2, dtype=F32, device=dev)
+        self.po_all = torch.zeros(world, B, H, D, dtype=F32, device=dev)
+
+    def kv_compressed(self, n_local: int):
+        return self.kv[:, :n_local]
+
+    def kv_window(self, n_local: int):
+        return self.kv[:, n_local:]
+
+
+class SeqShard:
+    """One rank's part of the sequence split for a stack of layers."""
+
+    def __init__(self, args: PathArgs, B: int, T_total: int, rank: int, world: int, device, k: int | None = None,
+                 n_layers: int = 1, max_seq_len: int | None = None, window_rank: int | None = None,
+                 scale: float | None = None, backend=None):
+        self.args = args
+        self.B = B
+        self.rank, self.world = rank, world
+        self.device = torch.device(device)
+        self.ops = backend if backend is not None else native_ops
+        self.T_total = T_total
+        self.lo, self.hi = seq_shard(T_total, rank, world)
+        self.n_local = self.hi - self.lo
+        self.k = args.index_topk if k is None else k
+        if self.k > T_total:
+            raise ValueError(f"index_topk {self.k} > compressed capacity {T_total}")
+        per = -(-T_total // world)
+        self.kc = min(self.k, per)
+        if world * self.kc > 16384:
+            raise ValueError(f"{world} x {self.kc} candidates exceed the 16384 the merge selects from")
+        self.window_rank = world - 1 if window_rank is None else window_rank
+        self.scale = args.softmax_scale if scale is None else scale
+        max_seq = max_seq_len if max_seq_len is not None else T_total * args.compress_ratio
+        self.cos, self.sin = rope_cos_sin(args, max_seq, compressed=True, device=self.device)
+        self.layers = [SeqShardLayer(args, B, self.n_local, self.k, self.kc, world, self.device)
+                       for _ in range(n_layers)]
+        dev = self.device
+        self.pos = torch.zeros(B, dtype=I32, device=dev)
+        self.t_active = torch.zeros(B, dtype=I32, device=dev)
+        self.t_local = torch.zeros(B, dtype=I32, device=dev)
+        self.status = torch.zeros(1, dtype=I32, device=dev)
+        H, D = args.n_heads, args.head_dim
+        ws_attn = 0
+        if backend is None:
+            ws_attn = int(native_ops.lib().dsa_sparse_attn_workspace_size(B, 1, H, D, args.window_size + self.k))
+            ws_topk = int(native_ops.lib().dsa_indexer_topk_workspace_size(B, max(self.n_local, 1), self.kc))
+            self.ws = native_ops.Workspace(dev, max(ws_attn, ws_topk))
+        else:
+            self.ws = None
+
+    def set_positions(self, pos) -> None:
+        p = torch.as_tensor(pos, dtype=I32).reshape(-1).expand(self.B).contiguous()
+        self.pos.copy_(p.to(self.device))
+        self.t_active.copy_(((p + 1) // self.args.compress_ratio).to(self.device))
+
+    # ---- phase 1: everything before the candidate exchange
+    def phase_local(self, L: SeqShardLayer, x: LayerInputs) -> None:
+        a, o = self.args, self.ops
+        W, r, n = a.window_size, a.compress_ratio, self.n_local
+        o.kv_window_write(x.kv, L.kv_window(n), self.pos, W, rope_dim=a.rope_head_dim)
+        o.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos, self.sin,
+                          L.keys[:, :max(n, 1)], -self.lo, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
+                          rope_dim=a.rope_head_dim)
+        if n == 0:
+            return
+        o.shard_active(self.t_active, self.lo, n, out=self.t_local)
+        o.indexer_score(x.iq, L.keys, x.iw, n, out=L.score, t_valid=self.t_local)
+        o.indexer_topk(L.score, self.t_local, self.kc if self.kc <= n else n, self.lo, T=n, sort_desc=False,
+                       mask_mode=1, out=L.cand_idx[:, :min(self.kc, n)], out_score=L.cand_score[:, :min(self.kc, n)],
+                       ws=self.ws)
+
+    # ---- phase 2: merge, local rows of the selection, partial attention
+    def phase_attend(self, L: SeqShardLayer, x: LayerInputs) -> None:
+        a, o = self.args, self.ops
+        W, r, n = a.window_size, a.compress_ratio, self.n_local
+        G, B = self.world, self.B
+        if B == 1:
+            cs, ci = L.cand_score_all.view(1, G * self.kc), L.cand_idx_all.view(1, G * self.kc)
+        else:
+            cs = L.cand_score_all.permute(1, 0, 2).reshape(B, G * self.kc)
+            ci = L.cand_idx_all.permute(1, 0, 2).reshape(B, G * self.kc)
+        o.topk_merge(cs, ci, self.k, 0, out=L.sel)
+        attend_window = self.rank == self.window_rank
+        if attend_window:
+            o.window_indices(self.pos, W, out=L.win_idx)
+        o.shard_local_indices(L.sel, self.lo, self.hi, W, L.win_idx if attend_window else None, local_base=0,
+                              win_base=n, out=L.lidx)
+        o.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
+                          L.kv_compressed(max(n, 1)) if n else L.kv[:, :1], -self.lo if n else -(1 << 30),
+                          self.pos, r, overlap=True, rotate=False, eps=a.norm_eps, rope_dim=a.rope_head_dim)
+        o.sparse_attn_partial(x.q, L.kv, L.lidx, self.scale, part_ml=L.pml, part_o=L.po, ws=self.ws,
+                              status=self.status)
+
+    # ---- phase 3: combine the gathered partials
+    def phase_combine(self, L: SeqShardLayer, out: torch.Tensor) -> None:
+        B, H, D = self.B, self.args.n_heads, self.args.head_dim
+        self.ops.lse_combine(L.pml_all.view(self.world, B, H, 2), L.po_all.view(self.world, B, H, D), L.sink,
+                             out=out.view(B, H, D))
+
+    def advance(self) -> None:
+        self.ops.advance_positions(self.pos, self.t_active, self.args.compress_ratio, 1)
+
+
+class SeqSplitPath:
+    """Runs a SeqShard's layers with the two all-gathers between phases."""
+
+    def __init__(self, shard: SeqShard, comm):
+        self.shard = shard
+        self.comm = comm
+
+    def layer_step(self, L: SeqShardLayer, x: LayerInputs, out: torch.Tensor) -> None:
+        s, c = self.shard, self.comm
+        s.phase_local(L, x)
+        c.all_gather(L.cand_score_all, L.cand_score)
+        c.all_gather(L.cand_idx_all, L.cand_idx)
+        s.phase_attend(L, x)
+        c.all_gather(L.pml_all, L.pml)
+        c.all_gather(L.po_all, L.po)
+        s.phase_combine(L, out)
+
+    def step(self, inputs, outs, advance: bool = True) -> None:
+        for L, x, o in zip(self.shard.layers, inputs, outs):
+            self.layer_step(L, x, o)
+        if advance:
+            self.shard.advance()
+
+
+def run_shards_in_process(shards, inputs, outs, advance: bool = True) -> None:
+    """One step of all G shards of a sequence split inside one process (the
+    exchanges become copies).  ``inputs[l]`` is shared by every shard (the
+    replicated per-token inputs); ``outs[g][l]`` receives shard g's result."""
+    G = len(shards)
+    for li in range(len(shards[0].layers)):
+        Ls = [s.layers[li] for s in shards]
+        for s, L in zip(shards, Ls):
+            s.phase_local(L, inputs[li])
+        for L in Ls:
+            for g in range(G):
+                L.cand_score_all[g].copy_(Ls[g].cand_score)
+                L.cand_idx_all[g].copy_(Ls[g].cand_idx)
+        for s, L in zip(shards, Ls):
+            s.phase_attend(L, inputs[li])
+        for L in Ls:
+            for g in range(G):
+                L.pml_all[g].copy_(Ls[g].pml)
+                L.po_all[g].copy_(Ls[g].po)
+        for g, (s, L) in enumerate(zip(shards, Ls)):
+            s.phase_combine(L, outs[g][li])
+    if advance:
+        for s in shards:
+            s.advance()

@@ -317,6 +317,38 @@ def topk_merge(cand_score: torch.Tensor, cand_idx: torch.Tensor, k: int, win: in
     return out
 
 
+def shard_active(t_active: torch.Tensor, lo: int, n_local: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """This shard's share of T_active: clamp(t_active - lo, 0, n_local)."""
+    _need(t_active, "t_active", I32)
+    if out is None:
+        out = torch.empty_like(t_active)
+    check(lib().dsa_shard_active(t_active.data_ptr(), out.data_ptr(), t_active.numel(), lo, n_local,
+                                 _stream(t_active)), "shard_active")
+    return out
+
+
+def shard_local_indices(sel: torch.Tensor, lo: int, hi: int, W: int, win_idx: torch.Tensor | None = None,
+                        local_base: int = 0, win_base: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[B, W + k] local attention rows of a shard from the merged global
+    selection ``sel`` [B, k] (see dsa_shard_local_indices)."""
+    _need(sel, "sel", I32)
+    B, k = sel.shape
+    if sel.stride(-1) != 1:
+        raise ValueError("sel must have a unit stride in the last dim")
+    ld_win = 0
+    if win_idx is not None:
+        _need(win_idx, "win_idx", I32)
+        if win_idx.shape[-1] != W or win_idx.stride(-1) != 1:
+            raise ValueError(f"win_idx must be [B, {W}] with a unit last stride")
+        ld_win = win_idx.stride(0)
+    if out is None:
+        out = torch.empty(B, W + k, dtype=I32, device=sel.device)
+    check(lib().dsa_shard_local_indices(sel.data_ptr(), sel.stride(0), k, _ptr(win_idx), ld_win, W, lo, hi,
+                                        local_base, win_base, out.data_ptr(), out.stride(0), B, _stream(sel)),
+          "shard_local_indices")
+    return out
+
+
 def advance_positions(pos: torch.Tensor, t_active: torch.Tensor | None, ratio: int, step: int = 1) -> None:
     _need(pos, "pos", I32)
     check(lib().dsa_advance_positions(pos.data_ptr(), _ptr(t_active), pos.shape[0], ratio, step, _stream(pos)),
