@@ -49,7 +49,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel timings to stderr")
-    return ap.parse_args()
+    ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2",
+                    help="cfg2: batched decode, batch split; cfg3: one 256k context, sequence split")
+    a = ap.parse_args()
+    if a.workload == "cfg3" and "--ctx" not in sys.argv:
+        a.ctx = 262144
+    return a
 
 
 def peaks():
@@ -306,6 +311,9 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    if args.workload == "cfg3":
+        run_cfg3(args, rank, world, dev)
+        return
 
     log("building layers")
     pa, path, inputs, outs = build_path(args, dev, seed=1234 + rank)
@@ -400,6 +408,136 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+class _SelfComm:
+    """World of one: the all-gather is a copy."""
+
+    def all_gather(self, out, inp):
+        out[0].copy_(inp)
+
+
+def run_cfg3(args, rank, world, dev):
+    """Config 3: batch 1, one context of args.ctx tokens (args.ctx / 4
+    compressed entries), compressed KV and indexer keys split contiguously
+    over the ranks; per layer two all-gathers (candidates, partials) over
+    NCCL.  All 43 layers with their own shards; one step = one decode step
+    of all layers.  "scaling": "strong" (the context is fixed as N grows)."""
+    import torch
+    import torch.distributed as dist
+    from dsv4attn.dist import SeqShard, SeqSplitPath, TorchDistComm
+    from dsv4attn.layer import LayerInputs
+    from dsv4attn.tables import PathArgs
+    pa = PathArgs(index_topk=args.topk)
+    T_total = args.ctx // 4
+    max_seq = args.ctx + 4096
+    log(f"cfg3: building {args.layers} sharded layers (T={T_total}, rank {rank}/{world})")
+    shard = SeqShard(pa, 1, T_total, rank, world, dev, k=args.topk, n_layers=args.layers, max_seq_len=max_seq)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    for L in shard.layers:
+        L.kv.normal_(generator=g)
+        L.keys.normal_(generator=g)
+        for t in (L.cmp_kv, L.cmp_sc, L.icmp_kv, L.icmp_sc, L.ape, L.iape):
+            t.normal_(generator=g)
+    gi = torch.Generator(device=dev).manual_seed(99)   # replicated inputs: same seed on every rank
+    for L in shard.layers:
+        L.sink.normal_(generator=gi)
+    inputs = []
+    for _ in range(args.layers):
+        x = LayerInputs.empty(pa, 1, dev)
+        for t in x.tensors():
+            t.normal_(generator=gi)
+        x.iw.mul_(0.02)
+        inputs.append(x)
+    outs = [torch.empty(1, 64, 512, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
+    comm = TorchDistComm() if world > 1 else _SelfComm()
+    path = SeqSplitPath(shard, comm)
+    shard.set_positions(args.ctx - 1)
+    torch.cuda.synchronize()
+    path.step(inputs, outs)                    # eager warm-up (also sizes the workspace)
+    torch.cuda.synchronize()
+    graph, mode = None, "graph"
+    try:
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            path.step(inputs, outs)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            path.step(inputs, outs)
+    except Exception as e:                     # capture of the collectives refused: time eagerly
+        log(f"graph capture failed ({type(e).__name__}: {e}); timing eagerly")
+        graph, mode = None, "eager"
+        torch.cuda.synchronize()
+    shard.set_positions(args.ctx - 1)
+    torch.cuda.synchronize()
+
+    def one():
+        if graph is not None:
+            graph.replay()
+        else:
+            path.step(inputs, outs)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(int(str(dev).split(":")[-1]))
+    clocks.start()
+    time.sleep(0.3)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        one()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_total = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    if int(shard.status.item()) != 0:
+        raise RuntimeError(f"device status {int(shard.status.item())} during the cfg3 bench")
+    ms_step = ms_total / args.steps
+    us_layer = ms_step * 1e3 / args.layers
+    # algorithmic bytes per layer-step of the whole job: all keys once, the
+    # selected rows once, q/o, scores written and read once
+    W, k, D, Di = 128, args.topk, 512, 128
+    t_act = T_total
+    per_layer = t_act * Di * 2 + (W + k) * D * 2 + 64 * D * 2 * 2 + 64 * Di * 2 + 2 * t_act * 4
+    hbm, hbm_kind = peaks()
+    gbs = per_layer / (us_layer * 1e-6) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(1e3 / ms_step, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "us_per_layer": round(us_layer, 2), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) shards/inputs, indexer weights N(0,0.02))",
+            "config": {"workload": f"cfg3 long-context decode: batch 1, ctx {args.ctx} ({T_total} compressed), "
+                                   f"top-{k} + window {W}, {args.layers} layers, sequence split over {world} GPU(s)",
+                       "global_batch": 1, "seq_len": args.ctx, "layers": args.layers,
+                       "parallelism": f"sequence split x{world} (NCCL all-gather of candidates and partials)",
+                       "timing": mode},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm * world, "unit": "GB/s",
+                         "frac": round(gbs / (hbm * world), 4), "traffic": None,
+                         "peak_kind": f"{hbm_kind} x {world} GPUs",
+                         "algorithmic_bytes_per_layer": per_layer},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del graph
+        dist.destroy_process_group()
 
 
 def measure_e2e(args, path, inputs, outs, dev, world):

@@ -187,6 +187,26 @@ int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_a
                         int B, int T, int k, int win, int sort_desc, int mask_mode,
                         void* workspace, size_t workspace_bytes, dsa_stream_t stream);
 
+/* Top-k of a few long rows spread over many CTAs: one cooperative launch
+ * of cpr CTAs per row (cpr * B <= the SM count) running an MSD radix select
+ * with grid-wide barriers, for rows too long / too few for one CTA each
+ * (the sequence split's single context).  Same masking, validity, tie and
+ * win rules as dsa_indexer_topk; output in ascending position order.
+ * ids (may be NULL): [B, T] int32 - the output then carries ids[t] + win
+ * and slots with ids[t] < 0 count as -inf (the candidate merge of the split;
+ * ties break towards the lower slot, so pass candidates in position order).
+ * workspace: dsa_topk_wide_workspace_size(B, T) bytes, 16-byte aligned,
+ * zeroed before its first use (the kernel leaves it zeroed; re-zero after a
+ * timeout).  status (may be NULL): bit 2 set when a grid barrier timed out.
+ * Returns DSA_ERR_UNSUPPORTED when the rows need more CTAs than SMs.
+ * Replaces the ttnn.topk of _indexer_topk_body (inference.py:5841-5842) for
+ * single long rows. */
+size_t dsa_topk_wide_workspace_size(int B, int T);
+int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t* ids, int64_t ld_ids,
+                  const int32_t* t_active, int32_t* out_idx, float* out_score, int64_t ld_out,
+                  int B, int T, int k, int win, int mask_mode, void* workspace,
+                  size_t workspace_bytes, int32_t* status, dsa_stream_t stream);
+
 /* Device-side position advance for graph-replayed decode: pos[b] += step;
  * t_active[b] = (pos[b] + 1) / ratio (T_active of inference.py:6028; may
  * be NULL).  Replaces the per-step host staging of pre_stage_decode

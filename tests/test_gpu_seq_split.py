@@ -32,7 +32,7 @@ def _run_split(args, full, inputs, G, T_total, pos0, max_seq, dev, B):
         run_shards_in_process(shards, [xd], outs)
         torch.cuda.synchronize()
         outs_all.append([o[0].cpu() for o in outs])
-        sels.append(shards[0].layers[0].sel.cpu().clone())
+        sels.append(shards[0].layers[0].selected.cpu().clone())
         for s in shards:
             assert int(s.status.item()) == 0
     return outs_all, sels

@@ -272,12 +272,17 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_mma_kernel(SaArgs a
   }
 }
 
-// grid (M, H); 128 threads x 4 dims.  final: o = sum_p o_p e^{m_p-M} / L with
-// the sink in L; partial: (M, L, sum_p o_p e^{m_p-M}) without the sink.
-// One warp per (query row, head): the split statistics are reduced across
-// lanes (any number of splits), then lane l combines output dims
-// [16 l, 16 l + 16) of every split with all of a split's loads in flight.
+// Merge of the split-K partials of each query row: final mode writes
+// o = sum_p o_p e^{m_p - M} / L with the sink in L; partial mode writes
+// (M, L, sum_p o_p e^{m_p-M}) without the sink.  One warp per (query row,
+// head, slice of DPL * 32 output dims): the split statistics are reduced
+// across lanes (any number of splits), then lane l combines DPL dims of
+// every split, four splits' loads in flight at a time.  DPL = 16 covers the
+// 512 dims with one warp (many query rows); DPL = 4 spreads a row over 4x
+// more warps for the few-row case (a single long context), where the
+// combine would otherwise run on M * 8 CTAs.
 constexpr int kCombineWarps = 8;
+template <int DPL>
 __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
     const float* __restrict__ part_ml, const float* __restrict__ part_o, const float* __restrict__ sink, int P, int M,
     int H, int D, int final_mode, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, float* __restrict__ out_ml,
@@ -300,52 +305,60 @@ __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
   }
   float L = warp_sum(lsum);
   if (final_mode && Mx != -INFINITY) L += expf(sink[h] - Mx);
-  const int d0 = 16 * lane;  // D = 512: 16 dims per lane
-  float acc[16];
+  const int d0 = blockIdx.z * (32 * DPL) + DPL * lane;
+  float acc[DPL];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+#pragma unroll 4
   for (int p = 0; p < P; ++p) {
     const float mp = ml(p, 0);
-    if (mp == -INFINITY) continue;
-    const float w = expf(mp - Mx);
+    const float w = (mp == -INFINITY) ? 0.f : expf(mp - Mx);
     const float4* src = reinterpret_cast<const float4*>(part_o + ((int64_t(p) * M + m) * H + h) * D + d0);
-    const float4 v0 = __ldg(src), v1 = __ldg(src + 1), v2 = __ldg(src + 2), v3 = __ldg(src + 3);
-    acc[0] = fmaf(w, v0.x, acc[0]);
-    acc[1] = fmaf(w, v0.y, acc[1]);
-    acc[2] = fmaf(w, v0.z, acc[2]);
-    acc[3] = fmaf(w, v0.w, acc[3]);
-    acc[4] = fmaf(w, v1.x, acc[4]);
-    acc[5] = fmaf(w, v1.y, acc[5]);
-    acc[6] = fmaf(w, v1.z, acc[6]);
-    acc[7] = fmaf(w, v1.w, acc[7]);
-    acc[8] = fmaf(w, v2.x, acc[8]);
-    acc[9] = fmaf(w, v2.y, acc[9]);
-    acc[10] = fmaf(w, v2.z, acc[10]);
-    acc[11] = fmaf(w, v2.w, acc[11]);
-    acc[12] = fmaf(w, v3.x, acc[12]);
-    acc[13] = fmaf(w, v3.y, acc[13]);
-    acc[14] = fmaf(w, v3.z, acc[14]);
-    acc[15] = fmaf(w, v3.w, acc[15]);
+    float4 v[DPL / 4];
+#pragma unroll
+    for (int i = 0; i < DPL / 4; ++i) v[i] = __ldg(src + i);
+#pragma unroll
+    for (int i = 0; i < DPL / 4; ++i) {
+      acc[4 * i + 0] = fmaf(w, v[i].x, acc[4 * i + 0]);
+      acc[4 * i + 1] = fmaf(w, v[i].y, acc[4 * i + 1]);
+      acc[4 * i + 2] = fmaf(w, v[i].z, acc[4 * i + 2]);
+      acc[4 * i + 3] = fmaf(w, v[i].w, acc[4 * i + 3]);
+    }
   }
   if (final_mode) {
     const float inv = 1.f / L;
-    uint4* op = reinterpret_cast<uint4*>(out + (int64_t(m) * H + h) * D + d0);
-    op[0] = make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
-                       pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv));
-    op[1] = make_uint4(pack_bf16x2(acc[8] * inv, acc[9] * inv), pack_bf16x2(acc[10] * inv, acc[11] * inv),
-                       pack_bf16x2(acc[12] * inv, acc[13] * inv), pack_bf16x2(acc[14] * inv, acc[15] * inv));
+    uint2* op = reinterpret_cast<uint2*>(out + (int64_t(m) * H + h) * D + d0);
+#pragma unroll
+    for (int i = 0; i < DPL / 4; ++i)
+      op[i] = make_uint2(pack_bf16x2(acc[4 * i] * inv, acc[4 * i + 1] * inv),
+                         pack_bf16x2(acc[4 * i + 2] * inv, acc[4 * i + 3] * inv));
   } else {
     float4* op = reinterpret_cast<float4*>(out_o + (int64_t(m) * H + h) * D + d0);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) op[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+    for (int i = 0; i < DPL / 4; ++i) op[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
   }
-  if (lane == 0) {
+  if (lane == 0 && blockIdx.z == 0) {
     if (final_mode) {
       if (lse) lse[int64_t(m) * H + h] = Mx + logf(L);
     } else {
       out_ml[(int64_t(m) * H + h) * 2] = Mx;
       out_ml[(int64_t(m) * H + h) * 2 + 1] = L;
     }
+  }
+}
+
+// Launch of the combine: DPL = 4 (4 CTAs per 8 heads) when the rows alone
+// would leave most SMs idle.
+static void launch_lse_combine(const float* part_ml, const float* part_o, const float* sink, int P, int M, int H,
+                               int D, int final_mode, __nv_bfloat16* out, float* lse, float* out_ml, float* out_o,
+                               cudaStream_t st) {
+  const int hb = (H + kCombineWarps - 1) / kCombineWarps;
+  if (int64_t(M) * hb < 2 * num_sms()) {
+    lse_combine_kernel<4><<<dim3(M, hb, D / 128), 32 * kCombineWarps, 0, st>>>(
+        part_ml, part_o, sink, P, M, H, D, final_mode, out, lse, out_ml, out_o);
+  } else {
+    lse_combine_kernel<16><<<dim3(M, hb, D / 512), 32 * kCombineWarps, 0, st>>>(
+        part_ml, part_o, sink, P, M, H, D, final_mode, out, lse, out_ml, out_o);
   }
 }
 
@@ -500,10 +513,8 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   }
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {
-    lse_combine_kernel<<<dim3(M, kSaH / kCombineWarps), 32 * kCombineWarps, 0, st>>>(
-        ws_ml, ws_o, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
-                                                      static_cast<__nv_bfloat16*>(out), lse, part_ml_out,
-                                                      part_o_out);
+    launch_lse_combine(ws_ml, ws_o, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
+                       static_cast<__nv_bfloat16*>(out), lse, part_ml_out, part_o_out, st);
     DSA_CHECK_LAUNCH("sparse_attn(combine)");
   }
   return DSA_OK;
@@ -538,9 +549,8 @@ extern "C" int dsa_lse_combine(const float* part_ml, const float* part_o, const 
   DSA_CHECK_ARG(D == kSaD, "lse_combine: built for D=%d (got %d)", kSaD, D);
   DSA_CHECK_ARG(aligned(part_o, 16) && aligned(out, 16), "lse_combine: part_o / out must be 16-byte aligned");
   if (M == 0) return DSA_OK;
-  lse_combine_kernel<<<dim3(M, (H + kCombineWarps - 1) / kCombineWarps), 32 * kCombineWarps, 0,
-                       reinterpret_cast<cudaStream_t>(stream)>>>(
-      part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr, nullptr);
+  launch_lse_combine(part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
+                     nullptr, reinterpret_cast<cudaStream_t>(stream));
   DSA_CHECK_LAUNCH("lse_combine");
   return DSA_OK;
 }

@@ -111,7 +111,7 @@ struct Args {
 
 // trace slots (each kTrTiles long): producers issued tile t / MMA got tile t /
 // MMA issued S(t) / MMA issued PV(t) / softmax got S(t) / softmax wrote P(t) /
-// misc (0: start, 1: end)
+// misc (0: start, 1: end, 2: last PV done, 3: l reduced, 4: O stored)
 enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3, kTrPV = 4, kTrSGot = 5, kTrPDone = 6,
              kTrMisc = 7 };
 #define SA_TRACE(slot, t)                                                                         \
@@ -443,22 +443,25 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     // ---------------------------------------------------------------- epilogue
     if (n > 0) warp_wait(&aux->pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1);
     tc::fence_after_sync();
-    // l per head: the 8 lanes sharing q4, then the 4 warps
+    if (tid == 0) SA_TRACE(kTrMisc, 2);
+    // l per head: each head's partial sums sit in 32 threads (8 lanes of
+    // each warp); gather them through the P buffers, free now that the last
+    // PV has completed.  (A shuffle tree here measured ~10k cycles, this ~1k.)
+    float* lbuf = reinterpret_cast<float*>(smem + kOffP);
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1)
-#pragma unroll
-      for (int i = 0; i < 16; ++i) lp[i] += __shfl_xor_sync(0xffffffffu, lp[i], off);
-    if (g8 == 0) {
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        aux->red[warp][8 * r + 2 * q4] = lp[2 * r];
-        aux->red[warp][8 * r + 2 * q4 + 1] = lp[2 * r + 1];
-      }
-    }
+    for (int i = 0; i < 16; ++i) lbuf[i * 128 + tid] = lp[i];
     tc::named_bar_sync(1, 128);
     if (tid < H) {
       const float mh = aux->m[tid];
-      const float lh = (aux->red[0][tid] + aux->red[1][tid]) + (aux->red[2][tid] + aux->red[3][tid]);
+      const float* lr = lbuf + (2 * (tid >> 3) + (tid & 1)) * 128 + ((tid & 7) >> 1);
+      float lw[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        lw[w] = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) lw[w] += lr[w * 32 + g * 4];
+      }
+      const float lh = (lw[0] + lw[1]) + (lw[2] + lw[3]);
       if (a.final_mode) {
         const float sk = a.sink[tid] * kLog2e;
         const float Mx = fmaxf(mh, sk);
@@ -474,6 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       }
     }
     tc::named_bar_sync(1, 128);
+    if (tid == 0) SA_TRACE(kTrMisc, 3);
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
     const int dloc = warp * 32 + lane;
 #pragma unroll 1
@@ -501,6 +505,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       }
     }
   }
+  if (tid == 0) SA_TRACE(kTrMisc, 4);
   tc::fence_before_sync();
   __syncthreads();
   if (tid == 0) SA_TRACE(kTrMisc, 1);

@@ -105,6 +105,7 @@ class SeqShardLayer:
         self.cand_idx_all = torch.full((world, B, kc), -1, dtype=I32, device=dev)
         self.cand_score_all = torch.full((world, B, kc), float("-inf"), dtype=F32, device=dev)
         self.sel = torch.full((B, k), -1, dtype=I32, device=dev)
+        self.selected = self.sel     # the merged selection of the last step (a view of sel or cand_idx)
         self.win_idx = torch.full((B, W), -1, dtype=I32, device=dev)
         self.lidx = torch.full((B, W + k), -1, dtype=I32, device=dev)
         self.pml = torch.zeros(B, H, 2, dtype=F32, device=dev)
@@ -153,10 +154,17 @@ class SeqShard:
         self.status = torch.zeros(1, dtype=I32, device=dev)
         H, D = args.n_heads, args.head_dim
         ws_attn = 0
+        # few long rows: the multi-CTA top-k (one CTA per row would idle the GPU)
+        self.use_wide = backend is None and B <= 4
+        self.wide_ws = None
         if backend is None:
             ws_attn = int(native_ops.lib().dsa_sparse_attn_workspace_size(B, 1, H, D, args.window_size + self.k))
             ws_topk = int(native_ops.lib().dsa_indexer_topk_workspace_size(B, max(self.n_local, 1), self.kc))
             self.ws = native_ops.Workspace(dev, max(ws_attn, ws_topk))
+            if self.use_wide:
+                self.wide_ws = native_ops.WideTopkWorkspace(dev)
+                self.wide_ws.get(B, max(self.n_local, 1))
+                self.wide_ws.get(B, world * self.kc)
         else:
             self.ws = None
 
@@ -177,9 +185,13 @@ class SeqShard:
             return
         o.shard_active(self.t_active, self.lo, n, out=self.t_local)
         o.indexer_score(x.iq, L.keys, x.iw, n, out=L.score, t_valid=self.t_local)
-        o.indexer_topk(L.score, self.t_local, self.kc if self.kc <= n else n, self.lo, T=n, sort_desc=False,
-                       mask_mode=1, out=L.cand_idx[:, :min(self.kc, n)], out_score=L.cand_score[:, :min(self.kc, n)],
-                       ws=self.ws)
+        kn = min(self.kc, n)
+        if self.use_wide:
+            o.topk_wide(L.score, kn, self.lo, t_active=self.t_local, T=n, mask_mode=1, out=L.cand_idx[:, :kn],
+                        out_score=L.cand_score[:, :kn], ws=self.wide_ws, status=self.status)
+        else:
+            o.indexer_topk(L.score, self.t_local, kn, self.lo, T=n, sort_desc=False, mask_mode=1,
+                           out=L.cand_idx[:, :kn], out_score=L.cand_score[:, :kn], ws=self.ws)
 
     # ---- phase 2: merge, local rows of the selection, partial attention
     def phase_attend(self, L: SeqShardLayer, x: LayerInputs) -> None:
@@ -191,11 +203,20 @@ class SeqShard:
         else:
             cs = L.cand_score_all.permute(1, 0, 2).reshape(B, G * self.kc)
             ci = L.cand_idx_all.permute(1, 0, 2).reshape(B, G * self.kc)
-        o.topk_merge(cs, ci, self.k, 0, out=L.sel)
+        if G == 1 and self.kc == self.k:
+            L.selected = L.cand_idx          # one shard: its candidates are the global top-k
+        else:
+            if self.use_wide:
+                # candidates arrive in ascending position order (rank by rank),
+                # so the lower-slot tie rule is the lower-position rule
+                o.topk_wide(cs, self.k, 0, ids=ci, mask_mode=0, out=L.sel, ws=self.wide_ws, status=self.status)
+            else:
+                o.topk_merge(cs, ci, self.k, 0, out=L.sel)
+            L.selected = L.sel
         attend_window = self.rank == self.window_rank
         if attend_window:
             o.window_indices(self.pos, W, out=L.win_idx)
-        o.shard_local_indices(L.sel, self.lo, self.hi, W, L.win_idx if attend_window else None, local_base=0,
+        o.shard_local_indices(L.selected, self.lo, self.hi, W, L.win_idx if attend_window else None, local_base=0,
                               win_base=n, out=L.lidx)
         o.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
                           L.kv_compressed(max(n, 1)) if n else L.kv[:, :1], -self.lo if n else -(1 << 30),

@@ -302,6 +302,56 @@ def indexer_topk(score: torch.Tensor, t_active: torch.Tensor, k: int, win: int, 
     return out
 
 
+class WideTopkWorkspace:
+    """Zero-initialised, grow-only workspace of dsa_topk_wide (the kernel
+    leaves it zeroed after every call)."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.buf = torch.zeros(64, dtype=torch.uint8, device=self.device)
+
+    def get(self, B: int, T: int) -> torch.Tensor:
+        need = int(lib().dsa_topk_wide_workspace_size(B, T))
+        if need > self.buf.numel():
+            self.buf = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self.buf
+
+
+def topk_wide(score: torch.Tensor, k: int, win: int, t_active: torch.Tensor | None = None, T: int | None = None,
+              ids: torch.Tensor | None = None, mask_mode: int = 1, out: torch.Tensor | None = None,
+              out_score: torch.Tensor | None = None, ws: WideTopkWorkspace | None = None,
+              status: torch.Tensor | None = None) -> torch.Tensor:
+    """Multi-CTA top-k of a few long rows (see dsa_topk_wide); output in
+    ascending position order."""
+    _need(score, "score", F32)
+    B = score.shape[0]
+    T = score.shape[1] if T is None else T
+    if score.stride(-1) != 1:
+        raise ValueError("score must have a unit stride in the last dim")
+    ld_ids = 0
+    if ids is not None:
+        _need(ids, "ids", I32)
+        if ids.stride(-1) != 1:
+            raise ValueError("ids must have a unit stride in the last dim")
+        ld_ids = ids.stride(0)
+    if t_active is not None:
+        _need(t_active, "t_active", I32)
+    if out is None:
+        out = torch.empty(B, k, dtype=I32, device=score.device)
+    if out_score is not None and out_score.stride(0) != out.stride(0):
+        raise ValueError("out and out_score must share the row stride")
+    if ws is None:
+        ws = _wide_ws.setdefault(score.device, WideTopkWorkspace(score.device))
+    buf = ws.get(B, T)
+    check(lib().dsa_topk_wide(score.data_ptr(), score.stride(0), _ptr(ids), ld_ids, _ptr(t_active), out.data_ptr(),
+                              _ptr(out_score), out.stride(0), B, T, k, win, mask_mode, buf.data_ptr(), buf.numel(),
+                              _ptr(status), _stream(score)), "topk_wide")
+    return out
+
+
+_wide_ws: dict = {}
+
+
 def topk_merge(cand_score: torch.Tensor, cand_idx: torch.Tensor, k: int, win: int,
                out: torch.Tensor | None = None, out_score: torch.Tensor | None = None) -> torch.Tensor:
     """Global top-k from concatenated per-shard candidate lists."""
