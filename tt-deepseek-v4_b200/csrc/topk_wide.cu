@@ -11,12 +11,16 @@
 //
 // One cooperative launch, grid (cpr, B): each CTA owns a contiguous slice of
 // its row, keys (order-preserving uint32 of the masked value) in registers.
-// An MSD radix select over 12 + 12 + 8 bits finds the k-th largest key: per
-// level every CTA histograms its live keys into a global per-row histogram,
-// a grid barrier, then every CTA scans the histogram to the bin holding the
-// k-th key.  A last barrier exchanges per-CTA counts of keys above / equal
-// to the threshold, which gives each CTA its output offset, so the result
-// is written in position order with no atomics on the output.  Grid
+// MSD radix select: every CTA histograms the top 12 bits of its keys into a
+// global per-row histogram; after a grid barrier every CTA scans it to the
+// bin holding the k-th key.  Each CTA then publishes its count of keys above
+// that bin and its keys in it (at most kCap, in position order); after a
+// second barrier every CTA loads all published bin keys (a few hundred for
+// continuous scores) and finishes the select on their low 20 bits in shared
+// memory.  The per-CTA counts give each CTA its output offset, so the result
+// is written in position order with no atomics on the output.  A crowded bin
+// (some CTA holding more than kCap of its keys: ties, quantised scores) takes
+// two more grid-wide 12/8-bit levels and a count exchange instead.  Grid
 // barriers are an arrival count plus a generation word with a clock-bounded
 // spin; a wait that runs out sets *status and the CTA returns.  The
 // histograms are zeroed again at the end of the launch, so the workspace must be zeroed once
@@ -32,9 +36,13 @@ constexpr int kLevels = 3;
 constexpr int kMaxPerThread = 8;
 constexpr long long kSpinCycles = 2000000000ll;  // ~1 s at 1.9 GHz
 constexpr int kStatusTimeout = 2;
+constexpr int kCap = 24;                 // level-0 bin keys one CTA may publish
+constexpr int kMaxCtasPerRow = 148;
+constexpr int kCandSmem = kCap * kMaxCtasPerRow;
 
 struct RowWs {
   uint32_t hist[kLevels][kBins];
+  uint32_t bar[4];  // this row's grid barrier: arrival count, generation
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
@@ -42,81 +50,98 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
-// Grid-wide barrier over all nctas CTAs of the launch (sense by generation:
+// Barrier over the nctas CTAs of one row (sense by generation:
 // the last CTA to arrive resets the count, then bumps the generation), so
-// launches of any grid size can share one workspace.  False on timeout.
+// launches of any grid size can share one workspace.  Thread 0 arrives with
+// release semantics after the CTA's __syncthreads, which orders the whole
+// CTA's prior writes; waiters poll the generation with acquire loads.
+// False on timeout.
 __device__ bool grid_barrier(uint32_t* bar, unsigned nctas, int32_t* status, volatile int* s_ok) {
   uint32_t* count = bar;
   uint32_t* gen = bar + 1;
-  __threadfence();  // this thread's histogram / count writes before the arrival
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint32_t g = ld_acquire_u32(gen);
-    __threadfence();
-    const uint32_t old = atomicAdd(count, 1u);
+    const uint32_t old = atom_add_acq_rel(count, 1u);
     int ok = 1;
     if (old == nctas - 1) {
       atomicExch(count, 0u);
-      __threadfence();
-      atomicAdd(gen, 1u);
+      atom_add_acq_rel(gen, 1u);
     } else {
       const long long t0 = clock64();
+      int polls = 0;
       while (ld_acquire_u32(gen) == g) {
+        if (++polls > 256) __nanosleep(32);
         if (clock64() - t0 > kSpinCycles) {
           ok = 0;
           if (status) atomicOr(status, kStatusTimeout);
           break;
         }
-        __nanosleep(64);
       }
     }
-    __threadfence();
     *s_ok = ok;
   }
   __syncthreads();
   return *s_ok != 0;
 }
 
-// Block-wide: find the bin d (scanning from the top) where the running count
-// of higher bins first reaches `need`.  Returns d and sets *above to the
-// count in bins above d.
-__device__ int find_bin(const uint32_t* hist, uint32_t need, uint32_t* above, uint32_t* s_part, int* s_res,
-                        uint32_t* s_above) {
-  constexpr int kPer = kBins / kThreads;  // 8 bins per thread, thread 0 the top bins
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t h[kPer], tot = 0;
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    h[i] = __ldcg(hist + (kBins - 1 - (tid * kPer + i)));
-    tot += h[i];
-  }
-  // exclusive scan of tot over threads (descending bin order)
-  uint32_t incl = tot;
+// Block-wide exclusive scan of one value per thread (thread order); returns
+// the exclusive prefix and writes the block total to *total.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* s_w, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  uint32_t inc = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
+    const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
   }
-  if (lane == 31) s_part[warp] = incl;
+  if (lane == 31) s_w[warp] = inc;
   __syncthreads();
   if (warp == 0) {
-    uint32_t w = lane < kThreads / 32 ? s_part[lane] : 0;
+    const uint32_t w = lane < nw ? s_w[lane] : 0;
     uint32_t wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += v;
+      const uint32_t t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
     }
-    if (lane < kThreads / 32) s_part[lane] = wi - w;  // exclusive warp offsets
+    if (lane < nw) s_w[lane] = wi - w;
+    if (lane == nw - 1) s_w[32] = wi;
   }
   __syncthreads();
-  uint32_t run = s_part[warp] + incl - tot;  // count in bins above this thread's first bin
+  const uint32_t r = s_w[warp] + inc - v;
+  *total = s_w[32];
+  __syncthreads();
+  return r;
+}
+
+// Block-wide: find the bin d (scanning from the top of nbins) where the
+// running count of higher bins first reaches `need`; *above = the count in
+// bins above d.  hist is global (L2) or shared memory.
+template <int kPer, bool kGlobal>
+__device__ int find_bin(const uint32_t* hist, int nbins, uint32_t need, uint32_t* above, uint32_t* s_w,
+                        int* s_res, uint32_t* s_above) {
+  const int tid = threadIdx.x;
+  uint32_t h[kPer], tot = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int bin = nbins - 1 - (tid * kPer + i);
+    h[i] = bin >= 0 ? (kGlobal ? __ldcg(hist + bin) : hist[bin]) : 0u;
+    tot += h[i];
+  }
+  uint32_t all;
+  uint32_t run = block_excl_scan(tot, s_w, &all);
   if (run < need && run + tot >= need) {
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       if (run < need && run + h[i] >= need) {
-        *s_res = kBins - 1 - (tid * kPer + i);
+        *s_res = nbins - 1 - (tid * kPer + i);
         *s_above = run;
       }
       run += h[i];
@@ -129,19 +154,24 @@ __device__ int find_bin(const uint32_t* hist, uint32_t need, uint32_t* above, ui
   return d;
 }
 
+// per-row counters: [0] keys above the level-0 bin, [1] keys in it, [2] keys
+// above the final threshold, [3] keys equal to it (overflow path)
+constexpr int kCountWords = 4;
+
 __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
     const float* __restrict__ score, int64_t ld_score, const int32_t* __restrict__ ids, int64_t ld_ids,
     const int32_t* __restrict__ t_active, int T, int k, int win, int mask_mode, int per_cta,
     int32_t* __restrict__ out_idx, float* __restrict__ out_score, int64_t ld_out, RowWs* __restrict__ rows,
-    uint32_t* __restrict__ counts, uint32_t* __restrict__ bar, int32_t* __restrict__ status) {
+    uint32_t* __restrict__ counts, unsigned long long* __restrict__ cands, int32_t* __restrict__ status) {
   __shared__ uint32_t s_hist[kBins];
-  __shared__ uint32_t s_part[kThreads / 32];
+  __shared__ unsigned long long s_cand[kCandSmem];
+  __shared__ uint32_t s_w[33];
+  __shared__ uint32_t s_coff[kMaxCtasPerRow + 1];
   __shared__ int s_res;
   __shared__ uint32_t s_above;
   __shared__ int s_ok;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int b = blockIdx.y, c = blockIdx.x, cpr = gridDim.x;
-  const unsigned nctas = gridDim.x * gridDim.y;
   const int s0 = c * per_cta;
   const int s1 = min(T, s0 + per_cta);
   const int ept = (per_cta + kThreads - 1) / kThreads;  // elements per thread (<= kMaxPerThread)
@@ -149,6 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
   const int ta = t_active ? t_active[b] : T;
   const float* srow = score + int64_t(b) * ld_score;
   const int32_t* irow = ids ? ids + int64_t(b) * ld_ids : nullptr;
+  RowWs* rw = rows + b;
+  uint32_t* bar = rw->bar;  // rows are independent: each synchronises only its own CTAs
+  const unsigned nctas = cpr;
+  uint32_t* crow = counts + int64_t(b) * cpr * kCountWords;
+  unsigned long long* cand_row = cands + int64_t(b) * cpr * kCap;
 
   uint32_t key[kMaxPerThread];
 #pragma unroll
@@ -167,134 +202,225 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
       key[i] = float_key(v);
     }
   }
+  auto live = [&](int i) { return i < ept && e0 + i < s1; };
 
-  RowWs* rw = rows + b;
-  uint32_t prefix = 0, pmask = 0, need = uint32_t(k);
+  // ---- level 0: top 12 bits over the whole row
+  for (int i = tid; i < kBins; i += kThreads) s_hist[i] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kMaxPerThread; ++i)
+    if (live(i)) atomicAdd(&s_hist[key[i] >> 20], 1u);
+  __syncthreads();
+  for (int i = tid; i < kBins; i += kThreads)
+    if (s_hist[i]) atomicAdd(&rw->hist[0][i], s_hist[i]);
+  if (!grid_barrier(bar, nctas, status, &s_ok)) return;
+  uint32_t above;
+  const uint32_t d0 = find_bin<kBins / kThreads, true>(rw->hist[0], kBins, uint32_t(k), &above, s_w, &s_res,
+                                                       &s_above);
+  uint32_t need = uint32_t(k) - above;  // keys still to take from bin d0
+
+  // ---- exchange: per CTA the keys above bin d0, and the keys in it
+  uint32_t n_gt = 0, n_in = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxPerThread; ++i) {
+    if (live(i)) {
+      n_gt += (key[i] >> 20) > d0;
+      n_in += (key[i] >> 20) == d0;
+    }
+  }
+  uint32_t cta_gt, cta_in;
+  (void)block_excl_scan(n_gt, s_w, &cta_gt);
+  const uint32_t in_base = block_excl_scan(n_in, s_w, &cta_in);  // this thread's first in-bin slot
+  if (tid == 0) {
+    crow[kCountWords * c + 0] = cta_gt;
+    crow[kCountWords * c + 1] = cta_in;
+  }
+  if (cta_in <= uint32_t(kCap)) {
+    uint32_t slot = in_base;
+#pragma unroll
+    for (int i = 0; i < kMaxPerThread; ++i) {
+      if (live(i) && (key[i] >> 20) == d0) {
+        cand_row[int64_t(c) * kCap + slot] = (uint64_t(key[i]) << 32) | uint32_t(e0 + i - s0);
+        ++slot;
+      }
+    }
+  }
+  if (!grid_barrier(bar, nctas, status, &s_ok)) return;
+  // level-0 histogram: every CTA read it before the barrier above
+  for (int i = c * kThreads + tid; i < kBins; i += cpr * kThreads) rw->hist[0][i] = 0u;
+
+  // the row's per-CTA counts: offsets of this CTA and the overflow test
+  uint32_t my_gt = 0, my_in = 0, over = 0;
+  if (tid < cpr) {
+    my_gt = __ldcg(crow + kCountWords * tid + 0);
+    my_in = __ldcg(crow + kCountWords * tid + 1);
+    over = my_in > uint32_t(kCap);
+  }
+  over = __syncthreads_or(over);
+  uint32_t tot_in;
+  const uint32_t in_off = block_excl_scan(tid < cpr ? my_in : 0u, s_w, &tot_in);  // candidates before CTA tid
+  if (tid < cpr) s_coff[tid] = in_off;
+  if (tid == 0) s_coff[cpr] = tot_in;
+  uint32_t gt_all;
+  const uint32_t gt_off = block_excl_scan(tid < cpr ? my_gt : 0u, s_w, &gt_all);
+  if (tid == c) s_above = gt_off;
+  __syncthreads();
+  const uint32_t gt_before = s_above;  // keys above bin d0 in the CTAs before this one
+
+  int32_t* orow = out_idx + int64_t(b) * ld_out;
+  float* osrow = out_score ? out_score + int64_t(b) * ld_out : nullptr;
+  auto emit = [&](uint32_t out_pos, uint32_t kk, int t) {
+    if (out_pos < uint32_t(k)) {  // holds unless the histograms were not zeroed
+      const float v = key_float(kk);
+      const int id = irow ? irow[t] : t;
+      orow[out_pos] = (v >= -1000.f && id >= 0) ? id + win : -1;
+      if (osrow) osrow[out_pos] = v;
+    }
+  };
+
+  if (!over && tot_in <= uint32_t(kCandSmem)) {
+    // ---- fast path: select `need` of the tot_in bin-d0 keys in every CTA
+    for (int j = tid; j < cpr; j += kThreads) {
+      const uint32_t o = s_coff[j], n = s_coff[j + 1] - o;
+      for (uint32_t q = 0; q < n; ++q) s_cand[o + q] = __ldcg(cand_row + int64_t(j) * kCap + q);
+    }
+    __syncthreads();
+    // two 10-bit passes over the low 20 bits, in shared memory
+    uint32_t prefix = d0 << 20, pmask = 0xfff00000u;
 #pragma unroll 1
-  for (int level = 0; level < kLevels; ++level) {
-    const int shift = level == 0 ? 20 : (level == 1 ? 8 : 0);
-    const uint32_t dmask = level == 2 ? 0xffu : 0xfffu;
+    for (int pass = 0; pass < 2; ++pass) {
+      const int shift = pass == 0 ? 10 : 0;
+      for (int i = tid; i < 1024; i += kThreads) s_hist[i] = 0;
+      __syncthreads();
+      for (uint32_t j = tid; j < tot_in; j += kThreads) {
+        const uint32_t kk = uint32_t(s_cand[j] >> 32);
+        if ((kk & pmask) == prefix) atomicAdd(&s_hist[(kk >> shift) & 0x3ffu], 1u);
+      }
+      __syncthreads();
+      uint32_t ab;
+      const uint32_t dd = find_bin<2, false>(s_hist, 1024, need, &ab, s_w, &s_res, &s_above);
+      need -= ab;
+      prefix |= dd << shift;
+      pmask |= 0x3ffu << shift;
+    }
+    const uint32_t thr = prefix;  // the k-th largest key; `need` keys equal to it are taken
+    // selection flags of the candidates, in position order: > thr, or the
+    // first `need` equal to thr; count the selected ones before this CTA
+    const uint32_t per = (tot_in + kThreads - 1) / kThreads;
+    const uint32_t j0 = tid * per, j1 = min(tot_in, j0 + per);
+    uint32_t n_eq = 0;
+    for (uint32_t j = j0; j < j1; ++j) n_eq += uint32_t(s_cand[j] >> 32) == thr;
+    uint32_t eq_tot;
+    uint32_t eq_before = block_excl_scan(n_eq, s_w, &eq_tot);
+    const uint32_t my0 = s_coff[c];
+    uint32_t sel_before = 0;  // selected candidates before this CTA's own
+    for (uint32_t j = j0; j < j1; ++j) {
+      const uint32_t kk = uint32_t(s_cand[j] >> 32);
+      bool sel = kk > thr;
+      if (kk == thr) {
+        sel = eq_before < need;
+        ++eq_before;
+      }
+      // mark the selection in bit 31 of the entry's position word (positions are < 2^13)
+      if (sel) s_cand[j] |= 0x80000000ull;
+      if (sel && j < my0) ++sel_before;
+    }
+    uint32_t sel_tot;  // selected candidates before this CTA's own (summed over threads)
+    (void)block_excl_scan(sel_before, s_w, &sel_tot);
+    const uint32_t cta_base = gt_before + sel_tot;
+    // this thread's outputs in position order
+    uint32_t n_sel = 0;
+    uint32_t slot = my0 + in_base;
+#pragma unroll
+    for (int i = 0; i < kMaxPerThread; ++i) {
+      if (live(i)) {
+        const uint32_t dg = key[i] >> 20;
+        if (dg > d0) {
+          ++n_sel;
+        } else if (dg == d0) {
+          n_sel += (s_cand[slot] & 0x80000000ull) ? 1u : 0u;
+          ++slot;
+        }
+      }
+    }
+    uint32_t cta_sel;
+    uint32_t out_pos = cta_base + block_excl_scan(n_sel, s_w, &cta_sel);
+    slot = my0 + in_base;
+#pragma unroll
+    for (int i = 0; i < kMaxPerThread; ++i) {
+      if (live(i)) {
+        const uint32_t dg = key[i] >> 20;
+        bool take = dg > d0;
+        if (dg == d0) {
+          take = (s_cand[slot] & 0x80000000ull) != 0;
+          ++slot;
+        }
+        if (take) emit(out_pos++, key[i], e0 + i);
+      }
+    }
+    return;
+  }
+
+  // ---- overflow path (a crowded level-0 bin): two more levels grid-wide
+  uint32_t prefix = d0 << 20, pmask = 0xfff00000u;
+#pragma unroll 1
+  for (int level = 1; level < kLevels; ++level) {
+    const int shift = level == 1 ? 8 : 0;
+    const uint32_t dmask = level == 1 ? 0xfffu : 0xffu;
     for (int i = tid; i < kBins; i += kThreads) s_hist[i] = 0;
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < kMaxPerThread; ++i)
-      if (i < ept && e0 + i < s1 && (key[i] & pmask) == prefix) atomicAdd(&s_hist[(key[i] >> shift) & dmask], 1u);
+      if (live(i) && (key[i] & pmask) == prefix) atomicAdd(&s_hist[(key[i] >> shift) & dmask], 1u);
     __syncthreads();
     for (int i = tid; i < kBins; i += kThreads)
       if (s_hist[i]) atomicAdd(&rw->hist[level][i], s_hist[i]);
     if (!grid_barrier(bar, nctas, status, &s_ok)) return;
-    uint32_t above;
-    const int d = find_bin(rw->hist[level], need, &above, s_part, &s_res, &s_above);
-    need -= above;
-    prefix |= uint32_t(d) << shift;
+    uint32_t ab;
+    const uint32_t dd = find_bin<kBins / kThreads, true>(rw->hist[level], kBins, need, &ab, s_w, &s_res, &s_above);
+    need -= ab;
+    prefix |= dd << shift;
     pmask |= dmask << shift;
   }
-  const uint32_t thr = prefix;  // the k-th largest key; `need` of the keys equal to it are taken
-
-  // per-thread counts above / equal, then per-CTA totals to the global table
-  uint32_t n_gt = 0, n_eq = 0;
+  const uint32_t thr = prefix;
+  uint32_t g2 = 0, q2 = 0;
 #pragma unroll
   for (int i = 0; i < kMaxPerThread; ++i) {
-    if (i < ept && e0 + i < s1) {
-      n_gt += key[i] > thr;
-      n_eq += key[i] == thr;
+    if (live(i)) {
+      g2 += key[i] > thr;
+      q2 += key[i] == thr;
     }
   }
-  // block exclusive scans of n_gt and n_eq (thread order = position order)
-  uint32_t ig = n_gt, ie = n_eq;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t vg = __shfl_up_sync(0xffffffffu, ig, o), ve = __shfl_up_sync(0xffffffffu, ie, o);
-    if (lane >= o) {
-      ig += vg;
-      ie += ve;
-    }
-  }
-  __shared__ uint32_t s_wg[kThreads / 32], s_we[kThreads / 32], s_tot[2];
-  if (lane == 31) {
-    s_wg[warp] = ig;
-    s_we[warp] = ie;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t g = lane < kThreads / 32 ? s_wg[lane] : 0, e = lane < kThreads / 32 ? s_we[lane] : 0;
-    uint32_t gi = g, ei = e;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t vg = __shfl_up_sync(0xffffffffu, gi, o), ve = __shfl_up_sync(0xffffffffu, ei, o);
-      if (lane >= o) {
-        gi += vg;
-        ei += ve;
-      }
-    }
-    if (lane < kThreads / 32) {
-      s_wg[lane] = gi - g;
-      s_we[lane] = ei - e;
-    }
-    if (lane == kThreads / 32 - 1) {
-      s_tot[0] = gi;
-      s_tot[1] = ei;
-    }
-  }
-  __syncthreads();
-  const uint32_t thr_gt = s_wg[warp] + ig - n_gt, thr_eq = s_we[warp] + ie - n_eq;
-  uint32_t* crow = counts + int64_t(b) * cpr * 2;
+  uint32_t cg2, cq2;
+  const uint32_t tg = block_excl_scan(g2, s_w, &cg2);
+  const uint32_t tq = block_excl_scan(q2, s_w, &cq2);
   if (tid == 0) {
-    crow[2 * c] = s_tot[0];
-    crow[2 * c + 1] = s_tot[1];
+    crow[kCountWords * c + 2] = cg2;
+    crow[kCountWords * c + 3] = cq2;
   }
   if (!grid_barrier(bar, nctas, status, &s_ok)) return;
-  // offsets of this CTA: selected elements of the CTAs before it
-  uint32_t cg = 0, ce = 0;
-  for (int j = tid; j < c; j += kThreads) {
-    cg += __ldcg(crow + 2 * j);
-    ce += __ldcg(crow + 2 * j + 1);
+  for (int i = c * kThreads + tid; i < (kLevels - 1) * kBins; i += cpr * kThreads) (&rw->hist[1][0])[i] = 0u;
+  uint32_t pg = 0, pq = 0;
+  if (tid < c) {
+    pg = __ldcg(crow + kCountWords * tid + 2);
+    pq = __ldcg(crow + kCountWords * tid + 3);
   }
-  cg = __reduce_add_sync(0xffffffffu, cg);
-  ce = __reduce_add_sync(0xffffffffu, ce);
-  if (lane == 0) {
-    s_wg[warp] = cg;
-    s_we[warp] = ce;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    uint32_t a = 0, e = 0;
-    for (int w = 0; w < kThreads / 32; ++w) {
-      a += s_wg[w];
-      e += s_we[w];
-    }
-    s_tot[0] = a;
-    s_tot[1] = e;
-  }
-  __syncthreads();
-  const uint32_t cta_gt = s_tot[0], cta_eq = s_tot[1];
-  // selected before this thread = gt before it + min(eq before it, need)
-  uint32_t eq_before = cta_eq + thr_eq;
-  uint32_t out_pos = cta_gt + thr_gt + min(eq_before, need);
-  int32_t* orow = out_idx + int64_t(b) * ld_out;
-  float* osrow = out_score ? out_score + int64_t(b) * ld_out : nullptr;
+  uint32_t before_g, before_q;
+  (void)block_excl_scan(pg, s_w, &before_g);
+  (void)block_excl_scan(pq, s_w, &before_q);
+  uint32_t eq_before = before_q + tq;
+  uint32_t out_pos = before_g + tg + min(eq_before, need);
 #pragma unroll
   for (int i = 0; i < kMaxPerThread; ++i) {
-    const int t = e0 + i;
-    if (i < ept && t < s1) {
+    if (live(i)) {
       bool take = key[i] > thr;
       if (key[i] == thr) {
         take = eq_before < need;
         ++eq_before;
       }
-      if (take && out_pos < uint32_t(k)) {  // bound holds unless the histograms were not zeroed
-        const float v = key_float(key[i]);
-        const int id = irow ? irow[t] : t;
-        orow[out_pos] = (v >= -1000.f && id >= 0) ? id + win : -1;
-        if (osrow) osrow[out_pos] = v;
-        ++out_pos;
-      }
+      if (take) emit(out_pos++, key[i], e0 + i);
     }
   }
-  // every CTA has read the histograms (before the count barrier): clear them
-  // for the next launch
-  for (int i = c * kThreads + tid; i < kLevels * kBins; i += cpr * kThreads)
-    (&rw->hist[0][0])[i] = 0u;
 }
 
 }  // namespace wide
@@ -316,7 +442,8 @@ int wide_ctas_per_row(int B, int T) {
 extern "C" size_t dsa_topk_wide_workspace_size(int B, int T) {
   if (B <= 0 || T <= 0) return 0;
   const int cpr = wide_ctas_per_row(B, T);
-  return 64 + size_t(B) * sizeof(wide::RowWs) + size_t(B) * cpr * 2 * sizeof(uint32_t);
+  return 64 + size_t(B) * sizeof(wide::RowWs) + size_t(B) * cpr * wide::kCountWords * sizeof(uint32_t) +
+         size_t(B) * cpr * wide::kCap * sizeof(unsigned long long);
 }
 
 extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t* ids, int64_t ld_ids,
@@ -335,16 +462,17 @@ extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t
     return DSA_ERR_WORKSPACE;
   }
   const int cpr = wide_ctas_per_row(B, T);
-  if (int64_t(cpr) * B > num_sms()) {
+  if (int64_t(cpr) * B > num_sms() || cpr > wide::kMaxCtasPerRow) {
     set_error("topk_wide: %d rows x %d CTAs exceed one CTA per SM (%d SMs); use dsa_indexer_topk", B, cpr,
               num_sms());
     return DSA_ERR_UNSUPPORTED;
   }
   const int per_cta = (T + cpr - 1) / cpr;
   auto* base = static_cast<uint8_t*>(workspace);
-  auto* bar = reinterpret_cast<uint32_t*>(base);
   auto* rows = reinterpret_cast<wide::RowWs*>(base + 64);
   auto* counts = reinterpret_cast<uint32_t*>(base + 64 + size_t(B) * sizeof(wide::RowWs));
+  auto* cands = reinterpret_cast<unsigned long long*>(base + 64 + size_t(B) * sizeof(wide::RowWs) +
+                                                      size_t(B) * cpr * wide::kCountWords * sizeof(uint32_t));
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cpr, B);
@@ -357,7 +485,7 @@ extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, wide::topk_wide_kernel, score, ld_score, ids, ld_ids, t_active, T, k, win,
-                                     mask_mode, per_cta, out_idx, out_score, ld_out, rows, counts, bar, status);
+                                     mask_mode, per_cta, out_idx, out_score, ld_out, rows, counts, cands, status);
   if (e != cudaSuccess) {
     set_error("topk_wide: launch failed: %s", cudaGetErrorString(e));
     return DSA_ERR_CUDA;
