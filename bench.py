@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel timings to stderr")
     ap.add_argument("--workload", choices=["cfg2", "cfg3"], default="cfg2",
                     help="cfg2: batched decode, batch split; cfg3: one 256k context, sequence split")
+    ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p",
+                    help="cfg3 exchanges: peer-memory stores over NVLink, or NCCL all-gathers")
     a = ap.parse_args()
     if a.workload == "cfg3" and "--ctx" not in sys.argv:
         a.ctx = 262144
@@ -411,10 +413,19 @@ def main():
 
 
 class _SelfComm:
-    """World of one: the all-gather is a copy."""
+    """World of one: the exchange is a copy."""
 
-    def all_gather(self, out, inp):
-        out[0].copy_(inp)
+    def exchange(self, L, phase):
+        if phase == 0:
+            L.cand_all[0].copy_(L.cand)
+        else:
+            L.part_all[0].copy_(L.part)
+
+    def end_step(self):
+        pass
+
+    def close(self):
+        pass
 
 
 def run_cfg3(args, rank, world, dev):
@@ -425,14 +436,16 @@ def run_cfg3(args, rank, world, dev):
     of all layers.  "scaling": "strong" (the context is fixed as N grows)."""
     import torch
     import torch.distributed as dist
-    from dsv4attn.dist import SeqShard, SeqSplitPath, TorchDistComm
+    from dsv4attn.dist import P2PComm, SeqShard, SeqSplitPath, TorchDistComm
     from dsv4attn.layer import LayerInputs
     from dsv4attn.tables import PathArgs
     pa = PathArgs(index_topk=args.topk)
     T_total = args.ctx // 4
     max_seq = args.ctx + 4096
     log(f"cfg3: building {args.layers} sharded layers (T={T_total}, rank {rank}/{world})")
-    shard = SeqShard(pa, 1, T_total, rank, world, dev, k=args.topk, n_layers=args.layers, max_seq_len=max_seq)
+    p2p = world > 1 and args.comm == "p2p"
+    shard = SeqShard(pa, 1, T_total, rank, world, dev, k=args.topk, n_layers=args.layers, max_seq_len=max_seq,
+                     peer_exchange=p2p)
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     for L in shard.layers:
         L.kv.normal_(generator=g)
@@ -450,7 +463,7 @@ def run_cfg3(args, rank, world, dev):
         x.iw.mul_(0.02)
         inputs.append(x)
     outs = [torch.empty(1, 64, 512, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
-    comm = TorchDistComm() if world > 1 else _SelfComm()
+    comm = (P2PComm(shard) if p2p else TorchDistComm()) if world > 1 else _SelfComm()
     path = SeqSplitPath(shard, comm)
     shard.set_positions(args.ctx - 1)
     torch.cuda.synchronize()
@@ -525,7 +538,9 @@ def run_cfg3(args, rank, world, dev):
             "config": {"workload": f"cfg3 long-context decode: batch 1, ctx {args.ctx} ({T_total} compressed), "
                                    f"top-{k} + window {W}, {args.layers} layers, sequence split over {world} GPU(s)",
                        "global_batch": 1, "seq_len": args.ctx, "layers": args.layers,
-                       "parallelism": f"sequence split x{world} (NCCL all-gather of candidates and partials)",
+                       "parallelism": f"sequence split x{world} ("
+                                      + ("peer-memory exchange over NVLink" if p2p else
+                                         ("NCCL all-gather" if world > 1 else "no exchange")) + ")",
                        "timing": mode},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm * world, "unit": "GB/s",
                          "frac": round(gbs / (hbm * world), 4), "traffic": None,
@@ -537,6 +552,9 @@ def run_cfg3(args, rank, world, dev):
     if world > 1:
         dist.barrier()
         del graph
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
         dist.destroy_process_group()
 
 

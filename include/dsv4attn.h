@@ -192,6 +192,9 @@ int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_a
  * with grid-wide barriers, for rows too long / too few for one CTA each
  * (the sequence split's single context).  Same masking, validity, tie and
  * win rules as dsa_indexer_topk; output in ascending position order.
+ * seg_len > 0: each row is T / seg_len segments of seg_len elements placed
+ * seg_stride elements apart (score and ids alike; the per-rank lists of an
+ * all-gather), else contiguous.
  * ids (may be NULL): [B, T] int32 - the output then carries ids[t] + win
  * and slots with ids[t] < 0 count as -inf (the candidate merge of the split;
  * ties break towards the lower slot, so pass candidates in position order).
@@ -204,8 +207,8 @@ int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_a
 size_t dsa_topk_wide_workspace_size(int B, int T);
 int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t* ids, int64_t ld_ids,
                   const int32_t* t_active, int32_t* out_idx, float* out_score, int64_t ld_out,
-                  int B, int T, int k, int win, int mask_mode, void* workspace,
-                  size_t workspace_bytes, int32_t* status, dsa_stream_t stream);
+                  int B, int T, int k, int win, int mask_mode, int seg_len, int64_t seg_stride,
+                  void* workspace, size_t workspace_bytes, int32_t* status, dsa_stream_t stream);
 
 /* Device-side position advance for graph-replayed decode: pos[b] += step;
  * t_active[b] = (pos[b] + 1) / ratio (T_active of inference.py:6028; may
@@ -242,6 +245,36 @@ int dsa_shard_active(const int32_t* t_active, int32_t* t_local, int B, int lo, i
 int dsa_shard_local_indices(const int32_t* sel, int64_t ld_sel, int k, const int32_t* win_idx,
                             int64_t ld_win, int W, int lo, int hi, int local_base, int win_base,
                             int32_t* out, int64_t ld_out, int B, dsa_stream_t stream);
+
+/* Peer-memory exchange (the sequence split's all-gathers over NVLink).
+ * dsa_p2p_export: CUDA IPC handle (dsa_p2p_handle_size() bytes) of the
+ *   allocation holding ptr, and ptr's byte offset in it; dsa_p2p_import
+ *   maps a peer's handle (add the offset), dsa_p2p_close unmaps it.
+ *   dsa_p2p_alloc / dsa_p2p_free: a zeroed cudaMalloc buffer (set-up only;
+ *   the hot calls below allocate nothing).
+ * dsa_p2p_publish: copy `bytes` (multiple of 16) from src to the G device
+ *   addresses dst_ptrs[g] (device array; peers' receive slots, one may be
+ *   local), then release-store *epoch into the G flags flag_ptrs[g] once all
+ *   of that destination's stores are visible system-wide.  done: G local
+ *   zero-initialised counters (left zeroed).
+ * dsa_p2p_wait: wait (acquire, bounded ~1 s; a timeout sets status bit 2)
+ *   until flags[i] >= *epoch for all i < G.
+ * dsa_counter_bump: *counter += 1 on the device (the per-step epoch).
+ * Replaces the ttnn.all_gather / all_reduce collectives the reference's
+ * multi-device path issues (inference.py:5274-5275) for the split of
+ * briefs/future_max_utilization.md:177-204. */
+int dsa_p2p_alloc(size_t bytes, void** ptr);
+int dsa_p2p_free(void* ptr);
+size_t dsa_p2p_handle_size(void);
+int dsa_p2p_export(void* ptr, void* handle, uint64_t* offset);
+int dsa_p2p_import(const void* handle, void** ptr);
+int dsa_p2p_close(void* ptr);
+int dsa_p2p_publish(const void* src, size_t bytes, const unsigned long long* dst_ptrs,
+                    const unsigned long long* flag_ptrs, const uint32_t* epoch, int G,
+                    uint32_t* done, dsa_stream_t stream);
+int dsa_p2p_wait(const uint32_t* flags, int G, const uint32_t* epoch, int32_t* status,
+                 dsa_stream_t stream);
+int dsa_counter_bump(uint32_t* counter, dsa_stream_t stream);
 
 /* ------------------------------------------------------------ attn.sparse */
 
@@ -307,6 +340,12 @@ int dsa_sparse_attn_partial(const void* q, const void* kv, int64_t kv_bstride,
  * part_o and out 16-byte aligned. */
 int dsa_lse_combine(const float* part_ml, const float* part_o, const float* sink,
                     void* out, int P, int M, int H, int D, dsa_stream_t stream);
+/* dsa_lse_combine with the P partials ml_pstride / o_pstride floats apart
+ * (o_pstride a multiple of 4): partials packed one rank after another in
+ * one all-gathered buffer. */
+int dsa_lse_combine_strided(const float* part_ml, int64_t ml_pstride, const float* part_o,
+                            int64_t o_pstride, const float* sink, void* out, int P, int M,
+                            int H, int D, dsa_stream_t stream);
 
 /* --------------------------------------------------------------- tracing */
 

@@ -109,6 +109,12 @@ class OracleOps:
         return out
 
     @staticmethod
+    def lse_combine_strided(part_ml, ml_pstride, part_o, o_pstride, P, M, H, D, sink, out):
+        ml = torch.stack([part_ml[p * ml_pstride:p * ml_pstride + M * H * 2].view(M, H, 2) for p in range(P)])
+        o = torch.stack([part_o[p * o_pstride:p * o_pstride + M * H * D].view(M, H, D) for p in range(P)])
+        return OracleOps.lse_combine(ml, o, sink, out=out)
+
+    @staticmethod
     def advance_positions(pos, t_active, ratio, step=1):
         pos += step
         if t_active is not None:

@@ -91,3 +91,24 @@ def test_topk_wide_merge_mode_equals_topk_merge(cuda_dev):
     want = ops.topk_merge(cs, ci, k, 128)
     torch.cuda.synchronize()
     assert sorted(got[0].tolist()) == sorted(want[0].tolist())
+
+
+def test_topk_wide_segmented_rows_equal_contiguous(cuda_dev):
+    """A row read as G segments seg_stride apart (the rank-major all-gather
+    of [scores | ids] lists) selects what the contiguous row selects."""
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(9)
+    G, B, kc, k = 4, 2, 512, 700
+    blocks = []
+    sc = torch.randn(G, B, kc, generator=g)
+    ix = torch.arange(G * kc, dtype=torch.int32).view(G, 1, kc).expand(G, B, kc).contiguous()
+    for r in range(G):
+        blocks.append(torch.cat([sc[r].reshape(-1).view(torch.int32), ix[r].reshape(-1)]))
+    flat = torch.stack(blocks).to(cuda_dev).view(-1)
+    got = ops.topk_wide(flat.view(torch.float32), k, 3, ids=flat[B * kc:], mask_mode=0, seg_len=kc,
+                        seg_stride=2 * B * kc, B=B, T=G * kc, ld_score=kc)
+    cs = sc.permute(1, 0, 2).reshape(B, G * kc).to(cuda_dev)
+    ci = ix.permute(1, 0, 2).reshape(B, G * kc).to(cuda_dev)
+    want = ops.topk_wide(cs, k, 3, ids=ci, mask_mode=0)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)

@@ -285,12 +285,12 @@ constexpr int kCombineWarps = 8;
 template <int DPL>
 __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
     const float* __restrict__ part_ml, const float* __restrict__ part_o, const float* __restrict__ sink, int P, int M,
-    int H, int D, int final_mode, __nv_bfloat16* __restrict__ out, float* __restrict__ lse, float* __restrict__ out_ml,
-    float* __restrict__ out_o) {
+    int H, int D, int64_t ml_ps, int64_t o_ps, int final_mode, __nv_bfloat16* __restrict__ out,
+    float* __restrict__ lse, float* __restrict__ out_ml, float* __restrict__ out_o) {
   const int m = blockIdx.x, lane = threadIdx.x & 31;
   const int h = blockIdx.y * kCombineWarps + (threadIdx.x >> 5);
   if (h >= H) return;
-  auto ml = [&](int p, int j) { return part_ml[((int64_t(p) * M + m) * H + h) * 2 + j]; };
+  auto ml = [&](int p, int j) { return part_ml[int64_t(p) * ml_ps + (int64_t(m) * H + h) * 2 + j]; };
   float Mx = final_mode ? sink[h] : -INFINITY;
   for (int p0 = 0; p0 < P; p0 += 32) {
     const float mp = p0 + lane < P ? ml(p0 + lane, 0) : -INFINITY;
@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
   for (int p = 0; p < P; ++p) {
     const float mp = ml(p, 0);
     const float w = (mp == -INFINITY) ? 0.f : expf(mp - Mx);
-    const float4* src = reinterpret_cast<const float4*>(part_o + ((int64_t(p) * M + m) * H + h) * D + d0);
+    const float4* src = reinterpret_cast<const float4*>(part_o + int64_t(p) * o_ps + (int64_t(m) * H + h) * D + d0);
     float4 v[DPL / 4];
 #pragma unroll
     for (int i = 0; i < DPL / 4; ++i) v[i] = __ldg(src + i);
@@ -351,14 +351,16 @@ __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
 // would leave most SMs idle.
 static void launch_lse_combine(const float* part_ml, const float* part_o, const float* sink, int P, int M, int H,
                                int D, int final_mode, __nv_bfloat16* out, float* lse, float* out_ml, float* out_o,
-                               cudaStream_t st) {
+                               cudaStream_t st, int64_t ml_ps = -1, int64_t o_ps = -1) {
   const int hb = (H + kCombineWarps - 1) / kCombineWarps;
+  if (ml_ps < 0) ml_ps = int64_t(M) * H * 2;
+  if (o_ps < 0) o_ps = int64_t(M) * H * D;
   if (int64_t(M) * hb < 2 * num_sms()) {
     lse_combine_kernel<4><<<dim3(M, hb, D / 128), 32 * kCombineWarps, 0, st>>>(
-        part_ml, part_o, sink, P, M, H, D, final_mode, out, lse, out_ml, out_o);
+        part_ml, part_o, sink, P, M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
   } else {
     lse_combine_kernel<16><<<dim3(M, hb, D / 512), 32 * kCombineWarps, 0, st>>>(
-        part_ml, part_o, sink, P, M, H, D, final_mode, out, lse, out_ml, out_o);
+        part_ml, part_o, sink, P, M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
   }
 }
 
@@ -552,6 +554,23 @@ extern "C" int dsa_lse_combine(const float* part_ml, const float* part_o, const 
   launch_lse_combine(part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
                      nullptr, reinterpret_cast<cudaStream_t>(stream));
   DSA_CHECK_LAUNCH("lse_combine");
+  return DSA_OK;
+}
+
+extern "C" int dsa_lse_combine_strided(const float* part_ml, int64_t ml_pstride, const float* part_o,
+                                       int64_t o_pstride, const float* sink, void* out, int P, int M, int H, int D,
+                                       dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG(part_ml && part_o && sink && out, "lse_combine_strided: null pointer");
+  DSA_CHECK_ARG(P > 0 && M >= 0 && H > 0, "lse_combine_strided: bad P/M/H");
+  DSA_CHECK_ARG(D == kSaD, "lse_combine_strided: built for D=%d (got %d)", kSaD, D);
+  DSA_CHECK_ARG(ml_pstride >= int64_t(M) * H * 2 && o_pstride >= int64_t(M) * H * D && o_pstride % 4 == 0,
+                "lse_combine_strided: partial strides must cover M*H*2 / M*H*D floats (o stride a multiple of 4)");
+  DSA_CHECK_ARG(aligned(part_o, 16) && aligned(out, 16), "lse_combine_strided: part_o / out must be 16-byte aligned");
+  if (M == 0) return DSA_OK;
+  launch_lse_combine(part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
+                     nullptr, reinterpret_cast<cudaStream_t>(stream), ml_pstride, o_pstride);
+  DSA_CHECK_LAUNCH("lse_combine_strided");
   return DSA_OK;
 }
 

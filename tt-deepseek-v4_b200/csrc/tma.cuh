@@ -1,6 +1,6 @@
 // TMA (cp.async.bulk.tensor) helpers for sm_100a: tensor-map encoding on the
 // host and 2-D tile / 4-row gather loads that complete on an mbarrier.
-// Only non-multicast forms are used: every source is this GPU's own memory.
+// Every load here reads this GPU's own memory into its own CTA only.
 #pragma once
 
 #include <cuda.h>

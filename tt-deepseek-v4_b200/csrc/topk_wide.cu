@@ -160,7 +160,8 @@ constexpr int kCountWords = 4;
 
 __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
     const float* __restrict__ score, int64_t ld_score, const int32_t* __restrict__ ids, int64_t ld_ids,
-    const int32_t* __restrict__ t_active, int T, int k, int win, int mask_mode, int per_cta,
+    const int32_t* __restrict__ t_active, int T, int k, int win, int mask_mode, int per_cta, int seg_len,
+    int64_t seg_stride,
     int32_t* __restrict__ out_idx, float* __restrict__ out_score, int64_t ld_out, RowWs* __restrict__ rows,
     uint32_t* __restrict__ counts, unsigned long long* __restrict__ cands, int32_t* __restrict__ status) {
   __shared__ uint32_t s_hist[kBins];
@@ -191,13 +192,16 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
     const int t = e0 + i;
     key[i] = 0u;  // below every real key: padding
     if (i < ept && t < s1) {
+      // a segmented row (the gathered candidate lists) lives in pieces of
+      // seg_len elements seg_stride apart
+      const int64_t at = seg_len > 0 ? int64_t(t / seg_len) * seg_stride + t % seg_len : int64_t(t);
       float v;
-      if (irow && irow[t] < 0) {
+      if (irow && irow[at] < 0) {
         v = -INFINITY;
       } else if (t >= ta) {
-        v = mask_mode == 1 ? -INFINITY : __fsub_rn(srow[t], 1e4f);
+        v = mask_mode == 1 ? -INFINITY : __fsub_rn(srow[at], 1e4f);
       } else {
-        v = srow[t];
+        v = srow[at];
       }
       key[i] = float_key(v);
     }
@@ -272,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
   auto emit = [&](uint32_t out_pos, uint32_t kk, int t) {
     if (out_pos < uint32_t(k)) {  // holds unless the histograms were not zeroed
       const float v = key_float(kk);
-      const int id = irow ? irow[t] : t;
+      const int64_t at = seg_len > 0 ? int64_t(t / seg_len) * seg_stride + t % seg_len : int64_t(t);
+      const int id = irow ? irow[at] : t;
       orow[out_pos] = (v >= -1000.f && id >= 0) ? id + win : -1;
       if (osrow) osrow[out_pos] = v;
     }
@@ -448,12 +453,19 @@ extern "C" size_t dsa_topk_wide_workspace_size(int B, int T) {
 
 extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t* ids, int64_t ld_ids,
                              const int32_t* t_active, int32_t* out_idx, float* out_score, int64_t ld_out, int B, int T,
-                             int k, int win, int mask_mode, void* workspace, size_t workspace_bytes, int32_t* status,
-                             dsa_stream_t stream) {
+                             int k, int win, int mask_mode, int seg_len, int64_t seg_stride, void* workspace,
+                             size_t workspace_bytes, int32_t* status, dsa_stream_t stream) {
   clear_error();
   DSA_CHECK_ARG(score && out_idx && workspace, "topk_wide: null pointer");
   DSA_CHECK_ARG(B >= 0 && T > 0 && k > 0 && k <= T, "topk_wide: need 0 < k <= T (k=%d, T=%d)", k, T);
-  DSA_CHECK_ARG(ld_score >= T && ld_out >= k && (!ids || ld_ids >= T), "topk_wide: bad strides");
+  DSA_CHECK_ARG(seg_len >= 0 && (seg_len == 0 || (T % seg_len == 0 && seg_stride >= seg_len)),
+                "topk_wide: T must be a whole number of segments of seg_len <= seg_stride");
+  // contiguous rows: ld >= T; segmented rows: the B rows' pieces of one
+  // segment, ld apart, fit in seg_stride
+  auto ld_ok = [&](int64_t ld) {
+    return seg_len > 0 ? (ld >= seg_len && int64_t(B - 1) * ld + seg_len <= seg_stride) : ld >= T;
+  };
+  DSA_CHECK_ARG(ld_ok(ld_score) && ld_out >= k && (!ids || ld_ok(ld_ids)), "topk_wide: bad strides");
   DSA_CHECK_ARG(mask_mode == 0 || mask_mode == 1, "topk_wide: mask_mode must be 0 or 1");
   DSA_CHECK_ARG(aligned(workspace, 16), "topk_wide: workspace must be 16-byte aligned");
   if (B == 0) return DSA_OK;
@@ -485,7 +497,8 @@ extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, wide::topk_wide_kernel, score, ld_score, ids, ld_ids, t_active, T, k, win,
-                                     mask_mode, per_cta, out_idx, out_score, ld_out, rows, counts, cands, status);
+                                     mask_mode, per_cta, seg_len, seg_stride, out_idx, out_score, ld_out, rows,
+                                     counts, cands, status);
   if (e != cudaSuccess) {
     set_error("topk_wide: launch failed: %s", cudaGetErrorString(e));
     return DSA_ERR_CUDA;

@@ -47,14 +47,24 @@ PROTOTYPES = {
     "dsa_topk_merge": (I32, [P, P, I32, P, P, I64, I32, I32, I32, P]),
     "dsa_shard_active": (I32, [P, P, I32, I32, I32, P]),
     "dsa_topk_wide_workspace_size": (SZ, [I32, I32]),
-    "dsa_topk_wide": (I32, [P, I64, P, I64, P, P, P, I64, I32, I32, I32, I32, I32, P, SZ, P, P]),
+    "dsa_topk_wide": (I32, [P, I64, P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, I64, P, SZ, P, P]),
     "dsa_shard_local_indices": (I32, [P, I64, I32, P, I64, I32, I32, I32, I32, I32, P, I64, I32, P]),
     "dsa_sparse_attn_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "dsa_sparse_attn": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
     "dsa_sparse_attn_noalloc": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, P]),
     "dsa_sparse_attn_partial": (I32, [P, P, I64, I64, P, I64, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
     "dsa_lse_combine": (I32, [P, P, P, P, I32, I32, I32, I32, P]),
+    "dsa_lse_combine_strided": (I32, [P, I64, P, I64, P, P, I32, I32, I32, I32, P]),
     "dsa_set_trace": (I32, [P, SZ]),
+    "dsa_p2p_alloc": (I32, [SZ, P]),
+    "dsa_p2p_free": (I32, [P]),
+    "dsa_p2p_handle_size": (SZ, []),
+    "dsa_p2p_export": (I32, [P, P, P]),
+    "dsa_p2p_import": (I32, [P, P]),
+    "dsa_p2p_close": (I32, [P]),
+    "dsa_p2p_publish": (I32, [P, SZ, P, P, P, I32, P, P]),
+    "dsa_p2p_wait": (I32, [P, I32, P, P, P]),
+    "dsa_counter_bump": (I32, [P, P]),
 }
 
 _lock = threading.Lock()

@@ -13,10 +13,10 @@ of one layer on every rank:
            the emitted row stored only by the rank that owns its position),
            indexer score over the shard, local top-k' candidates
            (k' = min(k, shard rows)) with global positions
-  exchange all-gather of the candidates (G x k' x 8 bytes)
+  exchange one all-gather of the candidates (G x k' x 8 bytes)
   attend   global merge (identical on every rank), this shard's rows of the
            selection, partial attention (m, l, o) without the sink
-  exchange all-gather of the partials (G x H x (D + 2) x 4 bytes)
+  exchange one all-gather of the partials (G x H x (D + 2) x 4 bytes)
   combine  log-sum-exp merge with the sink counted once -> bf16 o
 
 Any global top-k entry is in its shard's top-k', and both selections break
@@ -26,8 +26,9 @@ rounding.  The reference plans this split (briefs/future_max_utilization.md:
 177-204) but does not implement it.
 
 ``SeqShard`` holds one rank's buffers and runs the three compute phases;
-``SeqSplitPath`` drives it with a ``Comm`` (torch.distributed all-gathers,
-NCCL on GPUs).  The phases are separate methods so that G shards can also be
+``SeqSplitPath`` drives it with a comm: ``P2PComm`` (peer-memory stores
+over NVLink with per-rank flags, the GPU default) or ``TorchDistComm``
+(all-gathers over a process group: NCCL, or gloo in the CPU tests).  The phases are separate methods so that G shards can also be
 driven inside one process (the exchanges become copies), which is how the
 single-GPU tests check the split against the unsplit path.
 """
@@ -63,7 +64,8 @@ def seq_shard(T_total: int, rank: int, world: int):
 
 
 class TorchDistComm:
-    """All-gathers over a torch.distributed process group."""
+    """The two exchanges as all-gathers over a torch.distributed process
+    group (NCCL on GPUs, gloo in the CPU tests)."""
 
     def __init__(self, group=None):
         import torch.distributed as dist
@@ -79,11 +81,127 @@ class TorchDistComm:
         except (RuntimeError, NotImplementedError):
             self.dist.all_gather(list(out.unbind(0)), inp, group=self.group)
 
+    def exchange(self, L, phase: int) -> None:
+        if phase == 0:
+            self.all_gather(L.cand_all, L.cand)
+        else:
+            self.all_gather(L.part_all, L.part)
+
+    def end_step(self) -> None:
+        pass
+
+    def close(self) -> None:
+        pass
+
+
+class P2PComm:
+    """The two exchanges as peer-memory stores over NVLink (dsa_p2p_*):
+    every rank publishes its candidates / partials straight into slot
+    ``rank`` of every peer's receive buffer and raises its flag there; the
+    consumer waits (bounded) on the G flags of that layer and phase.  The
+    receive buffers of all layers live in one arena per rank, exported once
+    as a CUDA IPC handle and mapped by the other ranks of the node.  Set-up
+    uses the process group once (an object all-gather of the handles)."""
+
+    def __init__(self, shard: "SeqShard", group=None):
+        import ctypes
+        import torch.distributed as dist
+        if shard.arena is None:
+            raise ValueError("P2PComm needs a SeqShard built with peer_exchange=True")
+        L = native_ops.lib()
+        self.shard = shard
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world != shard.world or self.rank != shard.rank:
+            raise ValueError("process group and shard disagree on rank / world")
+        dev = shard.device
+        base = shard.arena.buf.data_ptr()
+        hsize = int(L.dsa_p2p_handle_size())
+        h = ctypes.create_string_buffer(hsize)
+        off = ctypes.c_uint64(0)
+        native_ops.check(L.dsa_p2p_export(ctypes.c_void_p(base), h, ctypes.byref(off)), "p2p_export")
+        mine = (bytes(h.raw), int(off.value))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        self.mapped = []
+        peer_base = []
+        for g, (hb, o) in enumerate(allh):
+            if g == self.rank:
+                peer_base.append(base)
+                continue
+            p = ctypes.c_void_p(0)
+            native_ops.check(L.dsa_p2p_import(ctypes.create_string_buffer(hb, hsize), ctypes.byref(p)),
+                             "p2p_import")
+            self.mapped.append(p.value)
+            peer_base.append(p.value + o)
+        self.epoch = torch.ones(1, dtype=I32, device=dev)
+        # per layer and phase: device arrays of the G destination and flag addresses
+        self.routes = []
+        for Ly in shard.layers:
+            per = []
+            for phase, recv in ((0, Ly.cand_all), (1, Ly.part_all)):
+                slot = recv[self.rank].data_ptr() - base
+                flag = Ly.flags[phase, self.rank].data_ptr() - base
+                dst = torch.tensor([pb + slot for pb in peer_base], dtype=torch.int64, device=dev)
+                fl = torch.tensor([pb + flag for pb in peer_base], dtype=torch.int64, device=dev)
+                per.append((dst, fl))
+            self.routes.append(per)
+        self.layer_index = {id(Ly): i for i, Ly in enumerate(shard.layers)}
+        dist.barrier(group=group)
+
+    def exchange(self, L, phase: int) -> None:
+        lib = native_ops.lib()
+        src = L.cand if phase == 0 else L.part
+        dst, fl = self.routes[self.layer_index[id(L)]][phase]
+        st = torch.cuda.current_stream(src.device).cuda_stream
+        native_ops.check(lib.dsa_p2p_publish(src.data_ptr(), src.numel() * src.element_size(), dst.data_ptr(),
+                                             fl.data_ptr(), self.epoch.data_ptr(), self.world,
+                                             L.done[phase].data_ptr(), st), "p2p_publish")
+        native_ops.check(lib.dsa_p2p_wait(L.flags[phase].data_ptr(), self.world, self.epoch.data_ptr(),
+                                          self.shard.status.data_ptr(), st), "p2p_wait")
+
+    def end_step(self) -> None:
+        native_ops.check(native_ops.lib().dsa_counter_bump(self.epoch.data_ptr(),
+                                                           torch.cuda.current_stream(self.epoch.device).cuda_stream),
+                         "counter_bump")
+
+    def close(self) -> None:
+        lib = native_ops.lib()
+        for p in self.mapped:
+            lib.dsa_p2p_close(p)
+        self.mapped = []
+
+
+class _Arena:
+    """Bump allocator over one zeroed device buffer: the receive buffers
+    peers write into must share one allocation (one IPC export)."""
+
+    def __init__(self, nbytes: int, device):
+        self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        self.off = 0
+
+    def take(self, shape, dtype) -> torch.Tensor:
+        n = 1
+        for x in shape:
+            n *= x
+        nb = n * torch.tensor([], dtype=dtype).element_size()
+        if self.off + nb > self.buf.numel():
+            raise RuntimeError("exchange arena too small")
+        t = self.buf[self.off:self.off + nb].view(dtype).view(shape)
+        self.off += -(-nb // 256) * 256
+        return t
+
+    @staticmethod
+    def layer_bytes(B: int, kc: int, world: int, H: int, D: int) -> int:
+        r = lambda nb: -(-nb // 256) * 256
+        return r(world * 2 * B * kc * 4) + r(world * B * H * (D + 2) * 4) + r(2 * world * 4) + r(2 * world * 4)
+
 
 class SeqShardLayer:
     """One layer's shard: compressed rows [lo, hi) + the window ring."""
 
-    def __init__(self, args: PathArgs, B: int, n_local: int, k: int, kc: int, world: int, device):
+    def __init__(self, args: PathArgs, B: int, n_local: int, k: int, kc: int, world: int, device,
+                 arena: _Arena | None = None):
         D, Di, H, W, r = args.head_dim, args.index_head_dim, args.n_heads, args.window_size, args.compress_ratio
         dev = device
         # rows [0, n_local) compressed entries of this shard, then the W-row window ring
@@ -100,18 +218,39 @@ class SeqShardLayer:
         self.sink = torch.zeros(H, dtype=F32, device=dev)
         # per-step scratch
         self.score = torch.zeros(B, max(n_local, 1), dtype=F32, device=dev)
-        self.cand_idx = torch.full((B, kc), -1, dtype=I32, device=dev)
-        self.cand_score = torch.full((B, kc), float("-inf"), dtype=F32, device=dev)
-        self.cand_idx_all = torch.full((world, B, kc), -1, dtype=I32, device=dev)
-        self.cand_score_all = torch.full((world, B, kc), float("-inf"), dtype=F32, device=dev)
+        # candidates, one flat buffer so one all-gather moves them: B*kc fp32
+        # scores, then B*kc int32 global positions
+        self.kc = kc
+        self.cand = torch.empty(2 * B * kc, dtype=I32, device=dev)
+        self.cand_score = self.cand[:B * kc].view(F32).view(B, kc)
+        self.cand_idx = self.cand[B * kc:].view(B, kc)
+        self.cand_score.fill_(float("-inf"))
+        self.cand_idx.fill_(-1)
+        take = arena.take if arena is not None else (lambda shape, dt: torch.zeros(shape, dtype=dt, device=dev))
+        self.cand_all = take((world, 2 * B * kc), I32)
         self.sel = torch.full((B, k), -1, dtype=I32, device=dev)
         self.selected = self.sel     # the merged selection of the last step (a view of sel or cand_idx)
         self.win_idx = torch.full((B, W), -1, dtype=I32, device=dev)
         self.lidx = torch.full((B, W + k), -1, dtype=I32, device=dev)
-        self.pml = torch.zeros(B, H, 2, dtype=F32, device=dev)
-        self.po = torch.zeros(B, H, D, dtype=F32, device=dev)
-        self.pml_all = torch.zeros(world, B, H, 2, dtype=F32, device=dev)
-        self.po_all = torch.zeros(world, B, H, D, dtype=F32, device=dev)
+        # the partial (m, l) and o in one flat buffer as well: B*H*2, then B*H*D floats
+        self.part = torch.zeros(B * H * (D + 2), dtype=F32, device=dev)
+        self.pml = self.part[:B * H * 2].view(B, H, 2)
+        self.po = self.part[B * H * 2:].view(B, H, D)
+        self.part_all = take((world, B * H * (D + 2)), F32)
+        # peer-exchange bookkeeping: per phase (0 candidates, 1 partials) one
+        # flag per source rank, and the publish kernel's per-destination counters
+        self.flags = take((2, world), I32)
+        self.done = take((2, world), I32)
+
+    def cand_all_views(self, B: int):
+        """(scores [G, B, kc], positions [G, B, kc]) views of the gathered candidates."""
+        G = self.cand_all.shape[0]
+        n = B * self.kc
+        return (self.cand_all[:, :n].view(F32).view(G, B, self.kc), self.cand_all[:, n:].view(G, B, self.kc))
+
+    def part_all_views(self, B: int, H: int, D: int):
+        G = self.part_all.shape[0]
+        return (self.part_all[:, :B * H * 2].view(G, B, H, 2), self.part_all[:, B * H * 2:].view(G, B, H, D))
 
     def kv_compressed(self, n_local: int):
         return self.kv[:, :n_local]
@@ -125,7 +264,7 @@ class SeqShard:
 
     def __init__(self, args: PathArgs, B: int, T_total: int, rank: int, world: int, device, k: int | None = None,
                  n_layers: int = 1, max_seq_len: int | None = None, window_rank: int | None = None,
-                 scale: float | None = None, backend=None):
+                 scale: float | None = None, backend=None, peer_exchange: bool = False):
         self.args = args
         self.B = B
         self.rank, self.world = rank, world
@@ -145,7 +284,11 @@ class SeqShard:
         self.scale = args.softmax_scale if scale is None else scale
         max_seq = max_seq_len if max_seq_len is not None else T_total * args.compress_ratio
         self.cos, self.sin = rope_cos_sin(args, max_seq, compressed=True, device=self.device)
-        self.layers = [SeqShardLayer(args, B, self.n_local, self.k, self.kc, world, self.device)
+        self.arena = None
+        if peer_exchange:
+            self.arena = _Arena(n_layers * _Arena.layer_bytes(B, self.kc, world, args.n_heads, args.head_dim),
+                                self.device)
+        self.layers = [SeqShardLayer(args, B, self.n_local, self.k, self.kc, world, self.device, self.arena)
                        for _ in range(n_layers)]
         dev = self.device
         self.pos = torch.zeros(B, dtype=I32, device=dev)
@@ -197,20 +340,23 @@ class SeqShard:
     def phase_attend(self, L: SeqShardLayer, x: LayerInputs) -> None:
         a, o = self.args, self.ops
         W, r, n = a.window_size, a.compress_ratio, self.n_local
-        G, B = self.world, self.B
-        if B == 1:
-            cs, ci = L.cand_score_all.view(1, G * self.kc), L.cand_idx_all.view(1, G * self.kc)
-        else:
-            cs = L.cand_score_all.permute(1, 0, 2).reshape(B, G * self.kc)
-            ci = L.cand_idx_all.permute(1, 0, 2).reshape(B, G * self.kc)
-        if G == 1 and self.kc == self.k:
+        G, B, kc = self.world, self.B, self.kc
+        if G == 1 and kc == self.k:
             L.selected = L.cand_idx          # one shard: its candidates are the global top-k
         else:
             if self.use_wide:
-                # candidates arrive in ascending position order (rank by rank),
-                # so the lower-slot tie rule is the lower-position rule
-                o.topk_wide(cs, self.k, 0, ids=ci, mask_mode=0, out=L.sel, ws=self.wide_ws, status=self.status)
+                # row b of rank g's list sits at g * 2*B*kc + b*kc: read the
+                # gathered buffer in place as G segments per row; the lists
+                # arrive in ascending position order, rank by rank, so the
+                # lower-slot tie rule is the lower-position rule
+                flat = L.cand_all.view(-1)
+                o.topk_wide(flat.view(F32), self.k, 0,
+                            ids=flat[B * kc:], mask_mode=0, out=L.sel, ws=self.wide_ws, status=self.status,
+                            seg_len=kc, seg_stride=2 * B * kc, B=B, T=G * kc, ld_score=kc)
             else:
+                sc, ix = L.cand_all_views(B)
+                cs = sc.permute(1, 0, 2).reshape(B, G * kc)
+                ci = ix.permute(1, 0, 2).reshape(B, G * kc)
                 o.topk_merge(cs, ci, self.k, 0, out=L.sel)
             L.selected = L.sel
         attend_window = self.rank == self.window_rank
@@ -227,8 +373,10 @@ class SeqShard:
     # ---- phase 3: combine the gathered partials
     def phase_combine(self, L: SeqShardLayer, out: torch.Tensor) -> None:
         B, H, D = self.B, self.args.n_heads, self.args.head_dim
-        self.ops.lse_combine(L.pml_all.view(self.world, B, H, 2), L.po_all.view(self.world, B, H, D), L.sink,
-                             out=out.view(B, H, D))
+        ps = B * H * (D + 2)
+        flat = L.part_all.view(-1)
+        self.ops.lse_combine_strided(flat, ps, flat[B * H * 2:], ps, self.world, B, H, D, L.sink,
+                                     out.view(B, H, D))
 
     def advance(self) -> None:
         self.ops.advance_positions(self.pos, self.t_active, self.args.compress_ratio, 1)
@@ -244,16 +392,15 @@ class SeqSplitPath:
     def layer_step(self, L: SeqShardLayer, x: LayerInputs, out: torch.Tensor) -> None:
         s, c = self.shard, self.comm
         s.phase_local(L, x)
-        c.all_gather(L.cand_score_all, L.cand_score)
-        c.all_gather(L.cand_idx_all, L.cand_idx)
+        c.exchange(L, 0)
         s.phase_attend(L, x)
-        c.all_gather(L.pml_all, L.pml)
-        c.all_gather(L.po_all, L.po)
+        c.exchange(L, 1)
         s.phase_combine(L, out)
 
     def step(self, inputs, outs, advance: bool = True) -> None:
         for L, x, o in zip(self.shard.layers, inputs, outs):
             self.layer_step(L, x, o)
+        self.comm.end_step()
         if advance:
             self.shard.advance()
 
@@ -269,14 +416,12 @@ def run_shards_in_process(shards, inputs, outs, advance: bool = True) -> None:
             s.phase_local(L, inputs[li])
         for L in Ls:
             for g in range(G):
-                L.cand_score_all[g].copy_(Ls[g].cand_score)
-                L.cand_idx_all[g].copy_(Ls[g].cand_idx)
+                L.cand_all[g].copy_(Ls[g].cand)
         for s, L in zip(shards, Ls):
             s.phase_attend(L, inputs[li])
         for L in Ls:
             for g in range(G):
-                L.pml_all[g].copy_(Ls[g].pml)
-                L.po_all[g].copy_(Ls[g].po)
+                L.part_all[g].copy_(Ls[g].part)
         for g, (s, L) in enumerate(zip(shards, Ls)):
             s.phase_combine(L, outs[g][li])
     if advance:

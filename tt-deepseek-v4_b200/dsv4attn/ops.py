@@ -320,11 +320,14 @@ class WideTopkWorkspace:
 def topk_wide(score: torch.Tensor, k: int, win: int, t_active: torch.Tensor | None = None, T: int | None = None,
               ids: torch.Tensor | None = None, mask_mode: int = 1, out: torch.Tensor | None = None,
               out_score: torch.Tensor | None = None, ws: WideTopkWorkspace | None = None,
-              status: torch.Tensor | None = None) -> torch.Tensor:
+              status: torch.Tensor | None = None, seg_len: int = 0, seg_stride: int = 0,
+              B: int | None = None, ld_score: int | None = None) -> torch.Tensor:
     """Multi-CTA top-k of a few long rows (see dsa_topk_wide); output in
-    ascending position order."""
+    ascending position order.  With ``seg_len`` the T elements of a row are
+    read as T / seg_len pieces ``seg_stride`` elements apart (the rank-major
+    result of an all-gather); B / ld_score then describe the rows."""
     _need(score, "score", F32)
-    B = score.shape[0]
+    B = score.shape[0] if B is None else B
     T = score.shape[1] if T is None else T
     if score.stride(-1) != 1:
         raise ValueError("score must have a unit stride in the last dim")
@@ -343,9 +346,12 @@ def topk_wide(score: torch.Tensor, k: int, win: int, t_active: torch.Tensor | No
     if ws is None:
         ws = _wide_ws.setdefault(score.device, WideTopkWorkspace(score.device))
     buf = ws.get(B, T)
-    check(lib().dsa_topk_wide(score.data_ptr(), score.stride(0), _ptr(ids), ld_ids, _ptr(t_active), out.data_ptr(),
-                              _ptr(out_score), out.stride(0), B, T, k, win, mask_mode, buf.data_ptr(), buf.numel(),
-                              _ptr(status), _stream(score)), "topk_wide")
+    lds = score.stride(0) if ld_score is None else ld_score
+    if ids is not None and ld_score is not None:
+        ld_ids = ld_score
+    check(lib().dsa_topk_wide(score.data_ptr(), lds, _ptr(ids), ld_ids, _ptr(t_active), out.data_ptr(),
+                              _ptr(out_score), out.stride(0), B, T, k, win, mask_mode, seg_len, seg_stride,
+                              buf.data_ptr(), buf.numel(), _ptr(status), _stream(score)), "topk_wide")
     return out
 
 
@@ -471,6 +477,20 @@ def sparse_attn_partial(q, kv, idx, scale: float, part_ml=None, part_o=None, ws:
                                     w.buf.data_ptr() if w else None, w.nbytes if w else 0, _ptr(status),
                                     _stream(q)), "sparse_attn_partial")
     return part_ml, part_o
+
+
+def lse_combine_strided(part_ml: torch.Tensor, ml_pstride: int, part_o: torch.Tensor, o_pstride: int, P: int,
+                        M: int, H: int, D: int, sink: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """lse_combine over P partials ``ml_pstride`` / ``o_pstride`` floats apart
+    (rank-major all-gather output); out bf16 [M, H, D]."""
+    _need(part_ml, "part_ml", F32)
+    _need(part_o, "part_o", F32)
+    _need(sink, "sink", F32)
+    _need(out, "out", BF16)
+    check(lib().dsa_lse_combine_strided(part_ml.data_ptr(), ml_pstride, part_o.data_ptr(), o_pstride,
+                                        sink.data_ptr(), out.data_ptr(), P, M, H, D, _stream(part_o)),
+          "lse_combine_strided")
+    return out
 
 
 def lse_combine(part_ml, part_o, sink, out=None) -> torch.Tensor:
