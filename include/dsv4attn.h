@@ -153,7 +153,8 @@ int dsa_window_indices(const int32_t* pos, int32_t* idx, int64_t ld_idx, int B,
  * fp32 accumulation, for t < T.  q [B, H, Di] bf16; k bf16 rows of Di with
  * batch stride k_bstride elements; w [B, H] fp32 (already scaled by
  * Di^-1/2 * H^-1/2 when the caller follows the reference's fold);
- * score [B, T] fp32 with row stride ld_score.  t_valid (may be NULL):
+ * score [B, T] fp32 with row stride ld_score.  k_bstride 0: one key cache
+ * shared by all B rows (the queries of a prefill chunk).  t_valid (may be NULL):
  * device [B] int32; keys t >= t_valid[b] are neither read nor scored (their
  * score entries are left untouched).  Requires H == 64, Di == 128.
  * Replaces DeviceIndexer.forward_device_score's score stage
@@ -275,6 +276,19 @@ int dsa_p2p_publish(const void* src, size_t bytes, const unsigned long long* dst
 int dsa_p2p_wait(const uint32_t* flags, int G, const uint32_t* epoch, int32_t* status,
                  dsa_stream_t stream);
 int dsa_counter_bump(uint32_t* counter, dsa_stream_t stream);
+
+/* Prefill chunk of S tokens at positions base .. base+S-1 (one sequence):
+ * t_active[s] = min(T, (base + s + 1) / ratio) - the compressed entries the
+ * token at that position may see (entry j is complete once 4j+3 <= p) - and
+ * the first W columns of idx [S, ld_idx]: the causal window, rows of a raw
+ * buffer holding the n_hist tokens before the chunk and then the chunk
+ * (row s + i + n_hist - (W-1) for position p - W + 1 + i; -1 before row 0).
+ * The multi-token form of the window table and T_active
+ * (inference.py:479-506, 6028); the indexer scores of such a chunk come
+ * from dsa_indexer_score with B = S and k_bstride = 0 (one shared key
+ * cache), its per-token selection from dsa_indexer_topk with t_active. */
+int dsa_prefill_positions(int S, int base, int ratio, int T, int W, int n_hist,
+                          int32_t* t_active, int32_t* idx, int64_t ld_idx, dsa_stream_t stream);
 
 /* ------------------------------------------------------------ attn.sparse */
 

@@ -30,7 +30,7 @@ __all__ = [
     "compressor_step", "shift_matrix_apply", "indexer_score", "indexer_topk",
     "sparse_attn", "sparse_attn_partial", "lse_combine", "topk_merge",
     "hadamard_rotate", "LayerState", "decode_layer_step", "linear_bf16",
-    "head_norm_rope", "kv_norm_rope_quant", "BlockWeights", "attention_decode_block",
+    "head_norm_rope", "kv_norm_rope_quant", "BlockWeights", "attention_decode_block", "prefill_chunk",
 ]
 
 FP8_MAX = 448.0
@@ -513,3 +513,32 @@ def attention_decode_block(bw: BlockWeights, st: LayerState, x: torch.Tensor, po
     wa = bw.wo_a.to(torch.bfloat16).float().view(G, R, H * D // G)
     a = torch.einsum("bgi,gri->bgr", og, wa).to(torch.bfloat16).reshape(B, G * R)
     return linear_bf16(a, bw.wo_b).view(B, 1, -1)
+
+
+# --------------------------------------------------------------------------
+# multi-token (prefill chunk)
+# --------------------------------------------------------------------------
+
+def prefill_chunk(q, kv, n_raw: int, iq, ikeys, iw, sink, base: int, n_hist: int, T: int,
+                  k: int, W: int = 128, ratio: int = 4, scale: float = 512 ** -0.5, rows=None):
+    """S tokens at positions base..base+S-1, each attending its own top-k of
+    the compressed entries it may see (t < (p + 1) // ratio, the T_active
+    rule of inference.py:6028 per token) plus its causal window of W raw
+    tokens; indexer score and top-k as in the decode step (indexer.py:10-23,
+    inference.py:5823-5851), sink attention as inference.py:4459-4501.
+    kv: [n_raw + T', D] raw rows (n_hist before the chunk, then the chunk)
+    followed by the compressed entries.  ``rows``: chunk offsets of the
+    given tokens (default 0..S-1) when checking a sample of a chunk.
+    Returns (o [S, H, D] bf16, idx)."""
+    S = q.shape[0]
+    rows = list(range(S)) if rows is None else list(rows)
+    sc = torch.einsum("shd,td->sht", iq.float(), ikeys[:T].float())
+    score = (sc.relu() * iw.float().unsqueeze(-1)).sum(dim=1)
+    ta = torch.tensor([min(T, (base + s + 1) // ratio) for s in rows])
+    cidx = indexer_topk(score, ta, k, n_raw)
+    win = torch.tensor([[s + i + n_hist - (W - 1) for i in range(W)] for s in rows], dtype=torch.int32)
+    win = torch.where(win >= 0, win, torch.full_like(win, -1))
+    idx = torch.cat([win, cidx], dim=1)
+    kv3 = kv.unsqueeze(0).expand(S, -1, -1)
+    o = sparse_attn(q, kv3, idx, sink, scale)
+    return o, idx

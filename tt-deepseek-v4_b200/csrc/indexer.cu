@@ -140,7 +140,8 @@ extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, f
   DSA_CHECK_ARG(q && k && w && score, "indexer_score: null pointer");
   DSA_CHECK_ARG(H == kIdxH && Di == kIdxD, "indexer_score: built for H=64, Di=128 (got H=%d Di=%d)", H, Di);
   DSA_CHECK_ARG(B >= 0 && T >= 0, "indexer_score: bad B/T");
-  DSA_CHECK_ARG(k_bstride >= int64_t(T) * Di && k_bstride % 8 == 0, "indexer_score: bad k batch stride");
+  DSA_CHECK_ARG((k_bstride == 0 || k_bstride >= int64_t(T) * Di) && k_bstride % 8 == 0,
+                "indexer_score: bad k batch stride (0 = one key cache shared by all rows)");
   DSA_CHECK_ARG(ld_score >= T, "indexer_score: ld_score < T");
   DSA_CHECK_ARG(aligned(q, 16) && aligned(k, 16), "indexer_score: q/k must be 16-byte aligned");
   if (B == 0 || T == 0) return DSA_OK;

@@ -37,9 +37,38 @@ __global__ void shard_local_indices_kernel(const int32_t* __restrict__ sel, int6
   }
 }
 
+// Prefill chunk of S tokens at positions base .. base + S - 1: per query s
+// the compressed entries it may see, t_active[s] = min(T, (p + 1) / ratio)
+// (entry j holds tokens 4j .. 4j + 3, visible once all are <= p), and its
+// causal window of W raw rows: the raw buffer holds the n_hist tokens before
+// the chunk then the chunk, so position p - W + 1 + i sits in row
+// s + i + n_hist - (W - 1) (-1 before the first held token).
+__global__ void prefill_positions_kernel(int S, int base, int ratio, int T, int W, int n_hist,
+                                         int32_t* __restrict__ t_active, int32_t* __restrict__ idx, int64_t ld_idx) {
+  const int s = blockIdx.x;
+  if (threadIdx.x == 0) t_active[s] = min(T, (base + s + 1) / ratio);
+  for (int i = threadIdx.x; i < W; i += blockDim.x) {
+    const int row = s + i + n_hist - (W - 1);
+    idx[int64_t(s) * ld_idx + i] = row >= 0 ? row : -1;
+  }
+}
+
 }  // namespace dsa
 
 using namespace dsa;
+
+extern "C" int dsa_prefill_positions(int S, int base, int ratio, int T, int W, int n_hist, int32_t* t_active,
+                                     int32_t* idx, int64_t ld_idx, dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG(t_active && idx && S >= 0 && base >= 0 && ratio > 0 && T >= 0 && W > 0 && ld_idx >= W,
+                "prefill_positions: bad arguments");
+  DSA_CHECK_ARG(n_hist >= 0 && n_hist <= base, "prefill_positions: n_hist %d must be in [0, base]", n_hist);
+  if (S == 0) return DSA_OK;
+  prefill_positions_kernel<<<S, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(S, base, ratio, T, W, n_hist,
+                                                                                 t_active, idx, ld_idx);
+  DSA_CHECK_LAUNCH("prefill_positions");
+  return DSA_OK;
+}
 
 extern "C" int dsa_shard_active(const int32_t* t_active, int32_t* t_local, int B, int lo, int n_local,
                                 dsa_stream_t stream) {

@@ -46,6 +46,7 @@ PROTOTYPES = {
     "dsa_advance_positions": (I32, [P, P, I32, I32, I32, P]),
     "dsa_topk_merge": (I32, [P, P, I32, P, P, I64, I32, I32, I32, P]),
     "dsa_shard_active": (I32, [P, P, I32, I32, I32, P]),
+    "dsa_prefill_positions": (I32, [I32, I32, I32, I32, I32, I32, P, P, I64, P]),
     "dsa_topk_wide_workspace_size": (SZ, [I32, I32]),
     "dsa_topk_wide": (I32, [P, I64, P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, I64, P, SZ, P, P]),
     "dsa_shard_local_indices": (I32, [P, I64, I32, P, I64, I32, I32, I32, I32, I32, P, I64, I32, P]),

@@ -259,20 +259,27 @@ def window_indices(pos: torch.Tensor, win: int, out: torch.Tensor | None = None)
 def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: int,
                   out: torch.Tensor | None = None, t_valid: torch.Tensor | None = None) -> torch.Tensor:
     """``s[b,t] = sum_h w[b,h] relu(q[b,h].k[b,t])`` for t < T
-    (inference.py:5260-5275).  q [B,64,128] bf16, k_cache [B, >=T, 128] bf16,
-    w [B,64] fp32 -> [B, T] fp32."""
+    (inference.py:5260-5275).  q [B,64,128] bf16, k_cache [B, >=T, 128] bf16
+    (or [>=T, 128]: one cache shared by all B rows, the queries of a prefill
+    chunk), w [B,64] fp32 -> [B, T] fp32."""
     _need(q, "q", BF16)
     _need(k_cache, "k_cache", BF16)
     _need(w, "w", F32)
     _contig(q, "q")
     _contig(w, "w")
     B, H, Di = q.shape
-    if k_cache.shape[0] < B or k_cache.shape[1] < T or k_cache.shape[2] != Di or k_cache.stride(1) != Di:
-        raise ValueError("k_cache must be [B, >=T, Di] with contiguous rows")
+    if k_cache.dim() == 2:
+        if k_cache.shape[0] < T or k_cache.shape[1] != Di or k_cache.stride(0) != Di:
+            raise ValueError("a shared k_cache must be [>=T, Di] with contiguous rows")
+        k_bstride = 0
+    else:
+        if k_cache.shape[0] < B or k_cache.shape[1] < T or k_cache.shape[2] != Di or k_cache.stride(1) != Di:
+            raise ValueError("k_cache must be [B, >=T, Di] with contiguous rows")
+        k_bstride = k_cache.stride(0)
     if out is None:
         out = torch.empty(B, T, dtype=F32, device=q.device)
     check(lib().dsa_indexer_score(q.data_ptr(), k_cache.data_ptr(), w.data_ptr(), out.data_ptr(), _ptr(t_valid),
-                                  B, H, Di, T, k_cache.stride(0), out.stride(0), _stream(q)), "indexer_score")
+                                  B, H, Di, T, k_bstride, out.stride(0), _stream(q)), "indexer_score")
     return out
 
 
@@ -371,6 +378,18 @@ def topk_merge(cand_score: torch.Tensor, cand_idx: torch.Tensor, k: int, win: in
     check(lib().dsa_topk_merge(cand_score.data_ptr(), cand_idx.data_ptr(), n, out.data_ptr(), _ptr(out_score),
                                out.stride(0), B, k, win, _stream(cand_score)), "topk_merge")
     return out
+
+
+def prefill_positions(S: int, base: int, T: int, W: int, n_hist: int, ratio: int, t_active: torch.Tensor,
+                      idx: torch.Tensor) -> None:
+    """Per-token t_active and causal-window columns idx[:, :W] of a prefill
+    chunk (see dsa_prefill_positions)."""
+    _need(t_active, "t_active", I32)
+    _need(idx, "idx", I32)
+    if idx.stride(-1) != 1 or idx.shape[0] < S:
+        raise ValueError("idx must be [>=S, >=W] with a unit last stride")
+    check(lib().dsa_prefill_positions(S, base, ratio, T, W, n_hist, t_active.data_ptr(), idx.data_ptr(),
+                                      idx.stride(0), _stream(idx)), "prefill_positions")
 
 
 def shard_active(t_active: torch.Tensor, lo: int, n_local: int, out: torch.Tensor | None = None) -> torch.Tensor:
