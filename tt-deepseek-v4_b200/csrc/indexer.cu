@@ -14,6 +14,7 @@
 // HBM-bound on the key stream: 256 B per key in, 4 B per key out.
 #include "common.cuh"
 #include "indexer_tc.cuh"
+#include "indexer_prefill_tc.cuh"
 #include <stdlib.h>
 
 namespace dsa {
@@ -169,6 +170,35 @@ extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, f
     indexer_score_mma_kernel<<<grid, kIdxThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), w, score, t_valid, T, k_bstride,
         ld_score, per);
+  } else if (k_bstride == 0 && B % idxpf::QG == 0) {
+    // one key cache shared by all rows (a prefill chunk): 4 rows per MMA batch
+    static int pf_attr_dev = -1;
+    if (pf_attr_dev != dev) {
+      cudaFuncSetAttribute(idxpf::indexer_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           idxpf::kSmemBytes);
+      pf_attr_dev = dev;
+    }
+    DSA_CHECK_ARG(uint64_t(B) * kIdxH < (1ull << 31), "indexer_score: too many rows");
+    CUtensorMap tm_k, tm_q;
+    if (!tma::make_2d_bf16(&tm_k, k, kIdxD, uint64_t(T), kIdxD * 2, 64, idxpf::TILE) ||
+        !tma::make_2d_bf16(&tm_q, q, kIdxD, uint64_t(B) * kIdxH, kIdxD * 2, 64, idxpf::N)) {
+      set_error("indexer_score: cuTensorMapEncodeTiled failed");
+      return DSA_ERR_CUDA;
+    }
+    idxpf::Args a{};
+    a.w = w;
+    a.score = score;
+    a.t_valid = t_valid;
+    a.status = nullptr;
+    a.S = B;
+    a.T = T;
+    a.tiles = (T + idxpf::TILE - 1) / idxpf::TILE;
+    const int total = (B / idxpf::QG) * a.tiles;
+    a.items_per_cta = (total + nsm - 1) / nsm;
+    a.ld_score = ld_score;
+    const int grid = (total + a.items_per_cta - 1) / a.items_per_cta;
+    idxpf::indexer_prefill_tc_kernel<<<grid, idxpf::THREADS, idxpf::kSmemBytes,
+                                       reinterpret_cast<cudaStream_t>(stream)>>>(a, tm_k, tm_q);
   } else {
     DSA_CHECK_ARG(k_bstride % kIdxD == 0, "indexer_score: k batch stride must be a multiple of Di");
     const int64_t row_stride = k_bstride / kIdxD;
