@@ -46,6 +46,14 @@ F32 = torch.float32
 I32 = torch.int32
 
 
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
 def batch_shard(B_total: int, rank: int, world: int):
     """Contiguous [start, stop) of the sequences rank ``rank`` owns."""
     if B_total % world:
@@ -230,7 +238,6 @@ class SeqShardLayer:
         self.cand_all = take((world, 2 * B * kc), I32)
         self.sel = torch.full((B, k), -1, dtype=I32, device=dev)
         self.selected = self.sel     # the merged selection of the last step (a view of sel or cand_idx)
-        self.win_idx = torch.full((B, W), -1, dtype=I32, device=dev)
         self.lidx = torch.full((B, W + k), -1, dtype=I32, device=dev)
         # the partial (m, l) and o in one flat buffer as well: B*H*2, then B*H*D floats
         self.part = torch.zeros(B * H * (D + 2), dtype=F32, device=dev)
@@ -295,6 +302,8 @@ class SeqShard:
         self.t_active = torch.zeros(B, dtype=I32, device=dev)
         self.t_local = torch.zeros(B, dtype=I32, device=dev)
         self.status = torch.zeros(1, dtype=I32, device=dev)
+        self.win_idx = torch.full((B, args.window_size), -1, dtype=I32, device=dev)
+        self.side = torch.cuda.Stream(dev) if dev.type == "cuda" else None
         H, D = args.n_heads, args.head_dim
         ws_attn = 0
         # few long rows: the multi-CTA top-k (one CTA per row would idle the GPU)
@@ -315,18 +324,38 @@ class SeqShard:
         p = torch.as_tensor(pos, dtype=I32).reshape(-1).expand(self.B).contiguous()
         self.pos.copy_(p.to(self.device))
         self.t_active.copy_(((p + 1) // self.args.compress_ratio).to(self.device))
+        self._per_step()
+
+    def _per_step(self) -> None:
+        """What depends only on the positions, once per step for all layers:
+        this shard's T_active and the window ring indices."""
+        o, n = self.ops, self.n_local
+        o.shard_active(self.t_active, self.lo, n, out=self.t_local)
+        if self.rank == self.window_rank:
+            o.window_indices(self.pos, self.args.window_size, out=self.win_idx)
 
     # ---- phase 1: everything before the candidate exchange
     def phase_local(self, L: SeqShardLayer, x: LayerInputs) -> None:
         a, o = self.args, self.ops
         W, r, n = a.window_size, a.compress_ratio, self.n_local
-        o.kv_window_write(x.kv, L.kv_window(n), self.pos, W, rope_dim=a.rope_head_dim)
+        side = self.side
+        if side is not None:
+            # window write and attention compressor feed only the attention:
+            # a side branch, joined in phase_attend
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            ctx = torch.cuda.stream(side)
+        else:
+            ctx = _nullctx()
+        with ctx:
+            o.kv_window_write(x.kv, L.kv_window(n), self.pos, W, rope_dim=a.rope_head_dim)
+            o.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
+                              L.kv_compressed(max(n, 1)) if n else L.kv[:, :1], -self.lo if n else -(1 << 30),
+                              self.pos, r, overlap=True, rotate=False, eps=a.norm_eps, rope_dim=a.rope_head_dim)
         o.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos, self.sin,
                           L.keys[:, :max(n, 1)], -self.lo, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
                           rope_dim=a.rope_head_dim)
         if n == 0:
             return
-        o.shard_active(self.t_active, self.lo, n, out=self.t_local)
         o.indexer_score(x.iq, L.keys, x.iw, n, out=L.score, t_valid=self.t_local)
         kn = min(self.kc, n)
         if self.use_wide:
@@ -360,13 +389,10 @@ class SeqShard:
                 o.topk_merge(cs, ci, self.k, 0, out=L.sel)
             L.selected = L.sel
         attend_window = self.rank == self.window_rank
-        if attend_window:
-            o.window_indices(self.pos, W, out=L.win_idx)
-        o.shard_local_indices(L.selected, self.lo, self.hi, W, L.win_idx if attend_window else None, local_base=0,
-                              win_base=n, out=L.lidx)
-        o.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
-                          L.kv_compressed(max(n, 1)) if n else L.kv[:, :1], -self.lo if n else -(1 << 30),
-                          self.pos, r, overlap=True, rotate=False, eps=a.norm_eps, rope_dim=a.rope_head_dim)
+        o.shard_local_indices(L.selected, self.lo, self.hi, W, self.win_idx if attend_window else None,
+                              local_base=0, win_base=n, out=L.lidx)
+        if self.side is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.side)
         o.sparse_attn_partial(x.q, L.kv, L.lidx, self.scale, part_ml=L.pml, part_o=L.po, ws=self.ws,
                               status=self.status)
 
@@ -380,6 +406,7 @@ class SeqShard:
 
     def advance(self) -> None:
         self.ops.advance_positions(self.pos, self.t_active, self.args.compress_ratio, 1)
+        self._per_step()
 
 
 class SeqSplitPath:

@@ -26,7 +26,10 @@ reference's order (inference.py:5888-6093):
 
 and then advances the device-resident positions, so a captured CUDA graph
 of the whole step can be replayed without any host work (the reference
-needs two traces and host staging per step, inference.py:7498-7543).
+needs two traces and host staging per step, inference.py:7498-7543).  The
+window write and the attention compressor feed only the attention, so they
+run on a side stream in parallel with the indexer chain (a parallel branch
+of the captured graph).
 """
 
 from __future__ import annotations
@@ -181,6 +184,9 @@ class DecodePath:
         self.t_active = torch.zeros(self.B, dtype=I32, device=self.device)
         self.status = torch.zeros(1, dtype=I32, device=self.device)
         self.graph = None
+        # the window write and the attention compressor depend on nothing of
+        # the indexer chain: they run on a side stream, joined before attention
+        self.side = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
 
     def set_positions(self, pos) -> None:
         """Stage the current decode position(s) (pre_stage_decode,
@@ -192,16 +198,23 @@ class DecodePath:
     def layer_step(self, L: DecodeLayer, x: LayerInputs, out: torch.Tensor) -> None:
         a = self.args
         W, r = L.win, L.ratio
-        ops.kv_window_write(x.kv, L.kv_cache, self.pos, W, rope_dim=a.rope_head_dim)
+        main = torch.cuda.current_stream(self.device)
+        side = self.side
+        # side branch: attn.kv window write and attn.compress (both only feed the attention)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            ops.kv_window_write(x.kv, L.kv_cache, self.pos, W, rope_dim=a.rope_head_dim)
+            ops.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
+                                L.kv_cache, W, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
+                                rope_dim=a.rope_head_dim)
+        # main branch: attn.topk
         ops.window_indices(self.pos, W, out=L.idx[:, :W])
         ops.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos, self.sin,
                             L.idx_cache, 0, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
                             rope_dim=a.rope_head_dim)
         ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_active)
         ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws)
-        ops.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
-                            L.kv_cache, W, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
-                            rope_dim=a.rope_head_dim)
+        main.wait_stream(side)
         ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, self.scale, out=out, ws=L.ws, status=self.status)
 
     def step(self, inputs: list[LayerInputs], outs: list[torch.Tensor], advance: bool = True) -> None:
