@@ -49,14 +49,21 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel timings to stderr")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4"], default="cfg2",
-                    help="cfg2: batched decode, batch split; cfg3: one 256k context, sequence split; "
+    ap.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg2",
+                    help="cfg0: one layer, batch 1, 4096-token context; cfg1: compressor emit path alone; "
+                         "cfg2: batched decode, batch split; cfg3: one 256k context, sequence split; "
                          "cfg4: 4096-token prefill chunk")
     ap.add_argument("--comm", choices=["p2p", "nccl"], default="p2p",
                     help="cfg3 exchanges: peer-memory stores over NVLink, or NCCL all-gathers")
     a = ap.parse_args()
     if a.workload == "cfg3" and "--ctx" not in sys.argv:
         a.ctx = 262144
+    if a.workload == "cfg0":
+        # 43 independent single-layer problems per step, so the timed working set exceeds L2
+        for flag, attr, val in (("--batch", "batch", 1), ("--ctx", "ctx", 4096), ("--topk", "topk", 512),
+                                ("--layers", "layers", 43)):
+            if flag not in sys.argv:
+                setattr(a, attr, val)
     return a
 
 
@@ -320,6 +327,9 @@ def main():
     if args.workload == "cfg4":
         run_cfg4(args, rank, world, dev)
         return
+    if args.workload == "cfg1":
+        run_cfg1(args, rank, world, dev)
+        return
 
     log("building layers")
     pa, path, inputs, outs = build_path(args, dev, seed=1234 + rank)
@@ -395,11 +405,15 @@ def main():
             "step_hbm_gbs": round(step_gbs, 1), "step_hbm_frac": round(step_gbs / hbm, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) caches/inputs, indexer weights N(0,0.02), random-init layer params)",
-            "config": {"workload": "cfg2 batched decode: 43 layers, 64 seq/GPU, ctx 32768 (8192 compressed), "
-                                   "indexer top-2048 + window 128, H=64 D=512, Hi=64 Di=128",
+            "config": {"workload": (f"cfg2 batched decode: {args.layers} layers, {args.batch} seq/GPU, ctx {args.ctx} "
+                                    f"({args.ctx // 4} compressed), indexer top-{args.topk} + window 128, "
+                                    "H=64 D=512, Hi=64 Di=128") if args.workload == "cfg2" else
+                                   (f"cfg0 single-layer decode step: batch {args.batch}, ctx {args.ctx} "
+                                    f"({args.ctx // 4} compressed), top-{args.topk} + window 128"),
                        "global_batch": args.batch * world, "seq_len": args.ctx, "layers": args.layers,
                        "parallelism": f"dp{world} (batch split, no collective)",
-                       "l2": "working set 29 GB/GPU >> 126 MB L2; no flush needed"},
+                       "l2": f"working set {sum(L.nbytes() for L in path.layers) / 1e9:.2f} GB/GPU vs 126 MB L2; "
+                             "no flush between steps (each layer's caches are read once per step)"},
             "roofline": roofline, "clocks": clk, "gpu_launches": path.launches_per_step() * args.steps,
         }
         if e2e is not None:
@@ -560,6 +574,72 @@ def run_cfg3(args, rank, world, dev):
         dist.barrier()
         comm.close()
         dist.destroy_process_group()
+
+
+def run_cfg1(args, rank, world, dev):
+    """Config 1: the compressor emit path alone - batch 32, d 512, ratio 4,
+    the [32, 4, 512] state (one slot per step, non-overlap form), softmax
+    over slots, weighted sum, RMSNorm, emit every 4th step; 1000 steps from
+    position 0, positions advanced on the device, one CUDA graph per step.
+    Launch-bound by nature; reported as us per step."""
+    import torch
+    from dsv4attn import ops
+    from dsv4attn.tables import PathArgs, rope_cos_sin
+    B, d, r, steps = 32, 512, 4, 1000
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    kv_row = torch.randn(B, d, device=dev, generator=g).to(torch.bfloat16)
+    sc_row = torch.randn(B, d, device=dev, generator=g).to(torch.bfloat16)
+    ape = 0.1 * torch.randn(r, d, device=dev, generator=g)
+    gamma = 1 + 0.02 * torch.randn(d, device=dev, generator=g)
+    kv_state = torch.zeros(B, r, d, device=dev)
+    sc_state = torch.full((B, r, d), float("-inf"), device=dev)
+    cos, sin = rope_cos_sin(PathArgs(), steps + 64, compressed=True, device=dev)
+    cache = torch.zeros(B, steps // r + 2, d, dtype=torch.bfloat16, device=dev)
+    pos = torch.zeros(B, dtype=torch.int32, device=dev)
+    emitted = torch.zeros(B, dtype=torch.int32, device=dev)
+
+    def one():
+        ops.compressor_step(kv_row, sc_row, ape, kv_state, sc_state, gamma, cos, sin, cache, 0, pos, r, False,
+                            emitted=emitted)
+        ops.advance_positions(pos, None, r, 1)
+
+    s_ = torch.cuda.Stream(dev)
+    s_.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s_):
+        one()
+    torch.cuda.current_stream(dev).wait_stream(s_)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        one()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = None
+    for _ in range(max(1, args.warmup) + 3):
+        pos.zero_()
+        kv_state.zero_()
+        sc_state.fill_(float("-inf"))
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(steps):
+            gr.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    us_step = best * 1e3 / steps
+    n_emit = int((cache.float().abs().sum(-1) > 0).sum().item()) // B
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(B * 1e6 / us_step, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 5),
+            "us_per_step": round(us_step, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded N(0,1) rows, ape N(0,0.1), gamma 1+N(0,0.02))",
+            "config": {"workload": f"cfg1 compressor emit path: batch {B}, d {d}, ratio {r}, [32,4,512] state, "
+                                   f"{steps} steps, emit every 4th ({n_emit} emitted rows per sequence)",
+                       "global_batch": B, "parallelism": "replicas"},
+            "note": "one compressor launch + one position advance per step, graph-replayed; launch-bound"}),
+            flush=True)
 
 
 def run_cfg4(args, rank, world, dev):
