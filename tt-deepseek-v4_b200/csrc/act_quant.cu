@@ -91,6 +91,8 @@ __global__ void __launch_bounds__(256) kv_window_write_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nope = D - rope_dim;
   const int nblk = nope / 64;
+  pdl_wait();
+  pdl_launch_dependents();
   const int p = pos[b];
   const int slot = ((p % win) + win) % win;
   const __nv_bfloat16* src = kv + int64_t(b) * D;
@@ -149,9 +151,9 @@ extern "C" int dsa_kv_window_write(const void* kv, void* kv_cache, float* scales
   DSA_CHECK_ARG(aligned(kv, 4) && aligned(kv_cache, 4) && D % 2 == 0 && cache_bstride % 2 == 0,
                 "kv_window_write: kv/kv_cache must be 4-byte aligned");
   if (B == 0) return DSA_OK;
-  kv_window_write_kernel<<<B, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(kv), static_cast<__nv_bfloat16*>(kv_cache), scales, pos, D, rope_dim,
-      cache_bstride, win, 448.f, 1e-4f);
+  launch_pdl(kv_window_write_kernel, dim3(B), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(kv), static_cast<__nv_bfloat16*>(kv_cache), scales, pos, D, rope_dim,
+             cache_bstride, win, 448.f, 1e-4f);
   DSA_CHECK_LAUNCH("kv_window_write");
   return DSA_OK;
 }

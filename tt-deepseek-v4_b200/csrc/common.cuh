@@ -10,6 +10,7 @@
 #include <stdio.h>
 #include <string>
 #include <algorithm>
+#include <utility>
 
 #include "../../include/dsv4attn.h"
 
@@ -105,6 +106,36 @@ __device__ __forceinline__ void mma_bf16_16816(float* d, const uint32_t* a, cons
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// ---------------------------------------------- programmatic dependent launch
+// Kernels of the decode chain are launched with programmatic stream
+// serialisation: the next kernel of the stream may start (set up shared
+// memory, barriers, TMEM) while this one drains.  Every such kernel calls
+// pdl_wait() before its first global-memory access - it returns once the
+// previous kernel of the stream has completed and its writes are visible
+// (immediately when the launch had no programmatic dependency) - and then
+// pdl_launch_dependents(), which lets the next kernel be scheduled once all
+// CTAs of this one have reached it.  No CTA touches global memory before its
+// wait, so reads after writes and writes after reads across the chain keep
+// stream order.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // order-preserving map float -> uint32 (larger float -> larger key)

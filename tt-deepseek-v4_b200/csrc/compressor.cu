@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(kCmpThreads) compressor_step_kernel(
   __shared__ float s_red[32];
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
   const int p = pos[b];
   const int coff = overlap ? 2 : 1;
   const int cd = coff * d;
@@ -223,11 +225,11 @@ extern "C" int dsa_compressor_step(const void* kv_row, const void* score_row, in
   DSA_CHECK_ARG(!rotate || (d & (d - 1)) == 0, "compressor_step: Hadamard needs power-of-two d (got %d)", d);
   if (B == 0) return DSA_OK;
   const float had_scale = (float)(1.0 / sqrt((double)d));
-  compressor_step_kernel<<<B, kCmpThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(kv_row), static_cast<const __nv_bfloat16*>(score_row), ld_row, ape,
-      kv_state, score_state, gamma, cos_tab, sin_tab, n_pos, static_cast<__nv_bfloat16*>(kv_cache), cache_bstride,
-      cache_rows, slot_offset, pos, emitted, d, rope_dim, ratio, overlap ? 1 : 0, rotate ? 1 : 0,
-      write_state ? 1 : 0, had_scale, eps);
+  launch_pdl(compressor_step_kernel, dim3(B), dim3(kCmpThreads), 0, reinterpret_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(kv_row), static_cast<const __nv_bfloat16*>(score_row), ld_row, ape,
+             kv_state, score_state, gamma, cos_tab, sin_tab, n_pos, static_cast<__nv_bfloat16*>(kv_cache),
+             cache_bstride, cache_rows, slot_offset, pos, emitted, d, rope_dim, ratio, overlap ? 1 : 0,
+             rotate ? 1 : 0, write_state ? 1 : 0, had_scale, eps);
   DSA_CHECK_LAUNCH("compressor_step");
   return DSA_OK;
 }

@@ -223,8 +223,8 @@ extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, f
     a.ld_score = ld_score;
     a.k_row_stride = row_stride;
     const int grid = (total + a.items_per_cta - 1) / a.items_per_cta;
-    idxtc::indexer_score_tc_kernel<<<grid, idxtc::THREADS, idxtc::kSmemBytes,
-                                     reinterpret_cast<cudaStream_t>(stream)>>>(a, tm_k, tm_q);
+    launch_pdl(idxtc::indexer_score_tc_kernel, dim3(grid), dim3(idxtc::THREADS), idxtc::kSmemBytes,
+               reinterpret_cast<cudaStream_t>(stream), a, tm_k, tm_q);
   }
   DSA_CHECK_LAUNCH("indexer_score");
   return DSA_OK;

@@ -92,6 +92,10 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = aux->tmem_base;
+  // set-up above touches no global memory; keys, q, w and t_valid are the
+  // previous kernels' outputs
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer

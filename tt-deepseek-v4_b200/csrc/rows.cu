@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(32 * kRowWarps) head_norm_rope_kernel(
     const int32_t* __restrict__ pos, int inverse, int32_t* __restrict__ status) {
   const int lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_launch_dependents();
   if (row >= int64_t(B) * H) return;
   const int b = int(row / H), h = int(row - int64_t(b) * H);
   const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(x + int64_t(b) * ld_x + int64_t(h) * Dh);
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(1024) kv_norm_rope_write_kernel(
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
+  pdl_wait();
+  pdl_launch_dependents();
   const int c0 = warp * 64 + 2 * lane;
   const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kv + int64_t(b) * ld_kv + c0));
   float ss = fmaf(v.y, v.y, v.x * v.x);
@@ -166,9 +170,9 @@ extern "C" int dsa_head_norm_rope(const void* x, int64_t ld_x, void* out, int64_
   if (B == 0) return DSA_OK;
   const int64_t rows = int64_t(B) * H;
   const int grid = int((rows + kRowWarps - 1) / kRowWarps);
-  head_norm_rope_kernel<<<grid, 32 * kRowWarps, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<__nv_bfloat16*>(out), ld_out, B, H, Dh, rope_dim,
-      gamma, weight, do_norm ? 1 : 0, eps, cos_tab, sin_tab, n_pos, pos, inverse ? 1 : 0, status);
+  launch_pdl(head_norm_rope_kernel, dim3(grid), dim3(32 * kRowWarps), 0, reinterpret_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<__nv_bfloat16*>(out), ld_out, B, H, Dh, rope_dim,
+             gamma, weight, do_norm ? 1 : 0, eps, cos_tab, sin_tab, n_pos, pos, inverse ? 1 : 0, status);
   DSA_CHECK_LAUNCH("head_norm_rope");
   return DSA_OK;
 }
@@ -191,10 +195,10 @@ extern "C" int dsa_kv_norm_rope_window_write(const void* kv, int64_t ld_kv, cons
                 "kv_norm_rope_window_write: bad kv_out");
   DSA_CHECK_ARG(eps > 0.f, "kv_norm_rope_window_write: eps must be positive");
   if (B == 0) return DSA_OK;
-  kv_norm_rope_write_kernel<<<B, (D / 64) * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(kv), ld_kv, gamma, eps, cos_tab, sin_tab, n_pos, pos,
-      static_cast<__nv_bfloat16*>(kv_cache), cache_bstride, win, static_cast<__nv_bfloat16*>(kv_out), ld_out,
-      scales, D, rope_dim, 448.f, 1e-4f, status);
+  launch_pdl(kv_norm_rope_write_kernel, dim3(B), dim3((D / 64) * 32), 0, reinterpret_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(kv), ld_kv, gamma, eps, cos_tab, sin_tab, n_pos, pos,
+             static_cast<__nv_bfloat16*>(kv_cache), cache_bstride, win, static_cast<__nv_bfloat16*>(kv_out), ld_out,
+             scales, D, rope_dim, 448.f, 1e-4f, status);
   DSA_CHECK_LAUNCH("kv_norm_rope_window_write");
   return DSA_OK;
 }

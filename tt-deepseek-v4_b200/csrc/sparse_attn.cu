@@ -289,6 +289,8 @@ __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
     float* __restrict__ lse, float* __restrict__ out_ml, float* __restrict__ out_o) {
   const int m = blockIdx.x, lane = threadIdx.x & 31;
   const int h = blockIdx.y * kCombineWarps + (threadIdx.x >> 5);
+  pdl_wait();
+  pdl_launch_dependents();
   if (h >= H) return;
   auto ml = [&](int p, int j) { return part_ml[int64_t(p) * ml_ps + (int64_t(m) * H + h) * 2 + j]; };
   float Mx = final_mode ? sink[h] : -INFINITY;
@@ -356,11 +358,11 @@ static void launch_lse_combine(const float* part_ml, const float* part_o, const 
   if (ml_ps < 0) ml_ps = int64_t(M) * H * 2;
   if (o_ps < 0) o_ps = int64_t(M) * H * D;
   if (int64_t(M) * hb < 2 * num_sms()) {
-    lse_combine_kernel<4><<<dim3(M, hb, D / 128), 32 * kCombineWarps, 0, st>>>(
-        part_ml, part_o, sink, P, M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
+    launch_pdl(lse_combine_kernel<4>, dim3(M, hb, D / 128), dim3(32 * kCombineWarps), 0, st, part_ml, part_o, sink, P,
+               M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
   } else {
-    lse_combine_kernel<16><<<dim3(M, hb, D / 512), 32 * kCombineWarps, 0, st>>>(
-        part_ml, part_o, sink, P, M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
+    launch_pdl(lse_combine_kernel<16>, dim3(M, hb, D / 512), dim3(32 * kCombineWarps), 0, st, part_ml, part_o, sink,
+               P, M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
   }
 }
 
@@ -515,7 +517,8 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
       set_error("sparse_attn: cuTensorMapEncodeTiled failed");
       return DSA_ERR_CUDA;
     }
-    satc::sparse_attn_tc_kernel<<<dim3(p.nsplit, M), satc::THREADS, satc::kSmemBytes, st>>>(t, tm_q, row_stride);
+    launch_pdl(satc::sparse_attn_tc_kernel, dim3(p.nsplit, M), dim3(satc::THREADS), satc::kSmemBytes, st, t, tm_q,
+               row_stride);
   }
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {

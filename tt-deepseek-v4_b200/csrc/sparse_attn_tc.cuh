@@ -164,17 +164,6 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   long long* tr = (a.trace && blockIdx.x == 0 && blockIdx.y == 0) ? a.trace : nullptr;
   if (tid == 0) SA_TRACE(kTrMisc, 0);
 
-  // The split's index list, staged once: -1 for masked / padding slots,
-  // out-of-range rows clamped (and reported through status).
-  for (int e = tid; e < n * TK; e += THREADS) {
-    const int j = j_begin + e;
-    int id = (j < j_end) ? idxr[j] : -1;
-    if (id >= a.kv_rows) {
-      if (a.status) atomicOr(a.status, kStatusBadIndex);
-      id = int(a.kv_rows - 1);
-    }
-    s_idx[e] = id < 0 ? -1 : id;
-  }
   if (tid < H) aux->m[tid] = -INFINITY;
   if (tid == 0) aux->abort = 0;
 
@@ -198,6 +187,21 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     }
     tc::mbar_init(smem_u32(&aux->mma_done), 1);
     tc::mbar_fence_init();
+  }
+  // set-up above touches no global memory; the index list and q are the
+  // previous kernels' outputs
+  pdl_wait();
+  pdl_launch_dependents();
+  // The split's index list, staged once: -1 for masked / padding slots,
+  // out-of-range rows clamped (and reported through status).
+  for (int e = tid; e < n * TK; e += THREADS) {
+    const int j = j_begin + e;
+    int id = (j < j_end) ? idxr[j] : -1;
+    if (id >= a.kv_rows) {
+      if (a.status) atomicOr(a.status, kStatusBadIndex);
+      id = int(a.kv_rows - 1);
+    }
+    s_idx[e] = id < 0 ? -1 : id;
   }
   tc::fence_before_sync();
   __syncthreads();

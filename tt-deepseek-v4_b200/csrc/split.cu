@@ -13,6 +13,8 @@ namespace dsa {
 // t_local[b] = clamp(t_active[b] - lo, 0, n_local)
 __global__ void shard_active_kernel(const int32_t* __restrict__ t_active, int32_t* __restrict__ t_local, int B,
                                     int lo, int n_local) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) t_local[b] = min(max(t_active[b] - lo, 0), n_local);
 }
@@ -25,6 +27,8 @@ __global__ void shard_local_indices_kernel(const int32_t* __restrict__ sel, int6
                                            int hi, int local_base, int win_base, int32_t* __restrict__ out,
                                            int64_t ld_out) {
   const int b = blockIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
   const int32_t* s = sel + int64_t(b) * ld_sel;
   int32_t* o = out + int64_t(b) * ld_out;
   for (int j = threadIdx.x; j < W; j += blockDim.x) {
@@ -75,8 +79,8 @@ extern "C" int dsa_shard_active(const int32_t* t_active, int32_t* t_local, int B
   clear_error();
   DSA_CHECK_ARG(t_active && t_local && B >= 0 && lo >= 0 && n_local >= 0, "shard_active: bad arguments");
   if (B == 0) return DSA_OK;
-  shard_active_kernel<<<(B + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(t_active, t_local, B,
-                                                                                          lo, n_local);
+  launch_pdl(shard_active_kernel, dim3((B + 127) / 128), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream),
+             t_active, t_local, B, lo, n_local);
   DSA_CHECK_LAUNCH("shard_active");
   return DSA_OK;
 }
@@ -90,8 +94,8 @@ extern "C" int dsa_shard_local_indices(const int32_t* sel, int64_t ld_sel, int k
                 "shard_local_indices: bad strides");
   DSA_CHECK_ARG(lo >= 0 && hi >= lo && local_base >= 0 && win_base >= 0, "shard_local_indices: bad shard range");
   if (B == 0) return DSA_OK;
-  shard_local_indices_kernel<<<B, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      sel, ld_sel, k, win_idx, ld_win, W, lo, hi, local_base, win_base, out, ld_out);
+  launch_pdl(shard_local_indices_kernel, dim3(B), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), sel, ld_sel, k,
+             win_idx, ld_win, W, lo, hi, local_base, win_base, out, ld_out);
   DSA_CHECK_LAUNCH("shard_local_indices");
   return DSA_OK;
 }

@@ -405,6 +405,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
   const int b = blockIdx.y, c = blockIdx.x, n_chunks = gridDim.x;
   const int t0 = c * chunk;
   const int n = min(T, t0 + chunk) - t0;
+  pdl_wait();
+  pdl_launch_dependents();
   const int ta = t_active[b];
   const float* row = score + int64_t(b) * ld_score + t0;
   // every load of a thread in flight before any use (n <= 16 x 1024)
@@ -456,6 +458,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(
   int32_t* ids = reinterpret_cast<int32_t*>(smem + kTopkMaxN * 4);
   uint8_t* scratch = smem + kTopkMaxN * 8;
   const int b = blockIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
   for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
     const int32_t id = cand_id[int64_t(b) * n_cand + i];
     uint32_t key;
@@ -471,6 +475,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(
 
 __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ idx, int64_t ld,
                                       int B, int win) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   const int p = pos[b];
   for (int i = threadIdx.x; i < win; i += blockDim.x) {
@@ -497,7 +503,8 @@ extern "C" int dsa_window_indices(const int32_t* pos, int32_t* idx, int64_t ld_i
   DSA_CHECK_ARG(pos && idx, "window_indices: null pointer");
   DSA_CHECK_ARG(B >= 0 && win > 0 && ld_idx >= win, "window_indices: bad B/win/ld");
   if (B == 0) return DSA_OK;
-  window_indices_kernel<<<B, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(pos, idx, ld_idx, B, win);
+  launch_pdl(window_indices_kernel, dim3(B), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream), pos, idx, ld_idx,
+             B, win);
   DSA_CHECK_LAUNCH("window_indices");
   return DSA_OK;
 }
@@ -527,9 +534,8 @@ static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_ac
     attr_dev = dev;
   }
   if (T <= kTopkMaxN) {
-    topk_chunk_kernel<<<dim3(1, B), kTopkThreads, chunk_smem(), st>>>(score, ld_score, t_active, T, T, k, win,
-                                                                     sort_desc, mask_mode, out_idx, out_score,
-                                                                     ld_out, nullptr, nullptr);
+    launch_pdl(topk_chunk_kernel, dim3(1, B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T, T,
+               k, win, sort_desc, mask_mode, out_idx, out_score, ld_out, (uint32_t*)nullptr, (int32_t*)nullptr);
     DSA_CHECK_LAUNCH("indexer_topk");
     return DSA_OK;
   }
@@ -542,11 +548,11 @@ static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_ac
   DSA_CHECK_ARG(int64_t(n_chunks) * k <= kTopkMaxN, "indexer_topk: T=%d k=%d exceeds the two-level merge", T, k);
   uint32_t* ck = static_cast<uint32_t*>(ws);
   int32_t* ci = reinterpret_cast<int32_t*>(ck + size_t(B) * n_chunks * k);
-  topk_chunk_kernel<<<dim3(n_chunks, B), kTopkThreads, chunk_smem(), st>>>(
-      score, ld_score, t_active, T, kTopkMaxN, k, win, 0, mask_mode, nullptr, nullptr, 0, ck, ci);
+  launch_pdl(topk_chunk_kernel, dim3(n_chunks, B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T,
+             (int)kTopkMaxN, k, win, 0, mask_mode, (int32_t*)nullptr, (float*)nullptr, (int64_t)0, ck, ci);
   DSA_CHECK_LAUNCH("indexer_topk(chunks)");
-  topk_merge_kernel<<<B, kTopkThreads, merge_smem(), st>>>(ck, nullptr, ci, n_chunks * k, k, win, sort_desc, 1,
-                                                            out_idx, out_score, ld_out);
+  launch_pdl(topk_merge_kernel, dim3(B), dim3(kTopkThreads), merge_smem(), st, (const uint32_t*)ck,
+             (const float*)nullptr, (const int32_t*)ci, n_chunks * k, k, win, sort_desc, 1, out_idx, out_score, ld_out);
   DSA_CHECK_LAUNCH("indexer_topk(merge)");
   return DSA_OK;
 }
@@ -568,6 +574,8 @@ extern "C" int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const i
 }
 
 __global__ void advance_positions_kernel(int32_t* pos, int32_t* t_active, int B, int ratio, int step) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) {
     const int p = pos[b] + step;
@@ -581,8 +589,8 @@ extern "C" int dsa_advance_positions(int32_t* pos, int32_t* t_active, int B, int
   clear_error();
   DSA_CHECK_ARG(pos && B >= 0 && ratio > 0, "advance_positions: bad arguments");
   if (B == 0) return DSA_OK;
-  advance_positions_kernel<<<(B + 127) / 128, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(pos, t_active, B,
-                                                                                               ratio, step);
+  launch_pdl(advance_positions_kernel, dim3((B + 127) / 128), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream),
+             pos, t_active, B, ratio, step);
   DSA_CHECK_LAUNCH("advance_positions");
   return DSA_OK;
 }
