@@ -430,22 +430,6 @@ def main():
         print(json.dumps(line), flush=True)
 
 
-class _SelfComm:
-    """World of one: the exchange is a copy."""
-
-    def exchange(self, L, phase):
-        if phase == 0:
-            L.cand_all[0].copy_(L.cand)
-        else:
-            L.part_all[0].copy_(L.part)
-
-    def end_step(self):
-        pass
-
-    def close(self):
-        pass
-
-
 def run_cfg3(args, rank, world, dev):
     """Config 3: batch 1, one context of args.ctx tokens (args.ctx / 4
     compressed entries), compressed KV and indexer keys split contiguously
@@ -481,7 +465,7 @@ def run_cfg3(args, rank, world, dev):
         x.iw.mul_(0.02)
         inputs.append(x)
     outs = [torch.empty(1, 64, 512, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
-    comm = (P2PComm(shard) if p2p else TorchDistComm()) if world > 1 else _SelfComm()
+    comm = (P2PComm(shard) if p2p else TorchDistComm()) if world > 1 else None
     path = SeqSplitPath(shard, comm)
     shard.set_positions(args.ctx - 1)
     torch.cuda.synchronize()

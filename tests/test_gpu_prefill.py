@@ -56,6 +56,7 @@ def _sets_match(got_idx, want_idx, score, n_raw, W):
     (64, 1024, 256, 4 * 1024 - 64, 127),   # full visibility, selection among ~1000
     (48, 512, 64, 200, 100),               # t_active 50..62 < k (invalid slots), short history
     (32, 2048, 512, 4000, 0),              # no raw history: the first windows are partly empty
+    (30, 700, 128, 2700, 127),             # S not a multiple of 4: the per-token (decode) kernel, shared keys
 ])
 def test_prefill_chunk_matches_oracle(cuda_dev, S, T, k, base, n_hist):
     c = _case(S + T, S, T, n_hist, base)

@@ -67,3 +67,25 @@ def test_seq_split_config3_size_equals_one_way(cuda_dev):
             assert set(sel1[s][0].tolist()) == set(selg[s][0].tolist()), (G, s)
             for g in range(G):
                 assert torch.allclose(outg[s][g].float(), one[s][0].float(), rtol=1e-2, atol=1e-2), (G, s, g)
+
+
+def test_single_shard_path_writes_final_output(cuda_dev):
+    """World of one through SeqSplitPath: the attention writes the final
+    output directly (no partial exchange, no combine) and matches the oracle."""
+    from dsv4attn.dist import SeqShard, SeqSplitPath
+    T_total, W, k, steps = 4096, 128, 512, 4
+    pos0 = 4 * T_total - 1 - steps - 3
+    max_seq = 4 * T_total + 64
+    args, full, inputs = make_case(55, 1, T_total, W, k, steps, pos0)
+    want, _ = oracle_outputs(args, full, inputs, pos0, max_seq)
+    shard = SeqShard(args, 1, T_total, 0, 1, cuda_dev, k=k, max_seq_len=max_seq)
+    load_shard(shard, full)
+    shard.set_positions(pos0)
+    path = SeqSplitPath(shard)
+    for s, x in enumerate(inputs):
+        xd = type(x)(*[t.to(cuda_dev) for t in x.tensors()])
+        out = torch.empty(1, args.n_heads, args.head_dim, dtype=BF16, device=cuda_dev)
+        path.step([xd], [out])
+        torch.cuda.synchronize()
+        assert torch.allclose(out.cpu().float(), want[s].float(), rtol=2e-2, atol=2e-2), s
+    assert int(shard.status.item()) == 0

@@ -35,7 +35,7 @@ def _ref(score, ta, k, win, mask_mode, dev):
 
 @pytest.mark.parametrize("kind", ["normal", "equal", "few", "quantized", "neg_inf", "tiny_range"])
 @pytest.mark.parametrize("B,T,k,mask_mode", [(1, 65536, 2048, 1), (2, 8192, 2048, 0), (1, 16384, 2048, 1),
-                                              (3, 1000, 1000, 0), (1, 4096, 7, 1)])
+                                              (3, 1000, 1000, 0), (1, 4096, 7, 1), (2, 300, 17, 1), (1, 1, 1, 0)])
 def test_topk_wide_equals_per_row_kernel(cuda_dev, kind, B, T, k, mask_mode):
     from dsv4attn import ops
     g = torch.Generator().manual_seed(T + k + B)

@@ -366,7 +366,9 @@ class SeqShard:
                            out=L.cand_idx[:, :kn], out_score=L.cand_score[:, :kn], ws=self.ws)
 
     # ---- phase 2: merge, local rows of the selection, partial attention
-    def phase_attend(self, L: SeqShardLayer, x: LayerInputs) -> None:
+    def phase_attend(self, L: SeqShardLayer, x: LayerInputs, out: torch.Tensor | None = None) -> None:
+        """With ``out`` and a single shard the attention writes the final
+        output (sink included) and no partial exchange or combine follows."""
         a, o = self.args, self.ops
         W, r, n = a.window_size, a.compress_ratio, self.n_local
         G, B, kc = self.world, self.B, self.kc
@@ -393,6 +395,12 @@ class SeqShard:
                               local_base=0, win_base=n, out=L.lidx)
         if self.side is not None:
             torch.cuda.current_stream(self.device).wait_stream(self.side)
+        if out is not None:
+            if G != 1:
+                raise ValueError("a final output from phase_attend needs a single shard")
+            o.sparse_attn(x.q, L.kv, L.lidx, L.sink, self.scale, out=out.view(B, a.n_heads, a.head_dim), ws=self.ws,
+                          status=self.status)
+            return
         o.sparse_attn_partial(x.q, L.kv, L.lidx, self.scale, part_ml=L.pml, part_o=L.po, ws=self.ws,
                               status=self.status)
 
@@ -410,14 +418,22 @@ class SeqShard:
 
 
 class SeqSplitPath:
-    """Runs a SeqShard's layers with the two all-gathers between phases."""
+    """Runs a SeqShard's layers with the two exchanges between phases (a
+    single shard needs no comm: ``comm=None``)."""
 
-    def __init__(self, shard: SeqShard, comm):
+    def __init__(self, shard: SeqShard, comm=None):
+        if comm is None and shard.world != 1:
+            raise ValueError("a split over several ranks needs a comm")
         self.shard = shard
         self.comm = comm
 
     def layer_step(self, L: SeqShardLayer, x: LayerInputs, out: torch.Tensor) -> None:
         s, c = self.shard, self.comm
+        if s.world == 1:
+            # one shard: its candidates are the selection and its attention the result
+            s.phase_local(L, x)
+            s.phase_attend(L, x, out)
+            return
         s.phase_local(L, x)
         c.exchange(L, 0)
         s.phase_attend(L, x)
@@ -427,7 +443,8 @@ class SeqSplitPath:
     def step(self, inputs, outs, advance: bool = True) -> None:
         for L, x, o in zip(self.shard.layers, inputs, outs):
             self.layer_step(L, x, o)
-        self.comm.end_step()
+        if self.comm is not None:
+            self.comm.end_step()
         if advance:
             self.shard.advance()
 
