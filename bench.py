@@ -361,13 +361,25 @@ def main():
     e1.record(st)
     torch.cuda.synchronize()
     ms_total = e0.elapsed_time(e1)
+    # per-replay times (separate loop, events around every replay) for median / min
+    per = []
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    for i in range(args.steps):
+        ev[2 * i].record(st)
+        graph.replay()
+        ev[2 * i + 1].record(st)
+    torch.cuda.synchronize()
+    per = sorted(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps))
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     if world > 1:
-        t = torch.tensor([ms_total], device=dev)
+        t = torch.tensor([ms_total, per[len(per) // 2], per[0]], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
+        ms_total = float(t[0].item())
+        per_med, per_min = float(t[1].item()), float(t[2].item())
+    else:
+        per_med, per_min = per[len(per) // 2], per[0]
     if int(path.status.item()) != 0:
         raise RuntimeError("an attention index fell outside the cache during the bench")
     ms_step = ms_total / args.steps
@@ -402,6 +414,7 @@ def main():
         line = {
             "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "us_per_layer": round(us_layer, 2),
+            "ms_per_step_median": round(per_med, 4), "ms_per_step_min": round(per_min, 4),
             "step_hbm_gbs": round(step_gbs, 1), "step_hbm_frac": round(step_gbs / hbm, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) caches/inputs, indexer weights N(0,0.02), random-init layer params)",

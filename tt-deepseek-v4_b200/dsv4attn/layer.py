@@ -200,15 +200,16 @@ class DecodePath:
         W, r = L.win, L.ratio
         main = torch.cuda.current_stream(self.device)
         side = self.side
-        # side branch: attn.kv window write and attn.compress (both only feed the attention)
+        # side branch: attn.kv window write, the window ring indices and
+        # attn.compress (all three only feed the attention)
         side.wait_stream(main)
         with torch.cuda.stream(side):
             ops.kv_window_write(x.kv, L.kv_cache, self.pos, W, rope_dim=a.rope_head_dim)
+            ops.window_indices(self.pos, W, out=L.idx[:, :W])
             ops.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
                                 L.kv_cache, W, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
                                 rope_dim=a.rope_head_dim)
-        # main branch: attn.topk
-        ops.window_indices(self.pos, W, out=L.idx[:, :W])
+        # main branch: attn.topk (the top-k writes idx[:, W:], disjoint from the window columns)
         ops.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos, self.sin,
                             L.idx_cache, 0, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
                             rope_dim=a.rope_head_dim)
