@@ -6,10 +6,10 @@
 // the softmax denominator once.  K = V = the 512-d latent row (MQA).
 //
 // Flash-decoding over key splits: one CTA per (query row, key split) runs
-// the tcgen05 kernel of sparse_attn_tc.cuh; the splits of a row are merged
-// with the sink counted once by the last CTA of the row to finish (a
-// per-row arrival counter in the workspace), or by lse_combine_kernel for
-// callers that hand in their own partials (the sequence split).
+// the tcgen05 kernel of sparse_attn_tc.cuh; a row with one split is
+// finished by that CTA (sink included), the splits of a row with several
+// are merged, with the sink counted once, by lse_combine_kernel (which also
+// merges the partials that the sequence split gathers from other GPUs).
 #include "common.cuh"
 #include "sparse_attn_tc.cuh"
 #include <stdlib.h>

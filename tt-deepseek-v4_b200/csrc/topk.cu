@@ -10,12 +10,14 @@
 // level histograms the live scores linearly in value between their min and
 // max into 256 bins (a monotone map, so exact; masked -inf positions are left
 // out when at least k keys lie above them), a one-warp suffix scan finds the
-// bin holding the k-th largest, and only that bin's keys are kept.  Heavily
-// clustered rows go through further levels that bin the survivors' keys over
-// their own range (each narrows it by 2^8).  Once at most 512 keys are left,
-// one warp bisects over their key bits with ballot counts.  A deterministic
-// compaction then emits every key above the threshold and the lowest-index
-// keys equal to it.  Rows longer than one CTA's shared-memory budget are cut
+// bin holding the k-th largest, and only that bin's keys are kept.  When at
+// most 256 are, each is ranked directly (one thread per candidate counts the
+// candidates above it).  Heavily clustered rows go through further levels
+// that bin the survivors' keys over their own range (each narrows it by
+// 2^8), or, with at most 512 left, one warp bisects over their key bits with
+// ballot counts.  A deterministic compaction (ballot ranks inside each warp,
+// one scan over the warp counts) then emits every key above the threshold
+// and the lowest-index keys equal to it, in position order.  Rows longer than one CTA's shared-memory budget are cut
 // into chunks whose local top-k lists are merged by the same select
 // (dsa_topk_merge), which is also the cross-GPU merge of the sequence split.
 #include "common.cuh"
@@ -134,17 +136,18 @@ __device__ __forceinline__ int gather_bin(const uint32_t (&r)[kKeysPerThread], i
   return (int)s->ncand;
 }
 
-// Finds the k-th largest of keys[0, n) (1 <= k <= n <= kTopkMaxN, blockDim.x
-// == kTopkThreads) and leaves it in s->prefix.  `cand` holds up to n keys.
-__device__ void kth_key_select(const uint32_t* keys, int n, int k, SelectScratch* s, uint32_t* cand) {
+// Candidates of a bin few enough for a direct rank: thread t takes candidate
+// t and counts the candidates above it and at or above it.
+constexpr int kRankMax = 256;
+
+// Finds the k-th largest of the n keys (1 <= k <= n <= kTopkMaxN, blockDim.x
+// == kTopkThreads) held in registers, r[j] = key tid + j * kTopkThreads (0
+// past n), and in shared memory (keys[i]), and leaves it in s->prefix; r is
+// clobbered.  `cand` holds up to n keys.
+__device__ void kth_key_select(uint32_t (&r)[kKeysPerThread], const uint32_t* keys, int n, int k, SelectScratch* s,
+                               uint32_t* cand) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int nj = (n + kTopkThreads - 1) / kTopkThreads;
-  uint32_t r[kKeysPerThread];
-#pragma unroll
-  for (int j = 0; j < kKeysPerThread; ++j) {
-    const int i = tid + j * kTopkThreads;
-    r[j] = i < n ? keys[i] : 0u;
-  }
   // level 0 over the keys above the floor (the key of -inf: masked positions
   // and padding sit at or below it), binned by score value
   const uint32_t kfloor = float_key(-INFINITY);
@@ -183,6 +186,29 @@ __device__ void kth_key_select(const uint32_t* keys, int n, int k, SelectScratch
   // otherwise (threshold at or below the floor, or non-finite scores) the
   // key levels below start from all keys
   for (int level = 0; level < 6 && !done; ++level) {
+    if (nc >= 0 && nc <= kRankMax) {
+      // the kl-th largest of the nc candidates: the value c with fewer than
+      // kl candidates above it and at least kl at or above it (every thread
+      // holding that value writes the same word)
+      if (tid < nc) {
+        const uint32_t c = cand[tid];
+        uint32_t gt = 0, ge = 0;
+        const int n4 = nc & ~3;
+        for (int u = 0; u < n4; u += 4) {
+          const uint4 v = *reinterpret_cast<const uint4*>(cand + u);
+          gt += (v.x > c) + (v.y > c) + (v.z > c) + (v.w > c);
+          ge += (v.x >= c) + (v.y >= c) + (v.z >= c) + (v.w >= c);
+        }
+        for (int u = n4; u < nc; ++u) {
+          gt += cand[u] > c;
+          ge += cand[u] >= c;
+        }
+        if (gt < (uint32_t)kl && (uint32_t)kl <= ge) s->prefix = c;
+      }
+      __syncthreads();
+      thr = s->prefix;
+      break;
+    }
     if (nc >= 0) {
 #pragma unroll
       for (int j = 0; j < kKeysPerThread; ++j) {
@@ -258,53 +284,6 @@ __device__ void kth_key_select(const uint32_t* keys, int n, int k, SelectScratch
   __syncthreads();
 }
 
-// Block exclusive scan of two counters (above, equal); returns offsets and
-// writes the block totals to tot_a / tot_e.
-__device__ void block_scan2(uint32_t a, uint32_t e, uint32_t& off_a, uint32_t& off_e, SelectScratch* s,
-                            uint32_t& tot_a, uint32_t& tot_e) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  uint32_t ia = a, ie = e;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t va = __shfl_up_sync(0xffffffffu, ia, o), ve = __shfl_up_sync(0xffffffffu, ie, o);
-    if (lane >= o) {
-      ia += va;
-      ie += ve;
-    }
-  }
-  if (lane == 31) {
-    s->warp_cnt[0][warp] = ia;
-    s->warp_cnt[1][warp] = ie;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t wa = lane < nw ? s->warp_cnt[0][lane] : 0, we = lane < nw ? s->warp_cnt[1][lane] : 0;
-    uint32_t xa = wa, xe = we;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t va = __shfl_up_sync(0xffffffffu, xa, o), ve = __shfl_up_sync(0xffffffffu, xe, o);
-      if (lane >= o) {
-        xa += va;
-        xe += ve;
-      }
-    }
-    if (lane < nw) {
-      s->warp_cnt[0][lane] = xa - wa;
-      s->warp_cnt[1][lane] = xe - we;
-    }
-    if (lane == 31) {
-      s->hist[0] = xa;  // block totals (hist is free at this point)
-      s->hist[1] = xe;
-    }
-  }
-  __syncthreads();
-  off_a = s->warp_cnt[0][warp] + ia - a;
-  off_e = s->warp_cnt[1][warp] + ie - e;
-  tot_a = s->hist[0];
-  tot_e = s->hist[1];
-  __syncthreads();
-}
-
 // Bitonic sort of n_pow2 (key, idx) pairs in shared memory: descending key,
 // ascending idx among equal keys.
 __device__ void bitonic_desc(uint64_t* v, int n_pow2) {
@@ -325,40 +304,78 @@ __device__ void bitonic_desc(uint64_t* v, int n_pow2) {
   }
 }
 
-// Selects the k best of (keys[i], ids[i]) for i < n and writes them out.
+// Selects the k best of (keys[i], ids[i]) for i < n and writes them out, in
+// ascending position order.  r holds the keys in registers (r[j] = key
+// tid + j * kTopkThreads, 0 past n) for the select; keys[] holds them in
+// shared memory for the compaction.
 // mode_final: out index = id + win when the masked score >= -1000, else -1;
 // otherwise the raw id is written (intermediate candidate lists).
 // `scratch` (kScratchBytes) holds a level's survivors during the select and the
 // (key, id) pairs of the optional descending sort afterwards.
-__device__ void select_and_emit(uint32_t* keys, const int32_t* ids, int n, int k, bool sort_desc, bool mode_final,
-                                int win, int32_t* out_idx, float* out_score, uint8_t* scratch,
-                                SelectScratch* s) {
-  kth_key_select(keys, n, k, s, reinterpret_cast<uint32_t*>(scratch));
+__device__ void select_and_emit(uint32_t (&r)[kKeysPerThread], const uint32_t* keys, const int32_t* ids, int n,
+                                int k, bool sort_desc, bool mode_final, int win, int32_t* out_idx, float* out_score,
+                                uint8_t* scratch, SelectScratch* s) {
+  kth_key_select(r, keys, n, k, s, reinterpret_cast<uint32_t*>(scratch));
   uint64_t* sort_buf = reinterpret_cast<uint64_t*>(scratch);
   const uint32_t thr = s->prefix;
-  // contiguous per-thread ranges keep the output in ascending position order
+  // Compaction: warp w walks positions [w * 32 * per, (w + 1) * 32 * per),
+  // 32 consecutive ones per step (conflict-free shared reads); ballots give
+  // each key's rank inside its warp, one scan over the 32 warp counts the
+  // warps' offsets.  Keys above the threshold, then the lowest-position
+  // keys equal to it, land in ascending position order.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int per = (n + blockDim.x - 1) / blockDim.x;
-  const int i0 = threadIdx.x * per, i1 = min(n, i0 + per);
+  const int base = warp * 32 * per;
   uint32_t ca = 0, ce = 0;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t key = keys[i];
-    ca += key > thr;
-    ce += key == thr;
+#pragma unroll 4
+  for (int j = 0; j < per; ++j) {
+    const int i = base + 32 * j + lane;
+    const uint32_t key = i < n ? keys[i] : 0u;
+    ca += __popc(__ballot_sync(0xffffffffu, i < n && key > thr));
+    ce += __popc(__ballot_sync(0xffffffffu, i < n && key == thr));
   }
-  uint32_t oa, oe, ta, te;
-  block_scan2(ca, ce, oa, oe, s, ta, te);
-  (void)te;
-  const int n_above = (int)ta;  // < k by the choice of thr
-  const int n_eq_take = k - n_above;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t key = keys[i];
-    int slot = -1;
-    if (key > thr) {
-      slot = (int)oa++;
-    } else if (key == thr) {
-      if ((int)oe < n_eq_take) slot = n_above + (int)oe;
-      ++oe;
+  if (lane == 0) {
+    s->warp_cnt[0][warp] = ca;
+    s->warp_cnt[1][warp] = ce;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t wa = lane < nw ? s->warp_cnt[0][lane] : 0, we = lane < nw ? s->warp_cnt[1][lane] : 0;
+    uint32_t xa = wa, xe = we;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t va = __shfl_up_sync(0xffffffffu, xa, o), ve = __shfl_up_sync(0xffffffffu, xe, o);
+      if (lane >= o) {
+        xa += va;
+        xe += ve;
+      }
     }
+    if (lane < nw) {
+      s->warp_cnt[0][lane] = xa - wa;
+      s->warp_cnt[1][lane] = xe - we;
+    }
+    if (lane == 31) s->kgt = xa;  // keys above the threshold, all warps
+  }
+  __syncthreads();
+  uint32_t oa = s->warp_cnt[0][warp], oe = s->warp_cnt[1][warp];
+  const int n_above = (int)s->kgt;  // < k by the choice of thr
+  const int n_eq_take = k - n_above;
+  const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll 4
+  for (int j = 0; j < per; ++j) {
+    const int i = base + 32 * j + lane;
+    const uint32_t key = i < n ? keys[i] : 0u;
+    const bool above = i < n && key > thr, eq = i < n && key == thr;
+    const uint32_t ma = __ballot_sync(0xffffffffu, above), me = __ballot_sync(0xffffffffu, eq);
+    int slot = -1;
+    if (above) {
+      slot = (int)(oa + __popc(ma & lt));
+    } else if (eq) {
+      const int re = (int)(oe + __popc(me & lt));
+      if (re < n_eq_take) slot = n_above + re;
+    }
+    oa += __popc(ma);
+    oe += __popc(me);
     if (slot >= 0) {
       const int32_t id = ids ? ids[i] : i;
       if (sort_desc) {
@@ -409,21 +426,29 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
   pdl_launch_dependents();
   const int ta = t_active[b];
   const float* row = score + int64_t(b) * ld_score + t0;
-  // every load of a thread in flight before any use (n <= 16 x 1024)
-  float v[kKeysPerThread];
+  // every load of a thread in flight before any use (n <= 16 x 1024); the
+  // keys stay in registers for the select and go to shared memory for the
+  // compaction
+  uint32_t r[kKeysPerThread];
 #pragma unroll
   for (int j = 0; j < kKeysPerThread; ++j) {
     const int i = threadIdx.x + j * kTopkThreads;
-    v[j] = i < n ? __ldg(row + i) : 0.f;
+    r[j] = i < n ? __float_as_uint(__ldg(row + i)) : 0u;
   }
 #pragma unroll
   for (int j = 0; j < kKeysPerThread; ++j) {
     const int i = threadIdx.x + j * kTopkThreads;
-    if (i < n) keys[i] = float_key((t0 + i < ta) ? v[j] : (mask_mode ? -INFINITY : __fsub_rn(v[j], 1.0e4f)));
+    if (i < n) {
+      const float v = __uint_as_float(r[j]);
+      r[j] = float_key((t0 + i < ta) ? v : (mask_mode ? -INFINITY : __fsub_rn(v, 1.0e4f)));
+      keys[i] = r[j];
+    } else {
+      r[j] = 0u;
+    }
   }
   __syncthreads();
   if (n_chunks == 1) {
-    select_and_emit(keys, nullptr, n, k, sort_desc != 0, true, win, out_idx + int64_t(b) * ld_out,
+    select_and_emit(r, keys, nullptr, n, k, sort_desc != 0, true, win, out_idx + int64_t(b) * ld_out,
                     out_score ? out_score + int64_t(b) * ld_out : nullptr, scratch, &s);
     return;
   }
@@ -433,7 +458,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
   __syncthreads();
   const int64_t base = (int64_t(b) * n_chunks + c) * k;
   // write keys of the selected candidates: emit ids into cand_id, then keys
-  select_and_emit(keys, ids, n, kk, false, false, 0, cand_id + base, nullptr, scratch, &s);
+  select_and_emit(r, keys, ids, n, kk, false, false, 0, cand_id + base, nullptr, scratch, &s);
   __syncthreads();
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     if (i < kk) {
@@ -460,16 +485,23 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(
   const int b = blockIdx.x;
   pdl_wait();
   pdl_launch_dependents();
-  for (int i = threadIdx.x; i < n_cand; i += blockDim.x) {
-    const int32_t id = cand_id[int64_t(b) * n_cand + i];
-    uint32_t key;
-    if (cand_key) key = cand_key[int64_t(b) * n_cand + i];
-    else key = float_key(cand_score[int64_t(b) * n_cand + i]);
-    ids[i] = id;
-    keys[i] = (id < 0) ? 0u : key;
+  uint32_t r[kKeysPerThread];
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    const int i = threadIdx.x + j * kTopkThreads;
+    r[j] = 0u;
+    if (i < n_cand) {
+      const int32_t id = cand_id[int64_t(b) * n_cand + i];
+      uint32_t key;
+      if (cand_key) key = cand_key[int64_t(b) * n_cand + i];
+      else key = float_key(cand_score[int64_t(b) * n_cand + i]);
+      ids[i] = id;
+      r[j] = (id < 0) ? 0u : key;
+      keys[i] = r[j];
+    }
   }
   __syncthreads();
-  select_and_emit(keys, ids, n_cand, k, sort_desc != 0, final_mode != 0, win, out_idx + int64_t(b) * ld_out,
+  select_and_emit(r, keys, ids, n_cand, k, sort_desc != 0, final_mode != 0, win, out_idx + int64_t(b) * ld_out,
                   out_score ? out_score + int64_t(b) * ld_out : nullptr, scratch, &s);
 }
 
