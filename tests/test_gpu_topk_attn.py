@@ -83,6 +83,28 @@ def test_indexer_score_t_valid(cuda_dev):
     assert (o[0, 100:] == 123.0).all() and (o[1] == 123.0).all()
 
 
+@pytest.mark.parametrize("B,T,zero_frac", [(300, 700, 0.2), (4500, 64, 0.2), (7, 1000, 0.9)])
+def test_indexer_score_ragged_t_valid(cuda_dev, B, T, zero_frac):
+    # ragged live lengths: empty sequences, partial last tiles, t_valid past T
+    # (clamped); 4500 sequences take the all-items walk, the others the
+    # live-tile split, and (7, 1000) leaves most CTAs without work
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B + T)
+    q = torch.randn(B, 64, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, T, 128, generator=g).to(torch.bfloat16)
+    w = 0.02 * torch.randn(B, 64, generator=g)
+    tv = torch.randint(0, T + 41, (B,), generator=g, dtype=torch.int32)
+    tv[torch.rand(B, generator=g) < zero_frac] = 0
+    out = torch.full((B, T), 123.0, device=cuda_dev)
+    ops.indexer_score(q.to(cuda_dev), k.to(cuda_dev), w.to(cuda_dev), T, out=out, t_valid=tv.to(cuda_dev))
+    want = O.indexer_score(q, k, w)
+    o = out.cpu()
+    lim = tv.clamp(max=T)
+    live = torch.arange(T)[None, :] < lim[:, None]
+    torch.testing.assert_close(o[live], want[live], rtol=1e-3, atol=1e-3 * float(want.abs().max()))
+    assert (o[~live] == 123.0).all()
+
+
 def test_topk_reference_case(cuda_dev):
     # T_PAD 128, bucket 128, k 64, T_active 50 (test_lk_d_topk.py:42-46, 219-224)
     from dsv4attn import ops

@@ -96,7 +96,8 @@ extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, f
     a.items_per_cta = (total + nsm - 1) / nsm;
     a.ld_score = ld_score;
     a.k_row_stride = row_stride;
-    const int grid = (total + a.items_per_cta - 1) / a.items_per_cta;
+    a.balanced = B <= idxtc::kMaxSeqBalanced ? 1 : 0;
+    const int grid = a.balanced ? std::min(nsm, total) : (total + a.items_per_cta - 1) / a.items_per_cta;
     launch_pdl(idxtc::indexer_score_tc_kernel, dim3(grid), dim3(idxtc::THREADS), idxtc::kSmemBytes,
                reinterpret_cast<cudaStream_t>(stream), a, tm_k, tm_q);
   }

@@ -2,8 +2,12 @@
 //
 // s[b, t] = sum_h w[b, h] * relu(q[b, h, :] . k[b, t, :])   (H = 64, Di = 128)
 //
-// Persistent kernel: one CTA per SM walks a contiguous range of
-// (sequence, 128-key tile) work items.  Roles:
+// Persistent kernel: one CTA per SM walks a contiguous range of the live
+// (sequence, 128-key tile) work items -- tiles below the sequence's t_valid;
+// each CTA first builds the per-sequence prefix of live tiles in shared
+// memory and takes an equal share of them (a split over all allocated tiles
+// left CTAs whose range missed the dead tails with ~12 % more work at
+// t_valid = 8192 of T = 9216).  Roles:
 //   warp 0      TMA producer: per item a [128 keys x 128] tile of the key
 //               cache and the sequence's [64 x 128] q (two 128-B-swizzled
 //               k-blocks each) into a 4-stage ring (48 KB per stage).
@@ -31,7 +35,9 @@ constexpr int kKeyBytes = TILE * DI * 2;   // 32 KB: 2 k-blocks of [128 rows x 1
 constexpr int kQBytes = H * DI * 2;        // 16 KB: 2 k-blocks of [64 rows x 128 B]
 constexpr int kStageBytes = kKeyBytes + kQBytes;
 constexpr int kOffAux = NS * kStageBytes;
-constexpr int kSmemBytes = kOffAux + 256 + 1024;
+constexpr int kMaxSeqBalanced = 4096;      // sequences the live-tile prefix holds
+constexpr int kOffPre = kOffAux + 256;
+constexpr int kSmemBytes = kOffPre + (kMaxSeqBalanced + 1) * 4 + 1024;
 constexpr uint32_t kTmemCols = 128;        // 2 accumulators x 64 columns
 constexpr uint32_t kIdesc = tc::idesc_bf16(128, 64, false, false);
 
@@ -41,7 +47,9 @@ struct Aux {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
+  int wsum[THREADS / 32];
 };
+static_assert(sizeof(Aux) <= 256, "aux block");
 
 struct Args {
   const float* w;
@@ -49,17 +57,51 @@ struct Args {
   const int32_t* t_valid;
   int32_t* status;
   int B, T, tiles_per_seq, items_per_cta;
+  int balanced;           // B <= kMaxSeqBalanced: split the live tiles evenly (items_per_cta unused)
   int64_t ld_score;
   int64_t k_row_stride;   // rows between consecutive sequences in the key map
 };
 
+__device__ __forceinline__ int seq_limit(const Args& a, int b) {
+  return a.t_valid ? min(a.T, max(0, a.t_valid[b])) : a.T;
+}
+
 __device__ __forceinline__ bool item_live(const Args& a, int item, int& b, int& t0, int& t_lim) {
   b = item / a.tiles_per_seq;
   t0 = (item - b * a.tiles_per_seq) * TILE;
-  t_lim = a.T;
-  if (a.t_valid) t_lim = min(a.T, max(0, a.t_valid[b]));
+  t_lim = seq_limit(a, b);
   return t0 < t_lim;
 }
+
+// This CTA's work items in order.  Balanced: live items [l, l_end) of the
+// live-tile prefix pre[] (pre[b] = live tiles of the sequences before b);
+// otherwise the item range [item, i_end), dead items skipped.
+struct ItemWalk {
+  const Args* a;
+  const int* pre;
+  int l, l_end, b, tile;
+  int item, i_end;
+  __device__ bool next(int& b_, int& t0, int& t_lim) {
+    if (pre) {
+      if (l >= l_end) return false;
+      b_ = b;
+      t0 = tile * TILE;
+      t_lim = seq_limit(*a, b);
+      ++l;
+      if (++tile >= pre[b + 1] - pre[b]) {
+        tile = 0;
+        do {
+          ++b;
+        } while (b < a->B && pre[b + 1] == pre[b]);
+      }
+      return true;
+    }
+    while (item < i_end) {
+      if (item_live(*a, item++, b_, t0, t_lim)) return true;
+    }
+    return false;
+  }
+};
 
 __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args a,
                                                                       const __grid_constant__ CUtensorMap tm_k,
@@ -69,9 +111,6 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
   Aux* aux = reinterpret_cast<Aux*>(smem + kOffAux);
   const uint32_t sbase = smem_u32(smem);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int total = a.B * a.tiles_per_seq;
-  const int i_begin = blockIdx.x * a.items_per_cta;
-  const int i_end = min(total, i_begin + a.items_per_cta);
 
   if (warp == 1) {
     tc::tmem_alloc(smem_u32(&aux->tmem_base), kTmemCols);
@@ -97,15 +136,61 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
   pdl_wait();
   pdl_launch_dependents();
 
+  ItemWalk walk{};
+  walk.a = &a;
+  if (a.balanced) {
+    // live tiles per sequence -> exclusive prefix (one block scan)
+    int* pre = reinterpret_cast<int*>(smem + kOffPre);
+    auto live = [&](int b) { return (seq_limit(a, b) + TILE - 1) / TILE; };
+    const int per = (a.B + THREADS - 1) / THREADS;
+    const int b0 = min(a.B, tid * per), b1 = min(a.B, b0 + per);
+    int loc = 0;
+    for (int b = b0; b < b1; ++b) loc += live(b);
+    int inc = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    if (lane == 31) aux->wsum[warp] = inc;
+    __syncthreads();
+    int run = inc - loc;
+    for (int w = 0; w < warp; ++w) run += aux->wsum[w];
+    for (int b = b0; b < b1; ++b) {
+      pre[b] = run;
+      run += live(b);
+    }
+    if (tid == THREADS - 1) pre[a.B] = run;
+    __syncthreads();
+    const int total_live = pre[a.B];
+    const int share = (total_live + gridDim.x - 1) / gridDim.x;
+    walk.pre = pre;
+    walk.l = min(total_live, int(blockIdx.x) * share);
+    walk.l_end = min(total_live, walk.l + share);
+    if (walk.l < walk.l_end) {
+      // the sequence holding live item l: the last b with pre[b] <= l
+      int lo = 0, hi = a.B - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= walk.l) lo = mid;
+        else hi = mid - 1;
+      }
+      walk.b = lo;
+      walk.tile = walk.l - pre[lo];
+    }
+  } else {
+    walk.i_end = min(a.B * a.tiles_per_seq, int(blockIdx.x + 1) * a.items_per_cta);
+    walk.item = int(blockIdx.x) * a.items_per_cta;
+  }
+
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
       tma::prefetch_map(&tm_k);
       tma::prefetch_map(&tm_q);
       int it = 0;
-      for (int item = i_begin; item < i_end; ++item) {
-        int b, t0, t_lim;
-        if (!item_live(a, item, b, t0, t_lim)) continue;
+      int b, t0, t_lim;
+      while (walk.next(b, t0, t_lim)) {
         const int s = it % NS;
         if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2);
         const uint32_t st = sbase + s * kStageBytes;
@@ -124,9 +209,8 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       int it = 0;
-      for (int item = i_begin; item < i_end; ++item) {
-        int b, t0, t_lim;
-        if (!item_live(a, item, b, t0, t_lim)) continue;
+      int b, t0, t_lim;
+      while (walk.next(b, t0, t_lim)) {
         const int s = it % NS, acc = it & 1;
         tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2);
         if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2);
@@ -153,9 +237,8 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
     int it = 0;
     int cur_b = -1;
     float wv[H];
-    for (int item = i_begin; item < i_end; ++item) {
-      int b, t0, t_lim;
-      if (!item_live(a, item, b, t0, t_lim)) continue;
+    int b, t0, t_lim;
+    while (walk.next(b, t0, t_lim)) {
       const int acc = it & 1;
       if (b != cur_b) {
 #pragma unroll
