@@ -35,7 +35,8 @@ def _ref(score, ta, k, win, mask_mode, dev):
 
 @pytest.mark.parametrize("kind", ["normal", "equal", "few", "quantized", "neg_inf", "tiny_range"])
 @pytest.mark.parametrize("B,T,k,mask_mode", [(1, 65536, 2048, 1), (2, 8192, 2048, 0), (1, 16384, 2048, 1),
-                                              (3, 1000, 1000, 0), (1, 4096, 7, 1), (2, 300, 17, 1), (1, 1, 1, 0)])
+                                              (3, 1000, 1000, 0), (1, 4096, 7, 1), (2, 300, 17, 1), (1, 1, 1, 0),
+                                              (1, 100000, 2048, 1)])
 def test_topk_wide_equals_per_row_kernel(cuda_dev, kind, B, T, k, mask_mode):
     from dsv4attn import ops
     g = torch.Generator().manual_seed(T + k + B)
@@ -62,7 +63,8 @@ def test_topk_wide_repeated_calls_reuse_workspace(cuda_dev):
     from dsv4attn import ops
     ws = ops.WideTopkWorkspace(cuda_dev)
     g = torch.Generator().manual_seed(1)
-    for T, B, k in ((65536, 1, 2048), (3000, 2, 100), (16384, 1, 2048), (65536, 1, 2048)):
+    for T, B, k in ((65536, 1, 2048), (3000, 2, 100), (100000, 1, 2048), (16384, 1, 2048), (100000, 1, 64),
+                    (65536, 1, 2048)):
         s = torch.randn(B, T, generator=g).to(cuda_dev)
         got = ops.topk_wide(s, k, 0, T=T, mask_mode=1, ws=ws)
         ta = torch.full((B,), T, dtype=torch.int32, device=cuda_dev)
