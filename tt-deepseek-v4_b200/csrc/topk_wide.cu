@@ -24,7 +24,11 @@
 // barriers are an arrival count plus a generation word with a clock-bounded
 // spin; a wait that runs out sets *status and the CTA returns.  The
 // histograms are zeroed again at the end of the launch, so the workspace must be zeroed once
-// before its first use (and again after a timeout).
+// before its first use (and again after a timeout).  Workspace layout: a
+// 64-byte header, the per-launch count and candidate slots of up to
+// kScratchCtas CTAs at fixed offsets, then one histogram block per row; the
+// slots are rewritten by every launch and never overlap a histogram block,
+// so one workspace serves launches of any row count.
 #include "common.cuh"
 
 namespace dsa {
@@ -39,6 +43,7 @@ constexpr int kStatusTimeout = 2;
 constexpr int kCap = 24;                 // level-0 bin keys one CTA may publish
 constexpr int kMaxCtasPerRow = 148;
 constexpr int kCandSmem = kCap * kMaxCtasPerRow;
+constexpr int kScratchCtas = 1024;       // CTAs of one launch the count / candidate slots hold
 
 struct RowWs {
   uint32_t hist[kLevels][kBins];
@@ -444,11 +449,15 @@ int wide_ctas_per_row(int B, int T) {
 }
 }  // namespace
 
+namespace {
+constexpr size_t kWideCountBytes = size_t(wide::kScratchCtas) * wide::kCountWords * sizeof(uint32_t);
+constexpr size_t kWideCandBytes = size_t(wide::kScratchCtas) * wide::kCap * sizeof(unsigned long long);
+constexpr size_t kWideRowsOffset = 64 + kWideCountBytes + kWideCandBytes;
+}  // namespace
+
 extern "C" size_t dsa_topk_wide_workspace_size(int B, int T) {
   if (B <= 0 || T <= 0) return 0;
-  const int cpr = wide_ctas_per_row(B, T);
-  return 64 + size_t(B) * sizeof(wide::RowWs) + size_t(B) * cpr * wide::kCountWords * sizeof(uint32_t) +
-         size_t(B) * cpr * wide::kCap * sizeof(unsigned long long);
+  return kWideRowsOffset + size_t(B) * sizeof(wide::RowWs);
 }
 
 extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t* ids, int64_t ld_ids,
@@ -479,12 +488,13 @@ extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t
               num_sms());
     return DSA_ERR_UNSUPPORTED;
   }
+  DSA_CHECK_ARG(int64_t(cpr) * B <= wide::kScratchCtas, "topk_wide: %d CTAs exceed the %d workspace slots",
+                cpr * B, wide::kScratchCtas);
   const int per_cta = (T + cpr - 1) / cpr;
   auto* base = static_cast<uint8_t*>(workspace);
-  auto* rows = reinterpret_cast<wide::RowWs*>(base + 64);
-  auto* counts = reinterpret_cast<uint32_t*>(base + 64 + size_t(B) * sizeof(wide::RowWs));
-  auto* cands = reinterpret_cast<unsigned long long*>(base + 64 + size_t(B) * sizeof(wide::RowWs) +
-                                                      size_t(B) * cpr * wide::kCountWords * sizeof(uint32_t));
+  auto* counts = reinterpret_cast<uint32_t*>(base + 64);
+  auto* cands = reinterpret_cast<unsigned long long*>(base + 64 + kWideCountBytes);
+  auto* rows = reinterpret_cast<wide::RowWs*>(base + kWideRowsOffset);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cpr, B);
