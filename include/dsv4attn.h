@@ -188,6 +188,22 @@ int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_a
                         int B, int T, int k, int win, int sort_desc, int mask_mode,
                         void* workspace, size_t workspace_bytes, dsa_stream_t stream);
 
+/* dsa_indexer_topk_ws with the score of each row's newest live entry,
+ * t = min(t_active[b], T) - 1, recomputed from the indexer inputs rather than
+ * read from `score`: sum_h w[b,h] relu(q[b,h,:] . k_cache[b,t,:]) (the same
+ * formula as dsa_indexer_score, heads summed in order).  The decode step
+ * then scores rows [0, t_active - 1) while the indexer compressor writes
+ * row t_active - 1 (inference.py:5260-5275 followed by 5823-5851; the
+ * reference runs the compressor first).  q [B, 64, 128] bf16 contiguous,
+ * k_cache rows of 128 bf16 with batch stride k_bstride elements (>= T * 128,
+ * a multiple of 8), w [B, 64] fp32; q and k_cache 16-byte aligned.
+ * Workspace as for dsa_indexer_topk_ws (NULL / 0 when T <= 16384). */
+int dsa_indexer_topk_newest(const float* score, int64_t ld_score, const int32_t* t_active,
+                            int32_t* out_idx, float* out_score, int64_t ld_out,
+                            int B, int T, int k, int win, int sort_desc, int mask_mode,
+                            const void* q, const void* k_cache, int64_t k_bstride, const float* w,
+                            void* workspace, size_t workspace_bytes, dsa_stream_t stream);
+
 /* Top-k of a few long rows spread over many CTAs: one cooperative launch
  * of cpr CTAs per row (cpr * B <= the SM count) running an MSD radix select
  * with grid-wide barriers, for rows too long / too few for one CTA each
@@ -200,8 +216,10 @@ int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_a
  * and slots with ids[t] < 0 count as -inf (the candidate merge of the split;
  * ties break towards the lower slot, so pass candidates in position order).
  * workspace: dsa_topk_wide_workspace_size(B, T) bytes, 16-byte aligned,
- * zeroed before its first use (the kernel leaves it zeroed; re-zero after a
- * timeout).  status (may be NULL): bit 2 set when a grid barrier timed out.
+ * zeroed before its first use (the kernel leaves its histograms zeroed, so
+ * one workspace serves calls of any B and T it is large enough for; re-zero
+ * after a timeout).  status (may be NULL): bit 2 set when a grid barrier
+ * timed out.
  * Returns DSA_ERR_UNSUPPORTED when the rows need more CTAs than SMs.
  * Replaces the ttnn.topk of _indexer_topk_body (inference.py:5841-5842) for
  * single long rows. */

@@ -105,6 +105,31 @@ def test_indexer_score_ragged_t_valid(cuda_dev, B, T, zero_frac):
     assert (o[~live] == 123.0).all()
 
 
+@pytest.mark.parametrize("B,T,k", [(64, 9216, 2048), (2, 20000, 512)])
+def test_indexer_topk_newest_recomputes_last_row(cuda_dev, B, T, k):
+    # the decode step scores rows [0, t_active - 1) while the compressor
+    # writes the newest row; the top-k must recompute that row's score (its
+    # stored value is planted wrong here) and select what scoring every row
+    # first selects; T = 20000 takes the two-level (chunk + merge) path
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B + T)
+    q = torch.randn(B, 64, 128, generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, T, 128, generator=g).to(torch.bfloat16)
+    w = 0.02 * torch.randn(B, 64, generator=g)
+    ta = torch.randint(k, T + 1, (B,), generator=g, dtype=torch.int32)
+    ta[0], ta[-1] = T, k
+    W = 128
+    qd, kd, wd, tad = q.to(cuda_dev), kc.to(cuda_dev), w.to(cuda_dev), ta.to(cuda_dev)
+    score = torch.zeros(B, T, device=cuda_dev)
+    ops.indexer_score(qd, kd, wd, T, out=score, t_valid=tad - 1)
+    score[torch.arange(B, device=cuda_dev), (tad - 1).long()] = 1e6
+    got = ops.indexer_topk(score, tad, k, W, T=T, mask_mode=1, refresh=(qd, kd, wd)).cpu()
+    full = O.indexer_score(q, kc, w)
+    masked = full.masked_fill(torch.arange(T)[None, :] >= ta[:, None], float("-inf"))
+    want = torch.topk(masked, k, dim=1).indices.int() + W
+    assert_topk_sets(got, want, masked, W)
+
+
 def test_topk_reference_case(cuda_dev):
     # T_PAD 128, bucket 128, k 64, T_active 50 (test_lk_d_topk.py:42-46, 219-224)
     from dsv4attn import ops

@@ -40,6 +40,7 @@ struct SelectScratch {
   uint32_t ncand;
   uint32_t warp_cnt[2][32];
   uint32_t part[32][4];
+  float fix_dot[64];  // per-head dots of the recomputed newest entry
 };
 
 // Block-wide min / max / sum of one value each per thread; every thread
@@ -407,13 +408,48 @@ __device__ void select_and_emit(uint32_t (&r)[kKeysPerThread], const uint32_t* k
   }
 }
 
+// Score of one indexer key row: sum_h w[h] relu(q[h] . key) over the 64
+// heads of one sequence (q [64 x 128] bf16, key [128] bf16, w [64]); warp w
+// takes heads 2w and 2w + 1, the heads are summed in order h = 0..63 like
+// the indexer score's epilogue.  All threads of the CTA call it; every
+// thread gets the score.
+constexpr int kFixHeads = 64;
+constexpr int kFixDim = 128;
+__device__ float indexer_row_score(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ key,
+                                   const float* __restrict__ w, float* s_dot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint2 kraw = *reinterpret_cast<const uint2*>(key + 4 * lane);
+  const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kraw.x));
+  const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kraw.y));
+  for (int h = 2 * warp; h < kFixHeads && h < 2 * warp + 2; ++h) {
+    const uint2 qraw = *reinterpret_cast<const uint2*>(q + int64_t(h) * kFixDim + 4 * lane);
+    const float2 q01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qraw.x));
+    const float2 q23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qraw.y));
+    float d = q01.x * k01.x;
+    d = fmaf(q01.y, k01.y, d);
+    d = fmaf(q23.x, k23.x, d);
+    d = fmaf(q23.y, k23.y, d);
+    d = warp_sum(d);
+    if (lane == 0) s_dot[h] = d;
+  }
+  __syncthreads();
+  float sc = 0.f;
+  for (int h = 0; h < kFixHeads; ++h) sc = fmaf(w[h], fmaxf(s_dot[h], 0.f), sc);
+  return sc;
+}
+
 // grid (n_chunks, B).  Chunk c of row b covers t in [c*chunk, min(T, (c+1)*chunk)).
 // n_chunks == 1: final output.  Otherwise raw candidates at
 // cand[(b*n_chunks + c)*k ...] (fewer than k real ones pad with key 0 / id -1).
+// With fq != null the score of each row's newest live entry, t = t_active - 1,
+// is recomputed from the indexer inputs (fq [B, 64, 128], key rows fk + b *
+// fk_bstride + t * 128, fw [B, 64]) instead of read from `score`: the key row
+// may have been written after the score matrix was computed.
 __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
     const float* __restrict__ score, int64_t ld_score, const int32_t* __restrict__ t_active, int T, int chunk, int k,
     int win, int sort_desc, int mask_mode, int32_t* __restrict__ out_idx, float* __restrict__ out_score, int64_t ld_out,
-    uint32_t* __restrict__ cand_key, int32_t* __restrict__ cand_id) {
+    uint32_t* __restrict__ cand_key, int32_t* __restrict__ cand_id, const __nv_bfloat16* __restrict__ fq,
+    const __nv_bfloat16* __restrict__ fk, int64_t fk_bstride, const float* __restrict__ fw) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ SelectScratch s;
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
@@ -426,6 +462,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
   pdl_launch_dependents();
   const int ta = t_active[b];
   const float* row = score + int64_t(b) * ld_score + t0;
+  const int tf = min(ta, T) - 1;  // the newest live entry
+  const bool fix = fq != nullptr && tf >= t0 && tf < t0 + n;  // uniform across the CTA
   // every load of a thread in flight before any use (n <= 16 x 1024); the
   // keys stay in registers for the select and go to shared memory for the
   // compaction
@@ -435,11 +473,16 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
     const int i = threadIdx.x + j * kTopkThreads;
     r[j] = i < n ? __float_as_uint(__ldg(row + i)) : 0u;
   }
+  float fix_score = 0.f;
+  if (fix) {
+    fix_score = indexer_row_score(fq + int64_t(b) * kFixHeads * kFixDim, fk + int64_t(b) * fk_bstride +
+                                  int64_t(tf) * kFixDim, fw + int64_t(b) * kFixHeads, s.fix_dot);
+  }
 #pragma unroll
   for (int j = 0; j < kKeysPerThread; ++j) {
     const int i = threadIdx.x + j * kTopkThreads;
     if (i < n) {
-      const float v = __uint_as_float(r[j]);
+      const float v = (fix && t0 + i == tf) ? fix_score : __uint_as_float(r[j]);
       r[j] = float_key((t0 + i < ta) ? v : (mask_mode ? -INFINITY : __fsub_rn(v, 1.0e4f)));
       keys[i] = r[j];
     } else {
@@ -551,7 +594,8 @@ extern "C" size_t dsa_indexer_topk_workspace_size(int B, int T, int k) {
 
 static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_active, int32_t* out_idx,
                        float* out_score, int64_t ld_out, int B, int T, int k, int win, int sort_desc, int mask_mode,
-                       void* ws, size_t ws_bytes, cudaStream_t st) {
+                       void* ws, size_t ws_bytes, cudaStream_t st, const __nv_bfloat16* fq = nullptr,
+                       const __nv_bfloat16* fk = nullptr, int64_t fk_bstride = 0, const float* fw = nullptr) {
   DSA_CHECK_ARG(score && t_active && out_idx, "indexer_topk: null pointer");
   DSA_CHECK_ARG(B >= 0 && T > 0 && k > 0 && k <= T, "indexer_topk: need 0 < k <= T (k=%d T=%d)", k, T);
   DSA_CHECK_ARG(k <= kTopkMaxK, "indexer_topk: k=%d above the built maximum %d", k, kTopkMaxK);
@@ -567,7 +611,8 @@ static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_ac
   }
   if (T <= kTopkMaxN) {
     launch_pdl(topk_chunk_kernel, dim3(1, B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T, T,
-               k, win, sort_desc, mask_mode, out_idx, out_score, ld_out, (uint32_t*)nullptr, (int32_t*)nullptr);
+               k, win, sort_desc, mask_mode, out_idx, out_score, ld_out, (uint32_t*)nullptr, (int32_t*)nullptr, fq, fk,
+               fk_bstride, fw);
     DSA_CHECK_LAUNCH("indexer_topk");
     return DSA_OK;
   }
@@ -581,7 +626,8 @@ static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_ac
   uint32_t* ck = static_cast<uint32_t*>(ws);
   int32_t* ci = reinterpret_cast<int32_t*>(ck + size_t(B) * n_chunks * k);
   launch_pdl(topk_chunk_kernel, dim3(n_chunks, B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T,
-             (int)kTopkMaxN, k, win, 0, mask_mode, (int32_t*)nullptr, (float*)nullptr, (int64_t)0, ck, ci);
+             (int)kTopkMaxN, k, win, 0, mask_mode, (int32_t*)nullptr, (float*)nullptr, (int64_t)0, ck, ci, fq, fk,
+             fk_bstride, fw);
   DSA_CHECK_LAUNCH("indexer_topk(chunks)");
   launch_pdl(topk_merge_kernel, dim3(B), dim3(kTopkThreads), merge_smem(), st, (const uint32_t*)ck,
              (const float*)nullptr, (const int32_t*)ci, n_chunks * k, k, win, sort_desc, 1, out_idx, out_score, ld_out);
@@ -595,6 +641,20 @@ extern "C" int dsa_indexer_topk(const float* score, int64_t ld_score, const int3
   clear_error();
   return topk_launch(score, ld_score, t_active, out_idx, out_score, ld_out, B, T, k, win, sort_desc, mask_mode,
                      nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dsa_indexer_topk_newest(const float* score, int64_t ld_score, const int32_t* t_active,
+                                       int32_t* out_idx, float* out_score, int64_t ld_out, int B, int T, int k,
+                                       int win, int sort_desc, int mask_mode, const void* q, const void* k_cache,
+                                       int64_t k_bstride, const float* w, void* workspace, size_t workspace_bytes,
+                                       dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG(q && k_cache && w, "indexer_topk_newest: null q / k_cache / w");
+  DSA_CHECK_ARG(aligned(q, 16) && aligned(k_cache, 16) && k_bstride % 8 == 0 && k_bstride >= int64_t(T) * kFixDim,
+                "indexer_topk_newest: q / k_cache must be 16-byte aligned and k_bstride >= T * 128, a multiple of 8");
+  return topk_launch(score, ld_score, t_active, out_idx, out_score, ld_out, B, T, k, win, sort_desc, mask_mode,
+                     workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
+                     static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache), k_bstride, w);
 }
 
 extern "C" int dsa_indexer_topk_ws(const float* score, int64_t ld_score, const int32_t* t_active, int32_t* out_idx,

@@ -43,6 +43,8 @@ PROTOTYPES = {
     "dsa_indexer_topk": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
     "dsa_indexer_topk_workspace_size": (SZ, [I32, I32, I32]),
     "dsa_indexer_topk_ws": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, SZ, P]),
+    "dsa_indexer_topk_newest": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, P, I64, P, P, SZ,
+                                       P]),
     "dsa_advance_positions": (I32, [P, P, I32, I32, I32, P]),
     "dsa_topk_merge": (I32, [P, P, I32, P, P, I64, I32, I32, I32, P]),
     "dsa_shard_active": (I32, [P, P, I32, I32, I32, P]),

@@ -27,9 +27,12 @@ reference's order (inference.py:5888-6093):
 and then advances the device-resident positions, so a captured CUDA graph
 of the whole step can be replayed without any host work (the reference
 needs two traces and host staging per step, inference.py:7498-7543).  The
-window write and the attention compressor feed only the attention, so they
-run on a side stream in parallel with the indexer chain (a parallel branch
-of the captured graph).
+window write, the attention compressor and the indexer compressor run on a
+side stream in parallel with the indexer score (a parallel branch of the
+captured graph): the score covers the compressed rows before the newest,
+and the top-k, after the join, recomputes the newest row's score from the
+indexer inputs (dsa_indexer_topk_newest) -- the same selection as scoring
+after the compressor, with the compressor off the critical path.
 """
 
 from __future__ import annotations
@@ -182,11 +185,17 @@ class DecodePath:
         self.cos, self.sin = rope_cos_sin(a, max_seq_len, compressed=True, device=self.device)
         self.pos = torch.zeros(self.B, dtype=I32, device=self.device)
         self.t_active = torch.zeros(self.B, dtype=I32, device=self.device)
+        # t_active - 1: the indexer scores the rows before the newest, which
+        # the indexer compressor may write in the same step (the top-k
+        # recomputes that one row after the join)
+        self.t_prev = torch.zeros(self.B, dtype=I32, device=self.device)
         self.status = torch.zeros(1, dtype=I32, device=self.device)
         self.graph = None
         # the window write and the attention compressor depend on nothing of
         # the indexer chain: they run on a side stream, joined before attention
         self.side = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        # the indexer compressor: its own branch, joined before the top-k
+        self.side_idx = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
 
     def set_positions(self, pos) -> None:
         """Stage the current decode position(s) (pre_stage_decode,
@@ -194,13 +203,21 @@ class DecodePath:
         p = torch.as_tensor(pos, dtype=I32).reshape(-1).expand(self.B).contiguous()
         self.pos.copy_(p.to(self.device, non_blocking=False))
         self.t_active.copy_(((p + 1) // self.args.compress_ratio).to(self.device))
+        ops.shard_active(self.t_active, 1, 1 << 30, out=self.t_prev)
 
     def layer_step(self, L: DecodeLayer, x: LayerInputs, out: torch.Tensor) -> None:
         a = self.args
         W, r = L.win, L.ratio
         main = torch.cuda.current_stream(self.device)
         side = self.side
-        # side branch: attn.kv window write, the window ring indices and
+        # side branch 1: the indexer's compressor (joined before the top-k)
+        side_idx = self.side_idx
+        side_idx.wait_stream(main)
+        with torch.cuda.stream(side_idx):
+            ops.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos,
+                                self.sin, L.idx_cache, 0, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
+                                rope_dim=a.rope_head_dim)
+        # side branch 2: attn.kv window write, the window ring indices and
         # attn.compress (all three only feed the attention)
         side.wait_stream(main)
         with torch.cuda.stream(side):
@@ -209,12 +226,15 @@ class DecodePath:
             ops.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
                                 L.kv_cache, W, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
                                 rope_dim=a.rope_head_dim)
-        # main branch: attn.topk (the top-k writes idx[:, W:], disjoint from the window columns)
-        ops.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos, self.sin,
-                            L.idx_cache, 0, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
-                            rope_dim=a.rope_head_dim)
-        ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_active)
-        ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws)
+        # main branch: attn.topk.  The score covers the rows before the
+        # newest (t_prev = t_active - 1), which the indexer compressor may be
+        # writing meanwhile; after joining it the top-k recomputes that
+        # row's score from the indexer inputs.  The top-k writes idx[:, W:],
+        # disjoint from the window columns.
+        ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_prev)
+        main.wait_stream(side_idx)
+        ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws,
+                         refresh=(x.iq, L.idx_cache, x.iw))
         main.wait_stream(side)
         ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, self.scale, out=out, ws=L.ws, status=self.status)
 
@@ -223,6 +243,7 @@ class DecodePath:
             self.layer_step(L, x, o)
         if advance:
             ops.advance_positions(self.pos, self.t_active, self.args.compress_ratio, 1)
+            ops.shard_active(self.t_active, 1, 1 << 30, out=self.t_prev)
 
     def capture(self, inputs: list[LayerInputs], outs: list[torch.Tensor], warmup: int = 1):
         """Capture ``step`` (with the position advance) in a CUDA graph.  The

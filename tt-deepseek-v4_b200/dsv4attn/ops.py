@@ -285,9 +285,13 @@ def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: in
 
 def indexer_topk(score: torch.Tensor, t_active: torch.Tensor, k: int, win: int, T: int | None = None,
                  sort_desc: bool = False, mask_mode: int = 0, out: torch.Tensor | None = None,
-                 out_score: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
+                 out_score: torch.Tensor | None = None, ws: Workspace | None = None,
+                 refresh: tuple | None = None) -> torch.Tensor:
     """Masked top-k (inference.py:5823-5851) -> int32 [B, k] (idx + win, -1
-    for invalid)."""
+    for invalid).  ``refresh=(q [B,64,128] bf16, k_cache [B,T',128] bf16,
+    w [B,64] f32)``: the score of each row's newest live entry (t_active - 1)
+    is recomputed from the indexer inputs instead of read from ``score``, so
+    the score matrix may be computed before that key row is written."""
     _need(score, "score", F32)
     _need(t_active, "t_active", I32)
     B = score.shape[0]
@@ -296,6 +300,21 @@ def indexer_topk(score: torch.Tensor, t_active: torch.Tensor, k: int, win: int, 
         out = torch.empty(B, k, dtype=I32, device=score.device)
     L = lib()
     need = L.dsa_indexer_topk_workspace_size(B, T, k)
+    if refresh is not None:
+        q, kc, w = refresh
+        _need(q, "q", BF16)
+        _need(kc, "k_cache", BF16)
+        _need(w, "w", F32)
+        if q.shape[-2:] != (64, 128) or kc.shape[-1] != 128 or kc.stride(1) != 128 or not q.is_contiguous() \
+                or not w.is_contiguous():
+            raise ValueError("indexer_topk refresh: q [B,64,128], k_cache [B,T,128] rows contiguous, w [B,64]")
+        wsb = _ws(score.device, need, ws) if need else None
+        rc = L.dsa_indexer_topk_newest(score.data_ptr(), score.stride(0), t_active.data_ptr(), out.data_ptr(),
+                                       _ptr(out_score), out.stride(0), B, T, k, win, int(sort_desc), mask_mode,
+                                       q.data_ptr(), kc.data_ptr(), kc.stride(0), w.data_ptr(),
+                                       wsb.buf.data_ptr() if wsb else None, wsb.nbytes if wsb else 0, _stream(score))
+        check(rc, "indexer_topk_newest")
+        return out
     if need:
         w = _ws(score.device, need, ws)
         rc = L.dsa_indexer_topk_ws(score.data_ptr(), score.stride(0), t_active.data_ptr(), out.data_ptr(),
