@@ -273,4 +273,4 @@ class DecodePath:
                                                                 L0.win + L0.k) else 0
         topk2 = 1 if ops.lib().dsa_indexer_topk_workspace_size(self.B, L0.T_max, L0.k) else 0
         n = len(self.layers) * (self.kernels_per_layer + extra + topk2)
-        return n + 1
+        return n + 2  # + the position advance and t_prev
