@@ -21,6 +21,7 @@
 // into chunks whose local top-k lists are merged by the same select
 // (dsa_topk_merge), which is also the cross-GPU merge of the sequence split.
 #include "common.cuh"
+#include "indexer_row.cuh"
 
 namespace dsa {
 
@@ -408,36 +409,6 @@ __device__ void select_and_emit(uint32_t (&r)[kKeysPerThread], const uint32_t* k
   }
 }
 
-// Score of one indexer key row: sum_h w[h] relu(q[h] . key) over the 64
-// heads of one sequence (q [64 x 128] bf16, key [128] bf16, w [64]); warp w
-// takes heads 2w and 2w + 1, the heads are summed in order h = 0..63 like
-// the indexer score's epilogue.  All threads of the CTA call it; every
-// thread gets the score.
-constexpr int kFixHeads = 64;
-constexpr int kFixDim = 128;
-__device__ float indexer_row_score(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ key,
-                                   const float* __restrict__ w, float* s_dot) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint2 kraw = *reinterpret_cast<const uint2*>(key + 4 * lane);
-  const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kraw.x));
-  const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kraw.y));
-  for (int h = 2 * warp; h < kFixHeads && h < 2 * warp + 2; ++h) {
-    const uint2 qraw = *reinterpret_cast<const uint2*>(q + int64_t(h) * kFixDim + 4 * lane);
-    const float2 q01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qraw.x));
-    const float2 q23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qraw.y));
-    float d = q01.x * k01.x;
-    d = fmaf(q01.y, k01.y, d);
-    d = fmaf(q23.x, k23.x, d);
-    d = fmaf(q23.y, k23.y, d);
-    d = warp_sum(d);
-    if (lane == 0) s_dot[h] = d;
-  }
-  __syncthreads();
-  float sc = 0.f;
-  for (int h = 0; h < kFixHeads; ++h) sc = fmaf(w[h], fmaxf(s_dot[h], 0.f), sc);
-  return sc;
-}
-
 // grid (n_chunks, B).  Chunk c of row b covers t in [c*chunk, min(T, (c+1)*chunk)).
 // n_chunks == 1: final output.  Otherwise raw candidates at
 // cand[(b*n_chunks + c)*k ...] (fewer than k real ones pad with key 0 / id -1).
@@ -475,8 +446,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(
   }
   float fix_score = 0.f;
   if (fix) {
-    fix_score = indexer_row_score(fq + int64_t(b) * kFixHeads * kFixDim, fk + int64_t(b) * fk_bstride +
-                                  int64_t(tf) * kFixDim, fw + int64_t(b) * kFixHeads, s.fix_dot);
+    fix_score = indexer_row_score(fq + int64_t(b) * kRowHeads * kRowDim, fk + int64_t(b) * fk_bstride +
+                                  int64_t(tf) * kRowDim, fw + int64_t(b) * kRowHeads, s.fix_dot);
   }
 #pragma unroll
   for (int j = 0; j < kKeysPerThread; ++j) {
@@ -650,7 +621,7 @@ extern "C" int dsa_indexer_topk_newest(const float* score, int64_t ld_score, con
                                        dsa_stream_t stream) {
   clear_error();
   DSA_CHECK_ARG(q && k_cache && w, "indexer_topk_newest: null q / k_cache / w");
-  DSA_CHECK_ARG(aligned(q, 16) && aligned(k_cache, 16) && k_bstride % 8 == 0 && k_bstride >= int64_t(T) * kFixDim,
+  DSA_CHECK_ARG(aligned(q, 16) && aligned(k_cache, 16) && k_bstride % 8 == 0 && k_bstride >= int64_t(T) * kRowDim,
                 "indexer_topk_newest: q / k_cache must be 16-byte aligned and k_bstride >= T * 128, a multiple of 8");
   return topk_launch(score, ld_score, t_active, out_idx, out_score, ld_out, B, T, k, win, sort_desc, mask_mode,
                      workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
