@@ -163,6 +163,20 @@ int dsa_indexer_score(const void* q, const void* k, const float* w, float* score
                       const int32_t* t_valid, int B, int H, int Di, int T,
                       int64_t k_bstride, int64_t ld_score, dsa_stream_t stream);
 
+/* dsa_indexer_score with flags (same result; replaces the same reference
+ * stage, inference.py:5260-5275).  DSA_KEYS_READY: the caller guarantees
+ * that k and t_valid were complete before the kernel that precedes this
+ * call on the stream started (in a decode step: keys written by earlier
+ * steps, t_valid staged before the first layer, so no kernel between
+ * writes them).  The kernel may then request its first key tiles before
+ * waiting for that preceding kernel (programmatic dependent launch),
+ * overlapping their latency with its tail; q and w are read after the
+ * wait.  Only the per-sequence key path (k_bstride != 0) uses the flag. */
+enum { DSA_KEYS_READY = 1 };
+int dsa_indexer_score_ex(const void* q, const void* k, const float* w, float* score,
+                         const int32_t* t_valid, int B, int H, int Di, int T,
+                         int64_t k_bstride, int64_t ld_score, int flags, dsa_stream_t stream);
+
 /* Top-k of the masked indexer score, the reference's bucketed pad+mask
  * path (inference.py:5823-5851): masked = s - 1e4 * (t >= t_active[b]);
  * select the k largest of masked[b, 0:T]; out = t + win where

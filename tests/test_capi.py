@@ -72,6 +72,9 @@ def test_host_validation_rejects_bad_shapes_without_launch():
     assert rc == _lib.DSA_ERR_ARG
     # null pointers
     assert L.dsa_kv_window_write(None, None, None, None, 1, 512, 64, 512 * 128, 128, 64, None) == _lib.DSA_ERR_ARG
+    # unknown indexer-score flags are refused before anything runs
+    assert L.dsa_indexer_score_ex(1, 1, 1, 1, None, 1, 64, 128, 8, 1024, 8, 4, None) == _lib.DSA_ERR_ARG
+    assert "flags" in _lib.last_error()
 
 
 def test_workspace_queries_are_pure_host():

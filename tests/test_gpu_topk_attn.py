@@ -68,6 +68,29 @@ def test_indexer_score(cuda_dev, B, T):
     torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-3 * float(want.abs().max()))
 
 
+@pytest.mark.parametrize("B,T,tv_lo", [(64, 9216, 8000), (3, 1000, 0), (300, 700, 1)])
+def test_indexer_score_keys_ready_identical(cuda_dev, B, T, tv_lo):
+    """DSA_KEYS_READY (first key tiles requested before the launch wait)
+    gives bit-identical scores, entries at and past t_valid untouched,
+    also when q and w are rewritten right before the call."""
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B + T)
+    q = torch.randn(B, 64, 128, generator=g).to(torch.bfloat16).to(cuda_dev)
+    k = torch.randn(B, T, 128, generator=g).to(torch.bfloat16).to(cuda_dev)
+    w = (0.02 * torch.randn(B, 64, generator=g)).to(cuda_dev)
+    tv = torch.randint(tv_lo, T + 1, (B,), generator=g, dtype=torch.int32).to(cuda_dev)
+    want = torch.full((B, T), 7.0, device=cuda_dev)
+    ops.indexer_score(q, k, w, T, out=want, t_valid=tv)
+    q2, w2 = torch.zeros_like(q), torch.zeros_like(w)
+    for _ in range(2):
+        got = torch.full((B, T), 7.0, device=cuda_dev)
+        q2.copy_(q)
+        w2.copy_(w)
+        ops.indexer_score(q2, k, w2, T, out=got, t_valid=tv, keys_ready=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+
+
 def test_indexer_score_t_valid(cuda_dev):
     from dsv4attn import ops
     B, T = 2, 512

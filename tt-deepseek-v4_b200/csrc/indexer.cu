@@ -23,10 +23,9 @@ constexpr int kIdxD = 128;       // indexer head dim
 
 using namespace dsa;
 
-extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, float* score, const int32_t* t_valid,
-                                 int B, int H, int Di, int T, int64_t k_bstride, int64_t ld_score,
-                                 dsa_stream_t stream) {
-  clear_error();
+static int indexer_score_run(const void* q, const void* k, const float* w, float* score, const int32_t* t_valid,
+                             int B, int H, int Di, int T, int64_t k_bstride, int64_t ld_score, int flags,
+                             dsa_stream_t stream) {
   DSA_CHECK_ARG(q && k && w && score, "indexer_score: null pointer");
   DSA_CHECK_ARG(H == kIdxH && Di == kIdxD, "indexer_score: built for H=64, Di=128 (got H=%d Di=%d)", H, Di);
   DSA_CHECK_ARG(B >= 0 && T >= 0, "indexer_score: bad B/T");
@@ -97,10 +96,26 @@ extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, f
     a.ld_score = ld_score;
     a.k_row_stride = row_stride;
     a.balanced = B <= idxtc::kMaxSeqBalanced ? 1 : 0;
+    a.keys_ready = (flags & DSA_KEYS_READY) ? 1 : 0;
     const int grid = a.balanced ? std::min(nsm, total) : (total + a.items_per_cta - 1) / a.items_per_cta;
     launch_pdl(idxtc::indexer_score_tc_kernel, dim3(grid), dim3(idxtc::THREADS), idxtc::kSmemBytes,
                reinterpret_cast<cudaStream_t>(stream), a, tm_k, tm_q);
   }
   DSA_CHECK_LAUNCH("indexer_score");
   return DSA_OK;
+}
+
+extern "C" int dsa_indexer_score(const void* q, const void* k, const float* w, float* score, const int32_t* t_valid,
+                                 int B, int H, int Di, int T, int64_t k_bstride, int64_t ld_score,
+                                 dsa_stream_t stream) {
+  clear_error();
+  return indexer_score_run(q, k, w, score, t_valid, B, H, Di, T, k_bstride, ld_score, 0, stream);
+}
+
+extern "C" int dsa_indexer_score_ex(const void* q, const void* k, const float* w, float* score,
+                                    const int32_t* t_valid, int B, int H, int Di, int T, int64_t k_bstride,
+                                    int64_t ld_score, int flags, dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG((flags & ~DSA_KEYS_READY) == 0, "indexer_score: unknown flags 0x%x", flags);
+  return indexer_score_run(q, k, w, score, t_valid, B, H, Di, T, k_bstride, ld_score, flags, stream);
 }

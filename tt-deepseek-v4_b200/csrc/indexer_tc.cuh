@@ -58,6 +58,12 @@ struct Args {
   int32_t* status;
   int B, T, tiles_per_seq, items_per_cta;
   int balanced;           // B <= kMaxSeqBalanced: split the live tiles evenly (items_per_cta unused)
+  // The key cache and t_valid were complete before the previous kernel on
+  // the stream started (keys of earlier decode steps): the first NS key
+  // tiles are requested before the programmatic-dependent-launch wait, so
+  // their latency overlaps the previous kernel's tail; q and w are read
+  // after the wait.
+  int keys_ready;
   int64_t ld_score;
   int64_t k_row_stride;   // rows between consecutive sequences in the key map
 };
@@ -131,64 +137,94 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = aux->tmem_base;
-  // set-up above touches no global memory; keys, q, w and t_valid are the
-  // previous kernels' outputs
-  pdl_wait();
-  pdl_launch_dependents();
 
   ItemWalk walk{};
   walk.a = &a;
-  if (a.balanced) {
-    // live tiles per sequence -> exclusive prefix (one block scan)
-    int* pre = reinterpret_cast<int*>(smem + kOffPre);
-    auto live = [&](int b) { return (seq_limit(a, b) + TILE - 1) / TILE; };
-    const int per = (a.B + THREADS - 1) / THREADS;
-    const int b0 = min(a.B, tid * per), b1 = min(a.B, b0 + per);
-    int loc = 0;
-    for (int b = b0; b < b1; ++b) loc += live(b);
-    int inc = loc;
+  auto build_walk = [&]() {
+    if (a.balanced) {
+      // live tiles per sequence -> exclusive prefix (one block scan)
+      int* pre = reinterpret_cast<int*>(smem + kOffPre);
+      auto live = [&](int b) { return (seq_limit(a, b) + TILE - 1) / TILE; };
+      const int per = (a.B + THREADS - 1) / THREADS;
+      const int b0 = min(a.B, tid * per), b1 = min(a.B, b0 + per);
+      int loc = 0;
+      for (int b = b0; b < b1; ++b) loc += live(b);
+      int inc = loc;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += v;
-    }
-    if (lane == 31) aux->wsum[warp] = inc;
-    __syncthreads();
-    int run = inc - loc;
-    for (int w = 0; w < warp; ++w) run += aux->wsum[w];
-    for (int b = b0; b < b1; ++b) {
-      pre[b] = run;
-      run += live(b);
-    }
-    if (tid == THREADS - 1) pre[a.B] = run;
-    __syncthreads();
-    const int total_live = pre[a.B];
-    const int share = (total_live + gridDim.x - 1) / gridDim.x;
-    walk.pre = pre;
-    walk.l = min(total_live, int(blockIdx.x) * share);
-    walk.l_end = min(total_live, walk.l + share);
-    if (walk.l < walk.l_end) {
-      // the sequence holding live item l: the last b with pre[b] <= l
-      int lo = 0, hi = a.B - 1;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (pre[mid] <= walk.l) lo = mid;
-        else hi = mid - 1;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
       }
-      walk.b = lo;
-      walk.tile = walk.l - pre[lo];
+      if (lane == 31) aux->wsum[warp] = inc;
+      __syncthreads();
+      int run = inc - loc;
+      for (int w = 0; w < warp; ++w) run += aux->wsum[w];
+      for (int b = b0; b < b1; ++b) {
+        pre[b] = run;
+        run += live(b);
+      }
+      if (tid == THREADS - 1) pre[a.B] = run;
+      __syncthreads();
+      const int total_live = pre[a.B];
+      const int share = (total_live + gridDim.x - 1) / gridDim.x;
+      walk.pre = pre;
+      walk.l = min(total_live, int(blockIdx.x) * share);
+      walk.l_end = min(total_live, walk.l + share);
+      if (walk.l < walk.l_end) {
+        // the sequence holding live item l: the last b with pre[b] <= l
+        int lo = 0, hi = a.B - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (pre[mid] <= walk.l) lo = mid;
+          else hi = mid - 1;
+        }
+        walk.b = lo;
+        walk.tile = walk.l - pre[lo];
+      }
+    } else {
+      walk.i_end = min(a.B * a.tiles_per_seq, int(blockIdx.x + 1) * a.items_per_cta);
+      walk.item = int(blockIdx.x) * a.items_per_cta;
     }
-  } else {
-    walk.i_end = min(a.B * a.tiles_per_seq, int(blockIdx.x + 1) * a.items_per_cta);
-    walk.item = int(blockIdx.x) * a.items_per_cta;
+  };
+
+  // keys_ready: the work split (from t_valid) and the first NS key tiles
+  // before the wait; each stage's q follows after it on the same barrier
+  int npre = 0;
+  int qb[NS];
+  if (a.keys_ready) {
+    build_walk();
+    if (warp == 0 && lane == 0) {
+      tma::prefetch_map(&tm_k);
+      int b, t0, t_lim;
+      while (npre < NS && walk.next(b, t0, t_lim)) {
+        const uint32_t st = sbase + npre * kStageBytes;
+        const uint32_t fb = smem_u32(&aux->full[npre]);
+        tma::mbar_arrive_expect_tx(fb, kStageBytes);
+        const int krow = int(int64_t(b) * a.k_row_stride + t0);
+        tma::load_2d(st, &tm_k, 0, krow, fb);
+        tma::load_2d(st + kKeyBytes / 2, &tm_k, 64, krow, fb);
+        qb[npre++] = b;
+      }
+    }
   }
+  // otherwise the set-up above touches no global memory; keys, q, w and
+  // t_valid may be the previous kernels' outputs
+  pdl_wait();
+  pdl_launch_dependents();
+  if (!a.keys_ready) build_walk();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
       tma::prefetch_map(&tm_k);
       tma::prefetch_map(&tm_q);
-      int it = 0;
+      for (int i = 0; i < npre; ++i) {
+        const uint32_t st = sbase + i * kStageBytes;
+        const uint32_t fb = smem_u32(&aux->full[i]);
+        tma::load_2d(st + kKeyBytes, &tm_q, 0, qb[i] * H, fb);
+        tma::load_2d(st + kKeyBytes + kQBytes / 2, &tm_q, 64, qb[i] * H, fb);
+      }
+      int it = npre;
       int b, t0, t_lim;
       while (walk.next(b, t0, t_lim)) {
         const int s = it % NS;

@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libdsv4attn.so")
 
 DSA_OK = 0
 DSA_ERR_ARG = -1
+DSA_KEYS_READY = 1  # dsa_indexer_score_ex flag
 DSA_ERR_CUDA = -2
 DSA_ERR_UNSUPPORTED = -3
 DSA_ERR_TIMEOUT = -4
@@ -40,6 +41,7 @@ PROTOTYPES = {
                                   I32, I32, I32, I32, I32, I32, I32, F32, P]),
     "dsa_window_indices": (I32, [P, P, I64, I32, I32, P]),
     "dsa_indexer_score": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, P]),
+    "dsa_indexer_score_ex": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, I32, P]),
     "dsa_indexer_topk": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
     "dsa_indexer_topk_workspace_size": (SZ, [I32, I32, I32]),
     "dsa_indexer_topk_ws": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, SZ, P]),

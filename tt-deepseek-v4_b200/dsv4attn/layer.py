@@ -231,7 +231,13 @@ class DecodePath:
         # writing meanwhile; after joining it the top-k recomputes that
         # row's score from the indexer inputs.  The top-k writes idx[:, W:],
         # disjoint from the window columns.
-        ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_prev)
+        # keys_ready: the key rows scored here were written by earlier steps
+        # and t_prev before the first layer, so from the second layer on the
+        # kernel's first key tiles may be requested before the previous
+        # layer's last kernel ends (the first layer may directly follow the
+        # kernel that writes t_prev)
+        ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_prev,
+                          keys_ready=L is not self.layers[0])
         main.wait_stream(side_idx)
         ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws,
                          refresh=(x.iq, L.idx_cache, x.iw))

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import check, lib
+from ._lib import DSA_KEYS_READY, check, lib
 
 BF16 = torch.bfloat16
 I32 = torch.int32
@@ -257,11 +257,15 @@ def window_indices(pos: torch.Tensor, win: int, out: torch.Tensor | None = None)
 
 
 def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: int,
-                  out: torch.Tensor | None = None, t_valid: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, t_valid: torch.Tensor | None = None,
+                  keys_ready: bool = False) -> torch.Tensor:
     """``s[b,t] = sum_h w[b,h] relu(q[b,h].k[b,t])`` for t < T
     (inference.py:5260-5275).  q [B,64,128] bf16, k_cache [B, >=T, 128] bf16
     (or [>=T, 128]: one cache shared by all B rows, the queries of a prefill
-    chunk), w [B,64] fp32 -> [B, T] fp32."""
+    chunk), w [B,64] fp32 -> [B, T] fp32.  ``keys_ready``: k_cache and
+    t_valid were complete before the previous kernel on the stream started
+    (DSA_KEYS_READY: the kernel requests its first key tiles before waiting
+    for that kernel)."""
     _need(q, "q", BF16)
     _need(k_cache, "k_cache", BF16)
     _need(w, "w", F32)
@@ -278,8 +282,9 @@ def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: in
         k_bstride = k_cache.stride(0)
     if out is None:
         out = torch.empty(B, T, dtype=F32, device=q.device)
-    check(lib().dsa_indexer_score(q.data_ptr(), k_cache.data_ptr(), w.data_ptr(), out.data_ptr(), _ptr(t_valid),
-                                  B, H, Di, T, k_bstride, out.stride(0), _stream(q)), "indexer_score")
+    check(lib().dsa_indexer_score_ex(q.data_ptr(), k_cache.data_ptr(), w.data_ptr(), out.data_ptr(),
+                                     _ptr(t_valid), B, H, Di, T, k_bstride, out.stride(0),
+                                     DSA_KEYS_READY if keys_ready else 0, _stream(q)), "indexer_score")
     return out
 
 
