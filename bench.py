@@ -396,7 +396,9 @@ def main():
     kt = time_kernels(path, inputs, outs)
     dom = max(kt, key=kt.get)
     achieved = ab[dom] / (kt[dom] * 1e-3) / 1e9
-    traffic = read_traffic().get((dom, "cfg2"))
+    # ncu DRAM bytes of this workload's dominant kernel (None where no capture
+    # of that workload is committed)
+    traffic = read_traffic().get((dom, args.workload))
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "traffic": traffic,
                 "peak_kind": f"{hbm_kind} (MEASURED_PEAKS.json hbm_gbs)" if hbm_kind == "measured" else "fallback",
