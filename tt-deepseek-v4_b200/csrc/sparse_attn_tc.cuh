@@ -13,10 +13,18 @@
 //               completes on its slot's mbarrier through
 //               cp.async.mbarrier.arrive.
 //   warp 4      MMA issuer (one thread), ready-first over two kinds of batch:
-//               S(t)  = K_t Q^T   (M=64 keys, N=64 heads, K=512 dims; both
-//                       operands K-major) into one of two TMEM buffers (keys
-//                       in the M=64 lane layout, heads in columns), issued
-//                       once tile t has landed;
+//               S(t)  = K_t Q^T as one block-diagonal product: the tile is
+//                       read as 128 rows x 256 dims (a key's dims 0-255 in
+//                       one row, its dims 256-511 in another) against
+//                       Q' = [Q dims 0-255 | Q dims 256-511] as 128 columns,
+//                       so 16 MMAs of M=128 x N=128 x K=16 replace 32 of
+//                       M=64 x N=64 (a tcgen05.mma below N=128 costs ~80
+//                       cycles whatever its size, measured on B200).  Row r
+//                       of a key's first half pairs with columns 0-63, its
+//                       second half with columns 64-127; the two partials
+//                       of a key sit in the same TMEM sub-partition (rows
+//                       interleaved in 16-key chunks) and the softmax adds
+//                       them.  Issued once tile t has landed;
 //               PV(t): O^T += V_t^T P_t^T  (M=128 dims per block, N=64 heads,
 //                       K=64 keys; A = two adjacent k-block slabs read
 //                       MN-major, B = P, MN-major) into a TMEM accumulator that
@@ -26,8 +34,9 @@
 //               A wait between dependent batches drains the tensor pipe
 //               (about 700 cycles measured), so the issuer keeps whichever
 //               batch is ready queued.
-//   warps 0-3   softmax.  The 16x256b TMEM load spreads the 64 x 64 scores
-//               over 128 threads: thread i of warp w holds keys 16w + i/4 and
+//   warps 0-3   softmax.  Two 16x256b TMEM loads per warp (the two dim
+//               halves of its 16 keys) spread the 64 x 64 scores over 128
+//               threads: thread i of warp w holds keys 16w + i/4 and
 //               16w + 8 + i/4, heads 8r + 2(i%4) + {0,1}, r = 0..7.  The
 //               running max per head lives in shared memory and moves only
 //               when some score beats it by 2^8 (one barrier with an OR tells
@@ -54,8 +63,13 @@ constexpr int D = 512;
 constexpr int TK = 64;                                // keys per tile
 constexpr int KB = D / 64;                            // 64-dim k-blocks per row
 constexpr int NT = 2;                                 // tile slots
-constexpr int kSlabBytes = TK * 128;                  // one k-block of a tile: 8 KB
+constexpr int kSlabBytes = TK * 128;                  // one 64-dim k-block of a tile: 8 KB
 constexpr int kTileBytes = KB * kSlabBytes;           // 64 KB
+// A tile slot holds four 16 KB pair blocks; pair block j holds k-blocks j
+// (dims 64j..64j+63, "low") and j + 4 (dims 256 + 64j.., "high") of the 64
+// keys as 128 rows of 128 B: rows 32q..32q+15 = low half of keys
+// 16q..16q+15, rows 32q+16..32q+31 = their high half.
+constexpr int kPairBytes = 2 * kSlabBytes;            // 16 KB
 // 16 warps, four per scheduler (warp % 4): softmax 0-3, MMA issuer 4, and the
 // producers on the schedulers of warps 1-3 only (5-7, 9-11, 13-15), so the
 // MMA issuer shares its scheduler with one softmax warp; warps 8 and 12 idle.
@@ -81,11 +95,12 @@ constexpr int kOffIdx = kOffAux + kAuxBytes;
 constexpr int kSmemBytes = kOffIdx + kIdxCap * 4 + 1024;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0;                          // O^T: 4 blocks of [128 dims x 64 heads]
-constexpr uint32_t kColS = 256;                        // S: 2 buffers of [64 keys x 64 heads], M=64 layout
-constexpr uint32_t kIdescS = tc::idesc_bf16(64, 64, false, false);
+constexpr uint32_t kColS = 256;                        // S: 2 buffers of [128 rows x 128 cols], M=128 layout
+constexpr uint32_t kSCols = 128;
+constexpr uint32_t kIdescS = tc::idesc_bf16(128, 128, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 64, true, true);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(kColS + 2 * H <= kTmemCols, "TMEM columns");
+static_assert(kColS + 2 * kSCols <= kTmemCols, "TMEM columns");
 static_assert(TK % 16 == 0 && TK <= 64, "tile");
 
 enum : int { kStatusBadIndex = 1, kStatusTimeout = 2 };
@@ -114,10 +129,18 @@ struct Args {
 // misc (0: start, 1: end, 2: last PV done, 3: l reduced, 4: O stored)
 enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3, kTrPV = 4, kTrSGot = 5, kTrPDone = 6,
              kTrMisc = 7 };
+// Per-tile clock stamps for timeline analysis: compiled in only with
+// -DDSA_ATTN_TRACE (the hot build carries no trace branches).
+#ifdef DSA_ATTN_TRACE
 #define SA_TRACE(slot, t)                                                                         \
   do {                                                                                            \
     if (tr && (t) < kTrTiles) tr[(slot) * kTrTiles + (t)] = clock64();                            \
   } while (0)
+#else
+#define SA_TRACE(slot, t) \
+  do {                    \
+  } while (0)
+#endif
 
 struct Aux {
   float m[H];        // running max per head (log2 units)
@@ -137,11 +160,16 @@ struct Aux {
 };
 static_assert(sizeof(Aux) <= kAuxBytes, "aux block");
 
-// byte offset of 16-B chunk c (0..63) of tile row r: k-block slab c / 8, then
-// the 128-B swizzle of row r inside the slab
-__device__ __forceinline__ uint32_t chunk_off(int r, int c) {
-  return (c >> 3) * kSlabBytes + r * 128 + ((((c & 7) ^ (r & 7))) << 4);
+// byte offset of 16-B chunk c (0..63) of key k of a tile: k-block kb = c / 8
+// lives in pair block kb % 4, half kb / 4, at row 32 (k / 16) + 16 half + k % 16,
+// then the 128-B swizzle of that row
+__device__ __forceinline__ uint32_t chunk_off(int k, int c) {
+  const int kb = c >> 3;
+  const int row = ((k >> 4) << 5) + ((kb >> 2) << 4) + (k & 15);
+  return (kb & 3) * kPairBytes + row * 128 + ((((c & 7) ^ (k & 7))) << 4);
 }
+// Q is loaded in the same pairing: k-block kb at slab position 2 (kb % 4) + kb / 4
+__host__ __device__ constexpr int q_slab_pos(int kb) { return 2 * (kb & 3) + (kb >> 2); }
 
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a,
                                                                     const __grid_constant__ CUtensorMap tm_q,
@@ -161,7 +189,9 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   const int n = j_end > j_begin ? (j_end - j_begin + TK - 1) / TK : 0;
   const int32_t* idxr = a.idx + int64_t(m) * a.ld_idx;
   int32_t* s_idx = reinterpret_cast<int32_t*>(smem + kOffIdx);
+#ifdef DSA_ATTN_TRACE
   long long* tr = (a.trace && blockIdx.x == 0 && blockIdx.y == 0) ? a.trace : nullptr;
+#endif
   if (tid == 0) SA_TRACE(kTrMisc, 0);
 
   if (tid < H) aux->m[tid] = -INFINITY;
@@ -225,7 +255,8 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tma::prefetch_map(&tm_q);
       tma::mbar_arrive_expect_tx(smem_u32(&aux->q_full), kQBytes);
 #pragma unroll
-      for (int kb = 0; kb < KB; ++kb) tma::load_2d(sQ + kb * kQBlock, &tm_q, kb * 64, m * H, smem_u32(&aux->q_full));
+      for (int kb = 0; kb < KB; ++kb)
+        tma::load_2d(sQ + q_slab_pos(kb) * kQBlock, &tm_q, kb * 64, m * H, smem_u32(&aux->q_full));
     }
     const __nv_bfloat16* kvb = a.kv + int64_t(b) * kv_row_base_stride * D;
     for (int t = 0; t < n; ++t) {
@@ -251,7 +282,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
       const uint32_t q_lo = tc::desc_lo(sQ, 16);
       const uint32_t k_lo = tc::desc_lo(sRing, 16);          // K-major: LBO unused
-      const uint32_t v_lo = tc::desc_lo(sRing, kSlabBytes);  // MN-major: LBO = the next 64 dims (next slab)
+      const uint32_t v_lo = tc::desc_lo(sRing, kPairBytes);  // MN-major: LBO = the next 64 dims (next pair block)
       const uint32_t p_lo = tc::desc_lo(sP, kPBytes);        // MN-major, one 64-head group
       wait(&aux->q_full, 0);
       // Ready-first issue: PV(np) as soon as P(np) is written (it frees the
@@ -267,12 +298,15 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
           tc::fence_after_sync();
           const uint32_t vs = v_lo + (np % NT) * (kTileBytes / 16);
           const uint32_t ps = p_lo + (np & 1) * (kPBytes / 16);
-          // PV(np): 16 MMAs of M=128 dims x N=64 heads x K=16 keys
+          // PV(np): 16 MMAs of M=128 dims x N=64 heads x K=16 keys.  Dims
+          // 128jb.. are k-blocks 2jb, 2jb+1: pair blocks 2 (jb % 2) and the
+          // next, half jb / 2; keys 16kk.. are the 16 rows at 32kk + 16 half.
 #pragma unroll
           for (int jb = 0; jb < KB / 2; ++jb) {
 #pragma unroll
             for (int kk = 0; kk < TK / 16; ++kk) {
-              const uint64_t ad = tc::desc_pack(vs + (2 * jb * kSlabBytes + kk * 2048) / 16, hi);
+              const uint32_t off = (jb & 1) * 2 * kPairBytes + (jb >> 1) * 2048 + kk * 4096;
+              const uint64_t ad = tc::desc_pack(vs + off / 16, hi);
               const uint64_t bd = tc::desc_pack(ps + (kk * 2048) / 16, hi);
               tc::mma_bf16(tmem + kColO + H * jb, ad, bd, kIdescPV, (np > 0 || kk > 0) ? 1u : 0u);
             }
@@ -287,15 +321,16 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
           tc::fence_after_sync();
           SA_TRACE(kTrMmaGot, ns);
           const uint32_t ks0 = k_lo + (ns % NT) * (kTileBytes / 16);
-          const uint32_t d = tmem + kColS + H * (ns & 1);
-          // S(ns): 32 MMAs of M=64 keys x N=64 heads x K=16 dims
+          const uint32_t d = tmem + kColS + kSCols * (ns & 1);
+          // S(ns): 16 block-diagonal MMAs of M=128 rows x N=128 x K=16 dims
+          // over the four pair blocks (tile and Q' alike)
 #pragma unroll
-          for (int kb = 0; kb < KB; ++kb) {
+          for (int j = 0; j < KB / 2; ++j) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t ad = tc::desc_pack(ks0 + (kb * kSlabBytes + ks * 32) / 16, hi);
-              const uint64_t bd = tc::desc_pack(q_lo + (kb * kQBlock + ks * 32) / 16, hi);
-              tc::mma_bf16(d, ad, bd, kIdescS, (kb | ks) ? 1u : 0u);
+              const uint64_t ad = tc::desc_pack(ks0 + (j * kPairBytes + ks * 32) / 16, hi);
+              const uint64_t bd = tc::desc_pack(q_lo + (j * 2 * kQBlock + ks * 32) / 16, hi);
+              tc::mma_bf16(d, ad, bd, kIdescS, (j | ks) ? 1u : 0u);
             }
           }
           tc::mma_commit(smem_u32(&aux->s_full[ns & 1]));
@@ -318,10 +353,13 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     __syncwarp();
   } else if (warp < 4) {
     // ------------------------------------------------------------ softmax warps 0-3
-    // S rows (keys) 16w..16w+15 sit in TMEM lanes 32w..32w+15 (M=64 layout).
+    // Keys 16w..16w+15: their low-dim partials sit in TMEM lanes 32w..32w+15
+    // (columns 0-63 of the S buffer), their high-dim partials in lanes
+    // 32w+16..32w+31 (columns 64-127); S = low + high.
     const int q4 = lane & 3, g8 = lane >> 2;
     const int ka = warp * 16 + g8, kb2 = ka + 8;  // this thread's two keys
     const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t tq_hi = tmem + ((uint32_t)(warp * 32 + 16) << 16) + H;
     // [r][e] -> head 8r + 2 q4 + e: running max (a register copy of aux->m)
     // and partial sums of p over this thread's keys
     float mr[16], lp[16];
@@ -339,9 +377,12 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       warp_wait(&aux->s_full[t & 1], (t >> 1) & 1);
       tc::fence_after_sync();
       if (tid == 0) SA_TRACE(kTrSGot, t);
-      float v[32];
-      tc::tmem_ld16x256b_x8(tq + kColS + H * (t & 1), v);
+      float v[32], vh[32];
+      tc::tmem_ld16x256b_x8(tq + kColS + kSCols * (t & 1), v);
+      tc::tmem_ld16x256b_x8(tq_hi + kColS + kSCols * (t & 1), vh);
       tc::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += vh[i];
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(smem_u32(&aux->s_free[t & 1]));
