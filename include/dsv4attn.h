@@ -44,8 +44,10 @@ const char* dsa_last_error(void);
 /* ---------------------------------------------------------------- attn.kv */
 
 /* Block-wise max-abs FP8-E4M3 round trip of an [M, N] bf16 matrix along N.
- * Per block of `block` columns: amax = max|x|; s = max(amax, eps) / fp8_max;
- * q = e4m3_rn_satfinite(clamp(x / s, +-fp8_max)); out = bf16(float(q) * s).
+ * Per block of `block` columns: amax = max|x|; s = max(amax, eps) * r where
+ * r = 1/fp8_max rounded to fp32 (the chain multiplies by the constant, it
+ * does not divide); q = e4m3_rn_satfinite(clamp(x / s, +-fp8_max)) with an
+ * IEEE division; out = bf16(float(q) * s).
  * scales [M, N/block] fp32 (may be NULL); codes [M, N] e4m3 (may be NULL).
  * Replaces the tt-lang factory
  *   _compile_act_quant_block_kernel(M_pad, N, BLOCK, fp8_max, eps)(x, scaler, out)

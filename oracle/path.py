@@ -24,7 +24,7 @@ import torch
 
 __all__ = [
     "FP8_MAX", "ACT_QUANT_EPS", "TOPK_MASK_AMP", "TOPK_VALID_MIN",
-    "act_quant_block", "kv_quant_row", "window_indices", "window_table",
+    "act_quant_fp32", "act_quant_block", "kv_quant_row", "window_indices", "window_table",
     "yarn_freqs", "rope_tables", "rotary_interleaved", "rmsnorm",
     "compressor_init_state", "compressor_state_write", "compressor_emit",
     "compressor_step", "shift_matrix_apply", "indexer_score", "indexer_topk",
@@ -43,30 +43,43 @@ TOPK_VALID_MIN = -1000.0  # inference.py:5845 (valid = val >= -1000)
 # attn.kv : act_quant_block
 # --------------------------------------------------------------------------
 
-def act_quant_block(x: torch.Tensor, block: int = 64, fp8_max: float = FP8_MAX,
-                    eps: float = ACT_QUANT_EPS):
-    """Block-wise max-abs FP8-e4m3 round trip along the last dim.
+def act_quant_fp32(x: torch.Tensor, block: int = 64, fp8_max: float = FP8_MAX,
+                   eps: float = ACT_QUANT_EPS, e4m3: bool = True):
+    """The act_quant round trip in fp32, before the final bf16 rounding.
 
-    Follows the ttnn chain ``_device_act_quant_block`` (inference.py:4578-4607):
-    ``amax = max(|z|).clamp(min=eps)``, ``s = amax / fp8_max``,
-    ``y = clamp(z / s, -fp8_max, fp8_max)``, ``out = y * s`` - with the e4m3
-    cast that the CPU ``act_quant`` performs (inference.py:4582-4583,
-    device-compressor-indexer/README.md:76-82) inserted on ``y``.  Divisions
-    are IEEE fp32 divisions (``amax / 448`` and ``x / s``), not reciprocal
-    multiplies.
-
-    Returns ``(xhat bf16, scales fp32 [..., N/block], codes float8_e4m3fn)``.
-    """
+    Follows the ttnn chain ``_device_act_quant_block`` (inference.py:4578-4607)
+    op for op: ``amax = maximum(max(|z|), eps)``, ``s = multiply(amax,
+    1 / fp8_max)`` (a multiply by the fp32 constant 1/448, inference.py:4602,
+    not a division by 448), ``y = clamp(divide(z, s), -fp8_max, fp8_max)``
+    (an IEEE division), ``out = multiply(y, s)``.  With ``e4m3=True`` the
+    e4m3 cast of the CPU ``act_quant`` (inference.py:4582-4583,
+    device-compressor-indexer/README.md:76-82) is applied to ``y``; with
+    ``e4m3=False`` this is exactly the reference chain.
+    Returns ``(out fp32, s fp32 [..., N/block, 1], y or its e4m3 codes)``."""
     n = x.shape[-1]
     if n % block:
         raise ValueError(f"last dim {n} must be divisible by block_size {block}")
     xf = x.float()
     z = xf.reshape(*xf.shape[:-1], n // block, block)
-    amax = z.abs().amax(dim=-1, keepdim=True).clamp_min(eps)
-    s = amax / fp8_max
+    amax = torch.maximum(z.abs().amax(dim=-1, keepdim=True), torch.tensor(eps, dtype=torch.float32))
+    s = amax * (1.0 / fp8_max)
     y = torch.clamp(z / s, -fp8_max, fp8_max)
-    q = y.to(torch.float8_e4m3fn)
-    xhat = (q.float() * s).to(torch.bfloat16).reshape(x.shape)
+    if e4m3:
+        q = y.to(torch.float8_e4m3fn)
+        return q.float() * s, s, q
+    return y * s, s, y
+
+
+def act_quant_block(x: torch.Tensor, block: int = 64, fp8_max: float = FP8_MAX,
+                    eps: float = ACT_QUANT_EPS):
+    """Block-wise max-abs FP8-e4m3 round trip along the last dim: the
+    reference chain ``_device_act_quant_block`` (inference.py:4578-4607, see
+    ``act_quant_fp32``) with the CPU path's e4m3 cast, rounded to bf16.
+
+    Returns ``(xhat bf16, scales fp32 [..., N/block], codes float8_e4m3fn)``.
+    """
+    out, s, q = act_quant_fp32(x, block, fp8_max, eps, e4m3=True)
+    xhat = out.to(torch.bfloat16).reshape(x.shape)
     return xhat, s.squeeze(-1), q.reshape(x.shape)
 
 
@@ -407,9 +420,11 @@ def decode_layer_step(st: LayerState, pos: int, q, kv_row, cmp_kv_row, cmp_sc_ro
     compressor_step(st.icmp_kv, st.icmp_sc, icmp_kv_row, icmp_sc_row, st.iape, st.igamma,
                     st.cos, st.sin, pos, r, True, kv_cache=st.idx_kv_cache, slot_offset=0)
     idx = win_idx.unsqueeze(0).expand(B, W)
+    st.extra["score"] = None
     if t_active > 0:
         T_pad = t_active
         score = indexer_score(iq, st.idx_kv_cache[:, :T_pad], iw)
+        st.extra["score"] = score          # for near-tie checks of a selection
         k = min(st.index_topk, T_pad)
         cidx = indexer_topk(score, t_active, k, W)
         idx = torch.cat([idx, cidx], dim=-1)

@@ -65,12 +65,17 @@ def oracle_state(args, full, max_seq_len: int):
         index_topk=args.index_topk, scale=args.softmax_scale)
 
 
-def oracle_outputs(args, full, inputs, pos0: int, max_seq_len: int):
+def oracle_outputs(args, full, inputs, pos0: int, max_seq_len: int, with_scores: bool = False):
+    """The unsplit oracle's outputs and index rows per step (and, with
+    ``with_scores``, its indexer scores [B, T_active] per step)."""
     st = oracle_state(args, full, max_seq_len)
-    outs, idxs = [], []
+    outs, idxs, scores = [], [], []
     for s, x in enumerate(inputs):
         o, idx = ref.decode_layer_step(st, pos0 + s, x.q, x.kv, x.cmp_kv, x.cmp_score, x.iq, x.icmp_kv,
                                        x.icmp_score, x.iw)
         outs.append(o)
         idxs.append(idx)
+        scores.append(st.extra["score"])
+    if with_scores:
+        return outs, idxs, scores
     return outs, idxs

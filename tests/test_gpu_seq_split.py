@@ -5,13 +5,15 @@ is bench.py --workload cfg3 under torchrun).
 * small contexts: every shard's combined output equals the unsplit oracle
   step (rtol/atol 2e-2) and the merged selection equals the oracle's top-k
   set except at near-ties;
-* the config-3 size (65536 compressed entries, top-2048): the G-way split
-  selects exactly the 1-way selection and its output matches the 1-way
-  output (a size-independent property; the oracle is too slow there)."""
+* the config-3 size (65536 compressed entries, top-2048): the 1-, 2- and
+  8-way splits each select the oracle's top-k set except at near-ties and
+  match its output; the G-way selection also equals the 1-way one exactly
+  (the split is exact by construction)."""
 
 import pytest
 import torch
 
+from parity import assert_topk_sets, masked_scores
 from seqsplit_case import load_shard, make_case, oracle_outputs
 
 pytestmark = pytest.mark.gpu
@@ -44,29 +46,34 @@ def test_seq_split_matches_unsplit_oracle(cuda_dev, G, B):
     pos0 = 4 * T_total - 1 - steps - 3
     max_seq = 4 * T_total + 64
     args, full, inputs = make_case(100 + G, B, T_total, W, k, steps, pos0)
-    want, want_idx = oracle_outputs(args, full, inputs, pos0, max_seq)
+    want, want_idx, want_score = oracle_outputs(args, full, inputs, pos0, max_seq, with_scores=True)
     outs, sels = _run_split(args, full, inputs, G, T_total, pos0, max_seq, cuda_dev, B)
     for s in range(steps):
         for g in range(G):
             assert torch.allclose(outs[s][g].float(), want[s].float(), rtol=2e-2, atol=2e-2), (s, g)
-        for b in range(B):
-            got = set(int(v) + W for v in sels[s][b] if v >= 0)
-            exp = set(int(v) for v in want_idx[s][b, W:] if v >= 0)
-            assert len(got ^ exp) <= 2, (s, b, len(got ^ exp))
+        t_active = (pos0 + s + 1) // 4
+        got = torch.where(sels[s] >= 0, sels[s] + W, torch.full_like(sels[s], -1))
+        assert_topk_sets(got, want_idx[s][:, W:], masked_scores(want_score[s], t_active), W, what=f"step {s}")
 
 
-def test_seq_split_config3_size_equals_one_way(cuda_dev):
+def test_seq_split_config3_size_matches_oracle(cuda_dev):
     T_total, W, k, steps = 65536, 128, 2048, 2
     pos0 = 4 * T_total - 1 - steps - 1
     max_seq = 4 * T_total + 16
     args, full, inputs = make_case(3, 1, T_total, W, k, steps, pos0)
+    want, want_idx, want_score = oracle_outputs(args, full, inputs, pos0, max_seq, with_scores=True)
     one, sel1 = _run_split(args, full, inputs, 1, T_total, pos0, max_seq, cuda_dev, 1)
-    for G in (2, 8):
-        outg, selg = _run_split(args, full, inputs, G, T_total, pos0, max_seq, cuda_dev, 1)
+    for G in (1, 2, 8):
+        outg, selg = (one, sel1) if G == 1 else _run_split(args, full, inputs, G, T_total, pos0, max_seq,
+                                                          cuda_dev, 1)
         for s in range(steps):
+            t_active = (pos0 + s + 1) // 4
+            got = torch.where(selg[s] >= 0, selg[s] + W, torch.full_like(selg[s], -1))
+            assert_topk_sets(got, want_idx[s][:, W:], masked_scores(want_score[s], t_active), W,
+                             what=f"G={G} step {s}")
             assert set(sel1[s][0].tolist()) == set(selg[s][0].tolist()), (G, s)
             for g in range(G):
-                assert torch.allclose(outg[s][g].float(), one[s][0].float(), rtol=1e-2, atol=1e-2), (G, s, g)
+                assert torch.allclose(outg[s][g].float(), want[s].float(), rtol=2e-2, atol=2e-2), (G, s, g)
 
 
 def test_single_shard_path_writes_final_output(cuda_dev):

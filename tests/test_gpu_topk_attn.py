@@ -11,27 +11,9 @@ import pytest
 import torch
 
 import oracle as O
+from parity import NEAR_TIE_REL, assert_topk_sets  # noqa: F401
 
 pytestmark = pytest.mark.gpu
-
-NEAR_TIE_REL = 1e-3
-
-
-def assert_topk_sets(got_idx: torch.Tensor, want_idx: torch.Tensor, oracle_masked: torch.Tensor, win: int):
-    """Per row: the valid index sets match except for near-ties at the k-th
-    value of the oracle's masked scores."""
-    for b in range(got_idx.shape[0]):
-        g = set(int(v) for v in got_idx[b] if v >= 0)
-        w = set(int(v) for v in want_idx[b] if v >= 0)
-        if g == w:
-            continue
-        k = len(w)
-        kth = torch.topk(oracle_masked[b], k).values[-1]
-        tol = NEAR_TIE_REL * max(abs(float(kth)), 1e-6)
-        for v in g ^ w:
-            s = float(oracle_masked[b, v - win])
-            assert abs(s - float(kth)) <= tol, f"row {b}: index {v} score {s} vs k-th {float(kth)} is not a near-tie"
-        assert len(g) == len(w)
 
 
 def rel_err(got, want):

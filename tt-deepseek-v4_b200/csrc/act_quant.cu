@@ -2,7 +2,8 @@
 // with the window-ring KV write.
 //
 // Semantics (reference inference.py:4578-4607 plus the e4m3 cast):
-//   amax = max|x| over a block;  s = max(amax, eps) / fp8_max  (IEEE div)
+//   amax = max|x| over a block;  s = max(amax, eps) * (1 / fp8_max)
+//        (the chain's multiply by the fp32 constant 1/fp8_max, 4602)
 //   q = e4m3_rn_satfinite(clamp(x / s, +-fp8_max))            (IEEE div)
 //   out = bf16_rn(float(q) * s)
 // One warp owns one (row, block) pair; each lane holds block/32 contiguous
@@ -18,7 +19,7 @@ template <int EPL>
 __device__ __forceinline__ void quant_block_lane(const __nv_bfloat16* __restrict__ src,
                                                  __nv_bfloat16* __restrict__ dst, float* scale_out,
                                                  uint8_t* codes_out, int lane, float fp8_max,
-                                                 float eps) {
+                                                 float inv_max, float eps) {
   float v[EPL];
   if constexpr (EPL == 2) {
     __nv_bfloat162 h = reinterpret_cast<const __nv_bfloat162*>(src)[lane];
@@ -33,7 +34,7 @@ __device__ __forceinline__ void quant_block_lane(const __nv_bfloat16* __restrict
 #pragma unroll
   for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
   amax = warp_max(amax);
-  const float s = __fdiv_rn(fmaxf(amax, eps), fp8_max);
+  const float s = __fmul_rn(fmaxf(amax, eps), inv_max);
   uint8_t qb[EPL];
   float o[EPL];
 #pragma unroll
@@ -67,7 +68,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
                                                         float* __restrict__ scales,
                                                         uint8_t* __restrict__ codes, int64_t M,
                                                         int64_t N, int64_t ldx, int64_t ldo,
-                                                        float fp8_max, float eps) {
+                                                        float fp8_max, float inv_max, float eps) {
   constexpr int BLOCK = EPL * 32;
   const int64_t nb = N / BLOCK;
   const int64_t total = M * nb;
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
     const int64_t r = w / nb;
     const int64_t c0 = (w - r * nb) * BLOCK;
     quant_block_lane<EPL>(x + r * ldx + c0, out + r * ldo + c0, scales ? scales + w : nullptr,
-                          codes ? codes + r * N + c0 : nullptr, lane, fp8_max, eps);
+                          codes ? codes + r * N + c0 : nullptr, lane, fp8_max, inv_max, eps);
   }
 }
 
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(256) act_quant_kernel(const __nv_bfloat16* __r
 __global__ void __launch_bounds__(256) kv_window_write_kernel(
     const __nv_bfloat16* __restrict__ kv, __nv_bfloat16* __restrict__ cache,
     float* __restrict__ scales, const int32_t* __restrict__ pos, int D, int rope_dim,
-    int64_t cache_bstride, int win, float fp8_max, float eps) {
+    int64_t cache_bstride, int win, float fp8_max, float inv_max, float eps) {
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nope = D - rope_dim;
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(256) kv_window_write_kernel(
   const int nwarps = blockDim.x >> 5;
   for (int blk = warp; blk < nblk; blk += nwarps)
     quant_block_lane<2>(src + blk * 64, dst + blk * 64, scales ? scales + int64_t(b) * nblk + blk : nullptr,
-                        nullptr, lane, fp8_max, eps);
+                        nullptr, lane, fp8_max, inv_max, eps);
   for (int c = threadIdx.x; c < rope_dim; c += blockDim.x) dst[nope + c] = src[nope + c];
 }
 
@@ -119,6 +120,8 @@ extern "C" int dsa_act_quant_block(const void* x, void* out, float* scales, uint
   DSA_CHECK_ARG(N % block == 0, "act_quant_block: N=%lld not divisible by block=%d", (long long)N, block);
   DSA_CHECK_ARG(fp8_max > 0.f && eps > 0.f, "act_quant_block: fp8_max and eps must be positive");
   if (M == 0) return DSA_OK;
+  // 1 / fp8_max rounded once to fp32, as the reference's Python constant is
+  const float inv_max = float(1.0 / double(fp8_max));
   const int64_t total = M * (N / block);
   int grid = (int)std::min<int64_t>((total + 7) / 8, int64_t(num_sms()) * 16);
   auto* xp = static_cast<const __nv_bfloat16*>(x);
@@ -127,13 +130,13 @@ extern "C" int dsa_act_quant_block(const void* x, void* out, float* scales, uint
   if (block == 64) {
     DSA_CHECK_ARG(aligned(x, 4) && aligned(out, 4) && ld_x % 2 == 0 && ld_out % 2 == 0,
                   "act_quant_block: x/out must be 4-byte aligned with even strides");
-    act_quant_kernel<2><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, eps);
+    act_quant_kernel<2><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, inv_max, eps);
   } else if (block == 32) {
-    act_quant_kernel<1><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, eps);
+    act_quant_kernel<1><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, inv_max, eps);
   } else if (block == 128) {
-    act_quant_kernel<4><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, eps);
+    act_quant_kernel<4><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, inv_max, eps);
   } else {
-    act_quant_kernel<8><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, eps);
+    act_quant_kernel<8><<<grid, 256, 0, st>>>(xp, op, scales, codes, M, N, ld_x, ld_out, fp8_max, inv_max, eps);
   }
   DSA_CHECK_LAUNCH("act_quant_block");
   return DSA_OK;
@@ -153,7 +156,7 @@ extern "C" int dsa_kv_window_write(const void* kv, void* kv_cache, float* scales
   if (B == 0) return DSA_OK;
   launch_pdl(kv_window_write_kernel, dim3(B), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
              static_cast<const __nv_bfloat16*>(kv), static_cast<__nv_bfloat16*>(kv_cache), scales, pos, D, rope_dim,
-             cache_bstride, win, 448.f, 1e-4f);
+             cache_bstride, win, 448.f, float(1.0 / 448.0), 1e-4f);
   DSA_CHECK_LAUNCH("kv_window_write");
   return DSA_OK;
 }

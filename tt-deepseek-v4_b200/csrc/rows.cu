@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(1024) kv_norm_rope_write_kernel(
     const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int n_pos,
     const int32_t* __restrict__ pos, __nv_bfloat16* __restrict__ cache, int64_t cache_bstride, int win,
     __nv_bfloat16* __restrict__ kv_out, int64_t ld_out, float* __restrict__ scales, int D, int rope_dim,
-    float fp8_max, float q_eps, int32_t* __restrict__ status) {
+    float fp8_max, float inv_max, float q_eps, int32_t* __restrict__ status) {
   __shared__ float red[32];
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(1024) kv_norm_rope_write_kernel(
   if (c0 < nope) {
     // act_quant_block on this 64-wide block (same arithmetic as act_quant.cu)
     float amax = warp_max(fmaxf(fabsf(a), fabsf(c)));
-    const float s = __fdiv_rn(fmaxf(amax, q_eps), fp8_max);
+    const float s = __fmul_rn(fmaxf(amax, q_eps), inv_max);
     float y0 = fminf(fmaxf(__fdiv_rn(a, s), -fp8_max), fp8_max);
     float y1 = fminf(fmaxf(__fdiv_rn(c, s), -fp8_max), fp8_max);
     const __nv_fp8_storage_t q0 = __nv_cvt_float_to_fp8(y0, __NV_SATFINITE, __NV_E4M3);
@@ -198,7 +198,7 @@ extern "C" int dsa_kv_norm_rope_window_write(const void* kv, int64_t ld_kv, cons
   launch_pdl(kv_norm_rope_write_kernel, dim3(B), dim3((D / 64) * 32), 0, reinterpret_cast<cudaStream_t>(stream),
              static_cast<const __nv_bfloat16*>(kv), ld_kv, gamma, eps, cos_tab, sin_tab, n_pos, pos,
              static_cast<__nv_bfloat16*>(kv_cache), cache_bstride, win, static_cast<__nv_bfloat16*>(kv_out), ld_out,
-             scales, D, rope_dim, 448.f, 1e-4f, status);
+             scales, D, rope_dim, 448.f, float(1.0 / 448.0), 1e-4f, status);
   DSA_CHECK_LAUNCH("kv_norm_rope_window_write");
   return DSA_OK;
 }

@@ -227,9 +227,9 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
     t.part_ml = part_ml_out;
     t.part_o = part_o_out;
   }
-  CUtensorMap tm_q;
   DSA_CHECK_ARG(kv_bstride % kSaD == 0, "sparse_attn: kv batch stride must be a multiple of D");
   const int64_t row_stride = kv_bstride / kSaD;
+  CUtensorMap tm_q;
   if (!tma::make_2d_bf16(&tm_q, q, kSaD, uint64_t(M) * kSaH, kSaD * 2, 64, 64)) {
     set_error("sparse_attn: cuTensorMapEncodeTiled failed");
     return DSA_ERR_CUDA;

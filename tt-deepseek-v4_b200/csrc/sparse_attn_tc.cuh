@@ -1,50 +1,55 @@
 // attn.sparse on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
 // One CTA per (query row, key split), 16 warps with fixed roles, 64-key tiles
-// held in a two-slot ring (2 x 64 KB) next to the query block Q (64 KB):
+// held in a three-slot ring (3 x 64 KB); the query block lives in tensor
+// memory, so shared memory holds only the ring, P and the index list.
 //
-//   warps 5-7, 9-11, 13-15  gather producers.  Each selected kv row (1 KB) is copied whole,
-//               one 512-B half per warp instruction (16-byte cp.async from 32
-//               lanes), and scattered into the tile's eight 64-dim k-block
-//               slabs (128-B swizzled).  Measured on B200: random 1 KB rows
+// Measured tcgen05.mma costs on B200 (one issuing thread, bf16): about 80
+// cycles per instruction whatever its size below N = 128 (M = 64 or 128),
+// 89 at M = 128 x N = 128 with both operands in shared memory, 78 with A in
+// tensor memory, 128 at N = 256.  So the kernel issues few, wide MMAs:
+//
+//   S(t) = Q K_t^T as one block-diagonal product per 64-key tile: the tile
+//          is read as 128 rows x 256 dims (each key once with its dims
+//          0-255 and once with its dims 256-511) and Q' as 128 rows x 256
+//          dims the same way (each head's two dim halves), so 16 MMAs of
+//          M = 128 x N = 128 x K = 16 (A = Q' in TMEM, B = the tile in shared
+//          memory) cover the 64 heads x 64 keys x 512 dims; the two
+//          off-diagonal blocks are never read.  Rows are interleaved in
+//          16-row chunks (rows 32q..32q+15 = first halves, 32q+16..32q+31 =
+//          second halves) so that both partials of a (head, key) pair sit in
+//          the same TMEM sub-partition, where the softmax adds them.
+//   PV(t): O^T += V_t^T P_t^T  (M = 128 dims per block, N = 64 heads, K = 16
+//          keys: 16 MMAs; A = the tile read MN-major, B = P K-major) into a
+//          TMEM accumulator that lives for the whole split.
+//
+// Roles:
+//   warps 5-7, 9-11, 13-15  gather producers.  Each selected kv row (1 KB) is
+//               copied whole, one 512-B half per warp instruction (16-byte
+//               cp.async from 32 lanes), into the tile's four 16 KB pair
+//               blocks (128-B swizzled).  Measured on B200: random 1 KB rows
 //               requested whole reach ~7 TB/s from HBM, the same rows fetched
-//               128 B at a time only ~4.7 TB/s, and L2 prefetches do not help
-//               (they lowered it), so each row is read once, whole.  A tile
-//               completes on its slot's mbarrier through
+//               128 B at a time only ~4.7 TB/s, so each row is read once,
+//               whole.  A tile completes on its slot's mbarrier through
 //               cp.async.mbarrier.arrive.
-//   warp 4      MMA issuer (one thread), ready-first over two kinds of batch:
-//               S(t)  = K_t Q^T as one block-diagonal product: the tile is
-//                       read as 128 rows x 256 dims (a key's dims 0-255 in
-//                       one row, its dims 256-511 in another) against
-//                       Q' = [Q dims 0-255 | Q dims 256-511] as 128 columns,
-//                       so 16 MMAs of M=128 x N=128 x K=16 replace 32 of
-//                       M=64 x N=64 (a tcgen05.mma below N=128 costs ~80
-//                       cycles whatever its size, measured on B200).  Row r
-//                       of a key's first half pairs with columns 0-63, its
-//                       second half with columns 64-127; the two partials
-//                       of a key sit in the same TMEM sub-partition (rows
-//                       interleaved in 16-key chunks) and the softmax adds
-//                       them.  Issued once tile t has landed;
-//               PV(t): O^T += V_t^T P_t^T  (M=128 dims per block, N=64 heads,
-//                       K=64 keys; A = two adjacent k-block slabs read
-//                       MN-major, B = P, MN-major) into a TMEM accumulator that
-//                       lives for the whole split (lane = dim, column = head),
-//                       issued once the softmax of tile t wrote P; it then
-//                       releases the tile's slot for the next copy.
-//               A wait between dependent batches drains the tensor pipe
-//               (about 700 cycles measured), so the issuer keeps whichever
-//               batch is ready queued.
-//   warps 0-3   softmax.  Two 16x256b TMEM loads per warp (the two dim
-//               halves of its 16 keys) spread the 64 x 64 scores over 128
-//               threads: thread i of warp w holds keys 16w + i/4 and
-//               16w + 8 + i/4, heads 8r + 2(i%4) + {0,1}, r = 0..7.  The
-//               running max per head lives in shared memory and moves only
-//               when some score beats it by 2^8 (one barrier with an OR tells
-//               all 128 threads), so O^T is rescaled rarely and P <= 256.  P
-//               goes to one of two buffers as 128-B swizzled rows per key,
-//               written by stmatrix (the 16x256b fragment is its 8x8 layout).
-//               The epilogue reads O^T back (lane = output dim) and stores
-//               coalesced rows.
+//   warp 4      MMA issuer (one thread), ready-first: PV(t) as soon as P(t)
+//               is written (it frees the tile's slot), else S(t) as soon as
+//               tile t has landed and the softmax has read S(t-1).
+//   warps 0-3   softmax.  Warp w owns heads 16w..16w+15: per 16 keys, two
+//               16x256b TMEM loads (the two dim halves) give thread i the
+//               scores of heads 16w + i/4 and 16w + 8 + i/4 for keys
+//               2(i%4) + {0,1} (+8).  Per-head maxima are a 4-lane shuffle.
+//               The running max moves only when a score beats it by 2^8
+//               (one barrier with an OR tells all 128 threads), so O^T is
+//               rescaled rarely and P <= 256.  P goes to one of two buffers
+//               as 128-B swizzled rows per head (stmatrix: the 16x256b
+//               fragment is its 8x8 layout).  The epilogue reads O^T back
+//               (lane = output dim) and stores coalesced rows.
+//   all warps   at the start, the query block is brought into the third
+//               ring slot by TMA (128-B swizzled, 8 boxes of 64 heads x 64
+//               dims); each warp then moves a quarter of its sub-partition's
+//               rows of Q' into tensor memory (conflict-free ld.shared,
+//               tcgen05.st), after which the slot takes its first tile.
 //
 // Every mbarrier wait is bounded (about a second); a wait that runs out sets
 // a status bit and an abort flag that makes all later waits of the CTA return
@@ -62,7 +67,7 @@ constexpr int H = 64;
 constexpr int D = 512;
 constexpr int TK = 64;                                // keys per tile
 constexpr int KB = D / 64;                            // 64-dim k-blocks per row
-constexpr int NT = 2;                                 // tile slots
+constexpr int NT = 3;                                 // tile slots
 constexpr int kSlabBytes = TK * 128;                  // one 64-dim k-block of a tile: 8 KB
 constexpr int kTileBytes = KB * kSlabBytes;           // 64 KB
 // A tile slot holds four 16 KB pair blocks; pair block j holds k-blocks j
@@ -81,27 +86,26 @@ __device__ __forceinline__ int producer_index(int w) { return w - 5 - ((w - 4) >
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;             // log2 units
-constexpr int kQBytes = H * D * 2;                    // 64 KB: 8 k-blocks of [64 heads x 128 B]
-constexpr int kQBlock = H * 128;                      // 8 KB
-constexpr int kPBytes = TK * H * 2;                   // 8 KB per buffer: [64 keys x 64 heads] bf16
+constexpr int kPBytes = H * TK * 2;                   // 8 KB per buffer: [64 heads x 64 keys] bf16
 constexpr int kMaxTilesPerSplit = 36;
 constexpr int kIdxCap = kMaxTilesPerSplit * TK;       // indices staged per split
+constexpr int kIdxPerThread = (kIdxCap + THREADS - 1) / THREADS;
 constexpr int kAuxBytes = 4096;
-constexpr int kOffQ = 0;
-constexpr int kOffRing = kOffQ + kQBytes;
+constexpr int kOffRing = 0;
 constexpr int kOffP = kOffRing + NT * kTileBytes;
 constexpr int kOffAux = kOffP + 2 * kPBytes;
 constexpr int kOffIdx = kOffAux + kAuxBytes;
 constexpr int kSmemBytes = kOffIdx + kIdxCap * 4 + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0;                          // O^T: 4 blocks of [128 dims x 64 heads]
-constexpr uint32_t kColS = 256;                        // S: 2 buffers of [128 rows x 128 cols], M=128 layout
-constexpr uint32_t kSCols = 128;
+constexpr uint32_t kColO = 0;     // O^T: 4 blocks of [128 dims x 64 heads]
+constexpr uint32_t kColQ = 256;   // Q': 128 rows x 256 bf16 (128 columns)
+constexpr uint32_t kColS = 384;   // S: [128 Q' rows x 128 tile rows] fp32
 constexpr uint32_t kIdescS = tc::idesc_bf16(128, 128, false, false);
-constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 64, true, true);
+constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 64, true, false);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-static_assert(kColS + 2 * kSCols <= kTmemCols, "TMEM columns");
-static_assert(TK % 16 == 0 && TK <= 64, "tile");
+static_assert(kColS + 128 <= kTmemCols, "TMEM columns");
+static_assert(TK == 64, "the block-diagonal layout assumes 64-key tiles");
+static_assert(kIdxCap % 32 == 0 && THREADS % 32 == 0, "index staging ballots whole warps");
 
 enum : int { kStatusBadIndex = 1, kStatusTimeout = 2 };
 
@@ -126,7 +130,8 @@ struct Args {
 
 // trace slots (each kTrTiles long): producers issued tile t / MMA got tile t /
 // MMA issued S(t) / MMA issued PV(t) / softmax got S(t) / softmax wrote P(t) /
-// misc (0: start, 1: end, 2: last PV done, 3: l reduced, 4: O stored)
+// misc (0: start, 1: end, 2: last PV done, 3: l reduced, 4: O stored,
+// 5: indices staged, 6: Q' stored)
 enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3, kTrPV = 4, kTrSGot = 5, kTrPDone = 6,
              kTrMisc = 7 };
 // Per-tile clock stamps for timeline analysis: compiled in only with
@@ -143,15 +148,15 @@ enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3,
 #endif
 
 struct Aux {
-  float m[H];        // running max per head (log2 units)
-  float alpha[H];    // rescale factor of the last max update
-  float f[H];        // epilogue scale per head
-  float red[4][H];   // per-warp partial reductions
+  float alpha[H];                 // rescale factor of the last max update
+  float f[H];                     // epilogue scale per head
+  uint32_t vmask[kIdxCap / 32];   // validity bits of the staged indices
+  uint64_t q_tma;
   uint64_t q_full;
   uint64_t full[NT];
   uint64_t empty[NT];
-  uint64_t s_full[2];
-  uint64_t s_free[2];
+  uint64_t s_full;
+  uint64_t s_free;
   uint64_t p_full[2];
   uint64_t pv_done[2];
   uint64_t mma_done;
@@ -168,8 +173,29 @@ __device__ __forceinline__ uint32_t chunk_off(int k, int c) {
   const int row = ((k >> 4) << 5) + ((kb >> 2) << 4) + (k & 15);
   return (kb & 3) * kPairBytes + row * 128 + ((((c & 7) ^ (k & 7))) << 4);
 }
-// Q is loaded in the same pairing: k-block kb at slab position 2 (kb % 4) + kb / 4
-__host__ __device__ constexpr int q_slab_pos(int kb) { return 2 * (kb & 3) + (kb >> 2); }
+
+// Q' rows: warp w's sub-partition (w % 4) holds rows 32 (w % 4) + i = head
+// 16 (w % 4) + i % 16, dim half i / 16; warp w moves column quarter w / 4
+// (64 dims = k-block 4 half + w / 4) of those rows from the TMA copy of Q in
+// shared memory (box kb at kb * 8 KB, row h at h * 128 B, 16-B chunks
+// swizzled by h % 8) into tensor memory, then arrives on q_full.
+__device__ __forceinline__ void q_part_to_tmem(uint32_t sq, uint32_t tmem, int warp, int lane, uint64_t* q_full) {
+  const int sp = warp & 3, cq = warp >> 2;
+  const int h = 16 * sp + (lane & 15), kb = 4 * (lane >> 4) + cq;
+  const uint32_t row = sq + kb * (H * 128) + h * 128;
+  uint32_t w[32];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t addr = row + ((c ^ (h & 7)) << 4);
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                 : "r"(addr));
+  }
+  tc::tmem_st32_u(tmem + ((uint32_t)(32 * sp) << 16) + kColQ + 32 * cq, w);
+  tc::tmem_wait_st();
+  tc::fence_before_sync();
+  tc::mbar_arrive(smem_u32(q_full));
+}
 
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a,
                                                                     const __grid_constant__ CUtensorMap tm_q,
@@ -178,39 +204,36 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Aux* aux = reinterpret_cast<Aux*>(smem + kOffAux);
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t sQ = sbase + kOffQ, sRing = sbase + kOffRing, sP = sbase + kOffP;
+  const uint32_t sRing = sbase + kOffRing, sP = sbase + kOffP;
   volatile int* abort_flag = &aux->abort;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int m = blockIdx.y, split = blockIdx.x;
-  const int b = m / a.S;
+  const int mrow = blockIdx.y, split = blockIdx.x;
+  const int b = mrow / a.S;
   const int j_begin = split * a.tiles_per_split * TK;
   const int j_end = min(a.K, j_begin + a.tiles_per_split * TK);
   const int n = j_end > j_begin ? (j_end - j_begin + TK - 1) / TK : 0;
-  const int32_t* idxr = a.idx + int64_t(m) * a.ld_idx;
+  const int32_t* idxr = a.idx + int64_t(mrow) * a.ld_idx;
   int32_t* s_idx = reinterpret_cast<int32_t*>(smem + kOffIdx);
 #ifdef DSA_ATTN_TRACE
   long long* tr = (a.trace && blockIdx.x == 0 && blockIdx.y == 0) ? a.trace : nullptr;
 #endif
   if (tid == 0) SA_TRACE(kTrMisc, 0);
 
-  if (tid < H) aux->m[tid] = -INFINITY;
   if (tid == 0) aux->abort = 0;
-
   if (warp == 0) {
     tc::tmem_alloc(smem_u32(&aux->tmem_base), kTmemCols);
     tc::tmem_relinquish();
   }
   if (tid == 32) {
-    tc::mbar_init(smem_u32(&aux->q_full), 1);
+    tc::mbar_init(smem_u32(&aux->q_tma), 1);
+    tc::mbar_init(smem_u32(&aux->q_full), THREADS);  // every thread stores its part of Q'
     for (int s = 0; s < NT; ++s) {
       tc::mbar_init(smem_u32(&aux->full[s]), 32 * kProducerWarps);  // one cp.async arrival per producer lane
       tc::mbar_init(smem_u32(&aux->empty[s]), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      tc::mbar_init(smem_u32(&aux->s_full[s]), 1);
-      tc::mbar_init(smem_u32(&aux->s_free[s]), 4);
-    }
+    tc::mbar_init(smem_u32(&aux->s_full), 1);
+    tc::mbar_init(smem_u32(&aux->s_free), 4);
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(smem_u32(&aux->p_full[s]), 1);
       tc::mbar_init(smem_u32(&aux->pv_done[s]), 1);
@@ -222,21 +245,45 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   // previous kernels' outputs
   pdl_wait();
   pdl_launch_dependents();
+  // The query block into the last ring slot (free until Q' is in TMEM).
+  const uint32_t sQstage = sRing + (NT - 1) * kTileBytes;
+  if (tid == 32) {
+    tma::prefetch_map(&tm_q);
+    tma::mbar_arrive_expect_tx(smem_u32(&aux->q_tma), H * D * 2);
+#pragma unroll
+    for (int kb = 0; kb < KB; ++kb)
+      tma::load_2d(sQstage + kb * (H * 128), &tm_q, kb * 64, mrow * H, smem_u32(&aux->q_tma));
+  }
   // The split's index list, staged once: -1 for masked / padding slots,
-  // out-of-range rows clamped (and reported through status).
-  for (int e = tid; e < n * TK; e += THREADS) {
-    const int j = j_begin + e;
-    int id = (j < j_end) ? idxr[j] : -1;
-    if (id >= a.kv_rows) {
-      if (a.status) atomicOr(a.status, kStatusBadIndex);
-      id = int(a.kv_rows - 1);
+  // out-of-range rows clamped (and reported through status), plus one
+  // validity bit per index.  All loads are issued before the first store.
+  {
+    int ids[kIdxPerThread];
+#pragma unroll
+    for (int k = 0; k < kIdxPerThread; ++k) {
+      const int e = tid + k * THREADS;
+      ids[k] = (e < n * TK && j_begin + e < j_end) ? __ldg(idxr + j_begin + e) : -1;
     }
-    s_idx[e] = id < 0 ? -1 : id;
+#pragma unroll
+    for (int k = 0; k < kIdxPerThread; ++k) {
+      const int e = tid + k * THREADS;
+      if (e < n * TK) {  // whole warps: n * TK is a multiple of 64
+        int id = ids[k];
+        if (id >= a.kv_rows) {
+          if (a.status) atomicOr(a.status, kStatusBadIndex);
+          id = int(a.kv_rows - 1);
+        }
+        s_idx[e] = id < 0 ? -1 : id;
+        const uint32_t bits = __ballot_sync(0xffffffffu, id >= 0);
+        if (lane == 0) aux->vmask[e >> 5] = bits;
+      }
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = aux->tmem_base;
+  if (tid == 0) SA_TRACE(kTrMisc, 5);
 
   auto wait = [&](const uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
@@ -248,18 +295,23 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     __syncwarp();
   };
 
+  // every warp moves its part of Q' once the TMA copy has landed
+  auto q_part = [&]() {
+    warp_wait(&aux->q_tma, 0);
+    q_part_to_tmem(sQstage, tmem, warp, lane, &aux->q_full);
+  };
+
   if (is_producer_warp(warp)) {
     // ------------------------------------------------------------ producers
+    // Tiles 0 .. NT-2 are requested first; the last slot holds the query
+    // block until every thread has moved its part of Q' (q_full).
     const int pw = producer_index(warp);
-    if (pw == 0 && lane == 0 && n > 0) {
-      tma::prefetch_map(&tm_q);
-      tma::mbar_arrive_expect_tx(smem_u32(&aux->q_full), kQBytes);
-#pragma unroll
-      for (int kb = 0; kb < KB; ++kb)
-        tma::load_2d(sQ + q_slab_pos(kb) * kQBlock, &tm_q, kb * 64, m * H, smem_u32(&aux->q_full));
-    }
     const __nv_bfloat16* kvb = a.kv + int64_t(b) * kv_row_base_stride * D;
     for (int t = 0; t < n; ++t) {
+      if (t == NT - 1) {
+        q_part();
+        warp_wait(&aux->q_full, 0);
+      }
       const int slot = t % NT;
       if (t >= NT) warp_wait(&aux->empty[slot], ((t / NT) - 1) & 1);
       const uint32_t dst = sRing + slot * kTileBytes;
@@ -275,26 +327,28 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tc::cp_async_arrive_noinc(smem_u32(&aux->full[slot]));
       if (pw == 0 && lane == 0) SA_TRACE(kTrIssue, t);
     }
+    if (n < NT) q_part();
     cp_async_wait<0>();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
+    q_part();
     if (lane == 0 && n > 0) {
       const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
-      const uint32_t q_lo = tc::desc_lo(sQ, 16);
       const uint32_t k_lo = tc::desc_lo(sRing, 16);          // K-major: LBO unused
       const uint32_t v_lo = tc::desc_lo(sRing, kPairBytes);  // MN-major: LBO = the next 64 dims (next pair block)
-      const uint32_t p_lo = tc::desc_lo(sP, kPBytes);        // MN-major, one 64-head group
+      const uint32_t p_lo = tc::desc_lo(sP, 16);             // K-major rows of 64 keys per head
       wait(&aux->q_full, 0);
+      tc::fence_after_sync();
       // Ready-first issue: PV(np) as soon as P(np) is written (it frees the
       // tile's slot for the next copy), else S(ns) as soon as tile ns has
-      // landed and its S buffer is free.  Keeping MMAs queued avoids the
-      // ~700-cycle drain and refill of the tensor pipe that a wait between
-      // dependent batches costs.
+      // landed and the softmax has read S(ns - 1).  Keeping MMAs queued
+      // avoids the ~700-cycle drain and refill of the tensor pipe that a
+      // wait between dependent batches costs.
       int ns = 0, np = 0;
       long long last = clock64();
       while (np < n) {
         bool did = false;
-        if (np < ns && tc::mbar_try_wait(smem_u32(&aux->p_full[np & 1]), (np >> 1) & 1)) {
+        if (np < ns && tc::mbar_test_wait(smem_u32(&aux->p_full[np & 1]), (np >> 1) & 1)) {
           tc::fence_after_sync();
           const uint32_t vs = v_lo + (np % NT) * (kTileBytes / 16);
           const uint32_t ps = p_lo + (np & 1) * (kPBytes / 16);
@@ -307,7 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
             for (int kk = 0; kk < TK / 16; ++kk) {
               const uint32_t off = (jb & 1) * 2 * kPairBytes + (jb >> 1) * 2048 + kk * 4096;
               const uint64_t ad = tc::desc_pack(vs + off / 16, hi);
-              const uint64_t bd = tc::desc_pack(ps + (kk * 2048) / 16, hi);
+              const uint64_t bd = tc::desc_pack(ps + (kk * 32) / 16, hi);
               tc::mma_bf16(tmem + kColO + H * jb, ad, bd, kIdescPV, (np > 0 || kk > 0) ? 1u : 0u);
             }
           }
@@ -316,24 +370,22 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
           SA_TRACE(kTrPV, np);
           ++np;
           did = true;
-        } else if (ns < n && ns < np + NT && tc::mbar_try_wait(smem_u32(&aux->full[ns % NT]), (ns / NT) & 1) &&
-                   (ns < 2 || tc::mbar_try_wait(smem_u32(&aux->s_free[ns & 1]), ((ns - 2) >> 1) & 1))) {
+        } else if (ns < n && ns < np + NT && tc::mbar_test_wait(smem_u32(&aux->full[ns % NT]), (ns / NT) & 1) &&
+                   (ns == 0 || tc::mbar_test_wait(smem_u32(&aux->s_free), (ns - 1) & 1))) {
           tc::fence_after_sync();
           SA_TRACE(kTrMmaGot, ns);
           const uint32_t ks0 = k_lo + (ns % NT) * (kTileBytes / 16);
-          const uint32_t d = tmem + kColS + kSCols * (ns & 1);
-          // S(ns): 16 block-diagonal MMAs of M=128 rows x N=128 x K=16 dims
-          // over the four pair blocks (tile and Q' alike)
+          // S(ns): 16 block-diagonal MMAs of M=128 x N=128 x K=16 over the
+          // four pair blocks; Q' column 32j + 8ks holds the same dims
 #pragma unroll
           for (int j = 0; j < KB / 2; ++j) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t ad = tc::desc_pack(ks0 + (j * kPairBytes + ks * 32) / 16, hi);
-              const uint64_t bd = tc::desc_pack(q_lo + (j * 2 * kQBlock + ks * 32) / 16, hi);
-              tc::mma_bf16(d, ad, bd, kIdescS, (j | ks) ? 1u : 0u);
+              const uint64_t bd = tc::desc_pack(ks0 + (j * kPairBytes + ks * 32) / 16, hi);
+              tc::mma_bf16_ts(tmem + kColS, tmem + kColQ + 32 * j + 8 * ks, bd, kIdescS, (j | ks) ? 1u : 0u);
             }
           }
-          tc::mma_commit(smem_u32(&aux->s_full[ns & 1]));
+          tc::mma_commit(smem_u32(&aux->s_full));
           SA_TRACE(kTrS, ns);
           ++ns;
           did = true;
@@ -353,88 +405,77 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     __syncwarp();
   } else if (warp < 4) {
     // ------------------------------------------------------------ softmax warps 0-3
-    // Keys 16w..16w+15: their low-dim partials sit in TMEM lanes 32w..32w+15
-    // (columns 0-63 of the S buffer), their high-dim partials in lanes
-    // 32w+16..32w+31 (columns 64-127); S = low + high.
+    q_part();
+    if (tid == 0) SA_TRACE(kTrMisc, 6);
+    // Heads 16w..16w+15: first-half partials in TMEM lanes 32w..32w+15,
+    // second-half partials in lanes 32w+16..32w+31.  Keys 16q..16q+15 are S
+    // columns 32q..32q+15 for the first halves and 32q+16.. for the second.
     const int q4 = lane & 3, g8 = lane >> 2;
-    const int ka = warp * 16 + g8, kb2 = ka + 8;  // this thread's two keys
-    const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
-    const uint32_t tq_hi = tmem + ((uint32_t)(warp * 32 + 16) << 16) + H;
-    // [r][e] -> head 8r + 2 q4 + e: running max (a register copy of aux->m)
-    // and partial sums of p over this thread's keys
-    float mr[16], lp[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      mr[i] = -INFINITY;
-      lp[i] = 0.f;
-    }
-    // stmatrix x4 number j writes the 8x8 blocks (keys 16w + 8g.., heads
-    // 8r..) for (g, r) = (0, 2j), (1, 2j), (0, 2j+1), (1, 2j+1); lane l gives
-    // the address of row l % 8 of block l / 8: one 16-B chunk of a P row
-    const int sm_g = (lane >> 3) & 1, sm_r = lane >> 4, sm_key = warp * 16 + 8 * sm_g + (lane & 7);
+    const int ha = warp * 16 + g8, hb = ha + 8;  // this thread's two heads
+    const uint32_t t_lo = tmem + ((uint32_t)(warp * 32) << 16) + kColS;
+    const uint32_t t_hi = tmem + ((uint32_t)(warp * 32 + 16) << 16) + kColS + 16;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    // stmatrix x4 number j writes the 8x8 blocks (head group g = a/b, key
+    // chunk c) = (a, 2j), (b, 2j), (a, 2j+1), (b, 2j+1); lane l gives the
+    // address of row l % 8 of block l / 8: one 16-B chunk of a P row
+    const int sm_head = warp * 16 + 8 * ((lane >> 3) & 1) + (lane & 7), sm_c = lane >> 4;
     for (int t = 0; t < n; ++t) {
-      const bool va = s_idx[t * TK + ka] >= 0, vb = s_idx[t * TK + kb2] >= 0;
-      warp_wait(&aux->s_full[t & 1], (t >> 1) & 1);
+      const uint64_t vm = (uint64_t(aux->vmask[2 * t + 1]) << 32) | aux->vmask[2 * t];
+      warp_wait(&aux->s_full, t & 1);
       tc::fence_after_sync();
       if (tid == 0) SA_TRACE(kTrSGot, t);
-      float v[32], vh[32];
-      tc::tmem_ld16x256b_x8(tq + kColS + kSCols * (t & 1), v);
-      tc::tmem_ld16x256b_x8(tq_hi + kColS + kSCols * (t & 1), vh);
-      tc::tmem_wait_ld();
+      // v[8q + 4r + e]: head a, key 16q + 8r + 2 q4 + e; v[8q + 4r + 2 + e]: head b
+      float v[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += vh[i];
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float lo[16], hi[16];
+        tc::tmem_ld16x256b_x2(t_lo + 64 * h2, lo);
+        tc::tmem_ld16x256b_x2(t_lo + 64 * h2 + 32, lo + 8);
+        tc::tmem_ld16x256b_x2(t_hi + 64 * h2, hi);
+        tc::tmem_ld16x256b_x2(t_hi + 64 * h2 + 32, hi + 8);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[16 * h2 + i] = lo[i] + hi[i];
+      }
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(smem_u32(&aux->s_free[t & 1]));
-      bool need = false;
+      if (lane == 0) tc::mbar_arrive(smem_u32(&aux->s_free));
+      float mxa = -INFINITY, mxb = -INFINITY;
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        v[4 * r + 0] = va ? v[4 * r + 0] * a.scale_log2 : -INFINITY;
-        v[4 * r + 1] = va ? v[4 * r + 1] * a.scale_log2 : -INFINITY;
-        v[4 * r + 2] = vb ? v[4 * r + 2] * a.scale_log2 : -INFINITY;
-        v[4 * r + 3] = vb ? v[4 * r + 3] * a.scale_log2 : -INFINITY;
-        need |= fmaxf(v[4 * r + 0], v[4 * r + 2]) > mr[2 * r] + kRescaleThreshold;
-        need |= fmaxf(v[4 * r + 1], v[4 * r + 3]) > mr[2 * r + 1] + kRescaleThreshold;
-      }
-      const bool any = tc::named_bar_red_or(1, 128, need);
-      if (any) {
-        // tile max per head: this thread's two keys, then the 8 lanes that
-        // share q4 (xor 4, 8, 16), then the 4 warps through shared memory
-        float mx[16];
+      for (int q = 0; q < 4; ++q) {
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          mx[2 * r] = fmaxf(v[4 * r + 0], v[4 * r + 2]);
-          mx[2 * r + 1] = fmaxf(v[4 * r + 1], v[4 * r + 3]);
-        }
+        for (int r = 0; r < 2; ++r) {
 #pragma unroll
-        for (int off = 4; off < 32; off <<= 1)
-#pragma unroll
-          for (int i = 0; i < 16; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], off));
-        if (g8 == 0) {
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            aux->red[warp][8 * r + 2 * q4] = mx[2 * r];
-            aux->red[warp][8 * r + 2 * q4 + 1] = mx[2 * r + 1];
+          for (int e = 0; e < 2; ++e) {
+            const bool ok = (vm >> (16 * q + 8 * r + 2 * q4 + e)) & 1u;
+            float& xa = v[8 * q + 4 * r + e];
+            float& xb = v[8 * q + 4 * r + 2 + e];
+            xa = ok ? xa * a.scale_log2 : -INFINITY;
+            xb = ok ? xb * a.scale_log2 : -INFINITY;
+            mxa = fmaxf(mxa, xa);
+            mxb = fmaxf(mxb, xb);
           }
         }
-        tc::named_bar_sync(1, 128);
-        if (tid < H) {
-          const float tmax = fmaxf(fmaxf(aux->red[0][tid], aux->red[1][tid]), fmaxf(aux->red[2][tid], aux->red[3][tid]));
-          const float mo = aux->m[tid];
-          const float mn = fmaxf(mo, tmax);
-          aux->alpha[tid] = (mn == -INFINITY) ? 1.f : tc::ex2(mo - mn);
-          aux->m[tid] = mn;
+      }
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 1));
+      mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, 2));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 1));
+      mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, 2));
+      const bool need = (mxa > m_a + kRescaleThreshold) || (mxb > m_b + kRescaleThreshold);
+      const bool any = tc::named_bar_red_or(1, 128, need);
+      if (any) {
+        const float na = fmaxf(m_a, mxa), nb = fmaxf(m_b, mxb);
+        const float al_a = (na == -INFINITY) ? 1.f : tc::ex2(m_a - na);
+        const float al_b = (nb == -INFINITY) ? 1.f : tc::ex2(m_b - nb);
+        l_a *= al_a;
+        l_b *= al_b;
+        m_a = na;
+        m_b = nb;
+        if (q4 == 0) {
+          aux->alpha[ha] = al_a;
+          aux->alpha[hb] = al_b;
         }
         tc::named_bar_sync(1, 128);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const float2 al = *reinterpret_cast<const float2*>(&aux->alpha[8 * r + 2 * q4]);
-          const float2 mn = *reinterpret_cast<const float2*>(&aux->m[8 * r + 2 * q4]);
-          lp[2 * r] *= al.x;
-          lp[2 * r + 1] *= al.y;
-          mr[2 * r] = mn.x;
-          mr[2 * r + 1] = mn.y;
-        }
         if (t >= 1) {
           // (rare) O^T *= alpha per column, once PV(t-1) has completed
           warp_wait(&aux->pv_done[(t - 1) & 1], ((t - 1) >> 1) & 1);
@@ -454,29 +495,33 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
           tc::tmem_wait_st();
         }
       }
-      // p = 2^(x - m) <= 2^8, packed to bf16 pairs: pa[r] for key ka, pb[r]
-      // for key kb2, heads 8r + 2 q4 + {0, 1}
-      uint32_t pa[8], pb[8];
+      // p = 2^(x - m) <= 2^8, packed to bf16 pairs: wa[c] for head a, keys
+      // 8c + 2 q4 + {0, 1}; wb[c] for head b
+      uint32_t wa[8], wb[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float p0 = (v[4 * r + 0] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 0] - mr[2 * r]);
-        const float p1 = (v[4 * r + 1] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 1] - mr[2 * r + 1]);
-        const float p2 = (v[4 * r + 2] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 2] - mr[2 * r]);
-        const float p3 = (v[4 * r + 3] == -INFINITY) ? 0.f : tc::ex2(v[4 * r + 3] - mr[2 * r + 1]);
-        lp[2 * r] += p0 + p2;
-        lp[2 * r + 1] += p1 + p3;
-        pa[r] = pack_bf16x2(p0, p1);
-        pb[r] = pack_bf16x2(p2, p3);
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int i0 = 8 * q + 4 * r;
+          const float p0 = (v[i0 + 0] == -INFINITY) ? 0.f : tc::ex2(v[i0 + 0] - m_a);
+          const float p1 = (v[i0 + 1] == -INFINITY) ? 0.f : tc::ex2(v[i0 + 1] - m_a);
+          const float p2 = (v[i0 + 2] == -INFINITY) ? 0.f : tc::ex2(v[i0 + 2] - m_b);
+          const float p3 = (v[i0 + 3] == -INFINITY) ? 0.f : tc::ex2(v[i0 + 3] - m_b);
+          l_a += p0 + p1;
+          l_b += p2 + p3;
+          wa[2 * q + r] = pack_bf16x2(p0, p1);
+          wb[2 * q + r] = pack_bf16x2(p2, p3);
+        }
       }
       // P buffer t & 1 was last read by PV(t-2)
       if (t >= 2) warp_wait(&aux->pv_done[t & 1], ((t - 2) >> 1) & 1);
       const uint32_t pbuf = sP + (t & 1) * kPBytes;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int r = 2 * j + sm_r;
-        const uint32_t addr = pbuf + sm_key * 128 + ((r ^ (sm_key & 7)) << 4);
-        asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pa[2 * j]),
-                     "r"(pb[2 * j]), "r"(pa[2 * j + 1]), "r"(pb[2 * j + 1])
+        const int c = 2 * j + sm_c;
+        const uint32_t addr = pbuf + sm_head * 128 + ((c ^ (sm_head & 7)) << 4);
+        asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(wa[2 * j]),
+                     "r"(wb[2 * j]), "r"(wa[2 * j + 1]), "r"(wb[2 * j + 1])
                      : "memory");
       }
       tc::fence_proxy_async();
@@ -489,64 +534,66 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     if (n > 0) warp_wait(&aux->pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1);
     tc::fence_after_sync();
     if (tid == 0) SA_TRACE(kTrMisc, 2);
-    // l per head: each head's partial sums sit in 32 threads (8 lanes of
-    // each warp); gather them through the P buffers, free now that the last
-    // PV has completed.  (A shuffle tree here measured ~10k cycles, this ~1k.)
-    float* lbuf = reinterpret_cast<float*>(smem + kOffP);
+    // l per head: this thread's partial sums over its keys, then the 4 lanes
+    // of the quad
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+    if (q4 == 0) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) lbuf[i * 128 + tid] = lp[i];
-    tc::named_bar_sync(1, 128);
-    if (tid < H) {
-      const float mh = aux->m[tid];
-      const float* lr = lbuf + (2 * (tid >> 3) + (tid & 1)) * 128 + ((tid & 7) >> 1);
-      float lw[4];
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        lw[w] = 0.f;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) lw[w] += lr[w * 32 + g * 4];
-      }
-      const float lh = (lw[0] + lw[1]) + (lw[2] + lw[3]);
-      if (a.final_mode) {
-        const float sk = a.sink[tid] * kLog2e;
-        const float Mx = fmaxf(mh, sk);
-        const float w = (mh == -INFINITY) ? 0.f : exp2f(mh - Mx);
-        const float L = lh * w + exp2f(sk - Mx);
-        aux->f[tid] = w / L;
-        if (a.lse) a.lse[int64_t(m) * H + tid] = (Mx + log2f(L)) * kLn2;
-      } else {
-        const int64_t base = int64_t(split) * a.M + m;
-        a.part_ml[(base * H + tid) * 2 + 0] = (mh == -INFINITY) ? -INFINITY : mh * kLn2;
-        a.part_ml[(base * H + tid) * 2 + 1] = lh;
-        aux->f[tid] = 1.f;
+      for (int g = 0; g < 2; ++g) {
+        const int h = g ? hb : ha;
+        const float mh = g ? m_b : m_a, lh = g ? l_b : l_a;
+        if (a.final_mode) {
+          const float sk = a.sink[h] * kLog2e;
+          const float Mx = fmaxf(mh, sk);
+          const float w = (mh == -INFINITY) ? 0.f : exp2f(mh - Mx);
+          const float L = lh * w + exp2f(sk - Mx);
+          aux->f[h] = w / L;
+          if (a.lse) a.lse[int64_t(mrow) * H + h] = (Mx + log2f(L)) * kLn2;
+        } else {
+          const int64_t base = int64_t(split) * a.M + mrow;
+          a.part_ml[(base * H + h) * 2 + 0] = (mh == -INFINITY) ? -INFINITY : mh * kLn2;
+          a.part_ml[(base * H + h) * 2 + 1] = lh;
+          aux->f[h] = 1.f;
+        }
       }
     }
-    tc::named_bar_sync(1, 128);
-    if (tid == 0) SA_TRACE(kTrMisc, 3);
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    const int dloc = warp * 32 + lane;
-#pragma unroll 1
-    for (int jb = 0; jb < 4; ++jb) {
-      const int d = 128 * jb + dloc;
+  } else {
+    // ------------------------------------------------------------ idle warps 8, 12
+    q_part();
+  }
+  // -------------------------------------------------------------- O^T drain
+  // Every warp drains part of O^T: warp w reads TMEM lanes 32 (w % 4).. (its
+  // sub-partition) of block w / 4, i.e. output dims 128 (w / 4) + 32 (w % 4)
+  // + lane, for all 64 heads, and stores coalesced 128-B rows per head.
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (tid == 0) SA_TRACE(kTrMisc, 3);
+  {
+    const int sp = warp & 3, jb = warp >> 2;
+    const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
+    const int d = 128 * jb + 32 * sp + lane;
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        float o[32];
-        if (n > 0) {
-          tc::tmem_ld32(tl + kColO + H * jb + 32 * hf, o);
-          tc::tmem_wait_ld();
-        } else {
+    for (int hf = 0; hf < 2; ++hf) {
+      float o[32];
+      if (n > 0) {
+        tc::tmem_ld32(tl + kColO + H * jb + 32 * hf, o);
+        tc::tmem_wait_ld();
+      } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0.f;
-        }
-        if (a.final_mode) {
-          __nv_bfloat16* om = a.out + int64_t(m) * H * D + d;
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (a.final_mode) {
+        __nv_bfloat16* om = a.out + int64_t(mrow) * H * D + d;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) om[(32 * hf + i) * D] = f2bf(o[i] * aux->f[32 * hf + i]);
-        } else {
-          float* po = a.part_o + (int64_t(split) * a.M + m) * H * D + d;
+        for (int i = 0; i < 32; ++i) om[(32 * hf + i) * D] = f2bf(o[i] * aux->f[32 * hf + i]);
+      } else {
+        float* po = a.part_o + (int64_t(split) * a.M + mrow) * H * D + d;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) po[(32 * hf + i) * D] = o[i];
-        }
+        for (int i = 0; i < 32; ++i) po[(32 * hf + i) * D] = o[i];
       }
     }
   }
