@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--topk", type=int, default=2048)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-seq-split", action="store_true",
+                    help="skip the config-3 sequence-split record that the default (cfg2) run adds")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel timings to stderr")
     ap.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg2",
                     help="cfg0: one layer, batch 1, 4096-token context; cfg1: compressor emit path alone; "
@@ -240,32 +242,49 @@ def time_kernels(path, inputs, outs, reps=3):
     return res
 
 
-def cpu_baseline_sample(args, seconds=12.0, n_seq=2):
-    """Time the CPU oracle (all host threads) on a bounded sample of the same
-    workload: n_seq sequences of one layer at full config-2 shapes; report
-    tok/s for the 43-layer step."""
-    import torch
-    import oracle as O
-    torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    W, k, ctx = 128, args.topk, args.ctx
-    T = ctx // 4
-    B = n_seq
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def _oracle_state(O, torch, B, W, T, k, ctx, g):
     cos, sin = O.rope_tables(64, ctx + 8, compressed=True)
     ckv, csc = O.compressor_init_state(B, 512, 4, True)
     ikv, isc = O.compressor_init_state(B, 128, 4, True)
-    st = O.LayerState(kv_cache=torch.randn(B, W + T + 4, 512, generator=g).to(torch.bfloat16),
-                      idx_kv_cache=torch.randn(B, T + 4, 128, generator=g).to(torch.bfloat16),
-                      cmp_kv=ckv.normal_(generator=g), cmp_sc=csc.normal_(generator=g), icmp_kv=ikv.normal_(generator=g),
-                      icmp_sc=isc.normal_(generator=g), ape=torch.randn(4, 1024, generator=g),
-                      gamma=torch.ones(512), iape=torch.randn(4, 256, generator=g), igamma=torch.ones(128),
-                      sink=torch.randn(64, generator=g), cos=cos, sin=sin, win=W, ratio=4, index_topk=k,
-                      scale=512 ** -0.5)
+    return O.LayerState(kv_cache=torch.randn(B, W + T + 4, 512, generator=g).to(torch.bfloat16),
+                        idx_kv_cache=torch.randn(B, T + 4, 128, generator=g).to(torch.bfloat16),
+                        cmp_kv=ckv.normal_(generator=g), cmp_sc=csc.normal_(generator=g),
+                        icmp_kv=ikv.normal_(generator=g), icmp_sc=isc.normal_(generator=g),
+                        ape=torch.randn(4, 1024, generator=g), gamma=torch.ones(512),
+                        iape=torch.randn(4, 256, generator=g), igamma=torch.ones(128),
+                        sink=torch.randn(64, generator=g), cos=cos, sin=sin, win=W, ratio=4, index_topk=k,
+                        scale=512 ** -0.5)
+
+
+def _oracle_inputs(torch, B, g):
     bf = torch.bfloat16
-    x = [torch.randn(B, 1, 64, 512, generator=g).to(bf), torch.randn(B, 512, generator=g).to(bf),
-         torch.randn(B, 1024, generator=g), torch.randn(B, 1024, generator=g),
-         torch.randn(B, 64, 128, generator=g).to(bf), torch.randn(B, 256, generator=g),
-         torch.randn(B, 256, generator=g), 0.02 * torch.randn(B, 64, generator=g)]
+    return [torch.randn(B, 1, 64, 512, generator=g).to(bf), torch.randn(B, 512, generator=g).to(bf),
+            torch.randn(B, 1024, generator=g), torch.randn(B, 1024, generator=g),
+            torch.randn(B, 64, 128, generator=g).to(bf), torch.randn(B, 256, generator=g),
+            torch.randn(B, 256, generator=g), 0.02 * torch.randn(B, 64, generator=g)]
+
+
+def cpu_baseline_sample(args, seconds=12.0, n_seq=None):
+    """Time the CPU oracle (all host threads) on a bounded sample of the same
+    decode workload: ``n_seq`` sequences (default min(2, batch)) of one layer
+    at the run's shapes (context, top-k, window 128); report tok/s for the
+    ``args.layers``-layer step."""
+    import torch
+    import oracle as O
+    torch.set_num_threads(host_cores())
+    g = torch.Generator().manual_seed(0)
+    W, k, ctx = 128, args.topk, args.ctx
+    T = ctx // 4
+    B = n_seq if n_seq is not None else min(2, args.batch)
+    st = _oracle_state(O, torch, B, W, T, k, ctx, g)
+    x = _oracle_inputs(torch, B, g)
     pos = ctx - 1          # every repetition is the same decode step (state rewritten in place)
     n = 0
     t0 = time.perf_counter()
@@ -274,11 +293,71 @@ def cpu_baseline_sample(args, seconds=12.0, n_seq=2):
         n += 1
         if time.perf_counter() - t0 > seconds:
             break
-    dt = (time.perf_counter() - t0) / n          # seconds per layer-step of n_seq sequences
-    tok_s = n_seq / (dt * args.layers)
+    dt = (time.perf_counter() - t0) / n          # seconds per layer-step of B sequences
+    tok_s = B / (dt * args.layers)
     return {"value": tok_s, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} decode steps of 1 layer x {n_seq} sequences at config-2 shapes (T=8192, k={k}, W=128), "
+            "sample": f"{n} decode steps of 1 layer x {B} sequence(s) at ctx {ctx} (T={T}, k={k}, W=128), "
                       f"{dt * 1e3:.1f} ms per layer-step, scaled to {args.layers} layers"}
+
+
+def cpu_baseline_cfg1(seconds=10.0):
+    """CPU oracle of config 1: the compressor emit path, batch 32, d 512,
+    ratio 4, non-overlap state; timed over consecutive steps from position 0."""
+    import torch
+    import oracle as O
+    torch.set_num_threads(host_cores())
+    g = torch.Generator().manual_seed(11)
+    B, d, r = 32, 512, 4
+    kv_row = torch.randn(B, d, generator=g).to(torch.bfloat16).float()
+    sc_row = torch.randn(B, d, generator=g).to(torch.bfloat16).float()
+    ape = 0.1 * torch.randn(r, d, generator=g)
+    gamma = 1 + 0.02 * torch.randn(d, generator=g)
+    cos, sin = O.rope_tables(64, 1100, compressed=True)
+    kvs, scs = O.compressor_init_state(B, d, r, False)
+    cache = torch.zeros(B, 1000 // r + 2, d, dtype=torch.bfloat16)
+    n = 0
+    t0 = time.perf_counter()
+    while n < 1000:
+        O.compressor_step(kvs, scs, kv_row, sc_row, ape, gamma, cos, sin, n, r, False, kv_cache=cache)
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": B / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} compressor steps from position 0 (batch {B}, d {d}, ratio {r}), {dt * 1e6:.1f} us per step"}
+
+
+def cpu_baseline_cfg4(seconds=10.0, group=4):
+    """CPU oracle of config 4 on a slice of the prefill chunk: groups of
+    ``group`` tokens from the end of the 4096-token chunk (the oracle gathers
+    a copy of the keys per token, so a group stays small), each against the
+    full 32768-entry key set with per-token top-2048 + causal window, until
+    ``seconds`` have passed; reported as tok/s of that slice."""
+    import torch
+    import oracle as O
+    torch.set_num_threads(host_cores())
+    g = torch.Generator().manual_seed(77)
+    S, T, n_hist, k, W = 4096, 32768, 127, 2048, 128
+    base = 131072 - S
+    n_raw = n_hist + S
+    kv = torch.randn(n_raw + T, 512, generator=g).to(torch.bfloat16)
+    ikeys = torch.randn(T, 128, generator=g).to(torch.bfloat16)
+    sink = torch.randn(64, generator=g)
+    n_tok = 0
+    t0 = time.perf_counter()
+    while n_tok < S:
+        rows = list(range(S - n_tok - group, S - n_tok))
+        q = torch.randn(group, 64, 512, generator=g).to(torch.bfloat16)
+        iq = torch.randn(group, 64, 128, generator=g).to(torch.bfloat16)
+        iw = 0.02 * torch.randn(group, 64, generator=g)
+        O.prefill_chunk(q, kv, n_raw, iq, ikeys, iw, sink, base, n_hist, T, k, W=W, rows=rows)
+        n_tok += group
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n_tok / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"the last {n_tok} of the chunk's {S} tokens in groups of {group} (T={T}, top-{k}, "
+                      f"window {W}), {dt:.1f} s"}
 
 
 def run_reference(args, rank, world):
@@ -342,8 +421,7 @@ def main():
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
-    if int(path.status.item()) != 0:
-        raise RuntimeError(f"device status {int(path.status.item())} after warm-up (1 = bad index, 2 = wait timeout)")
+    ops.raise_for_status(path.status, "warm-up steps")
     log("warm-up done; timing")
     if world > 1:
         dist.barrier()
@@ -380,8 +458,7 @@ def main():
         per_med, per_min = float(t[1].item()), float(t[2].item())
     else:
         per_med, per_min = per[len(per) // 2], per[0]
-    if int(path.status.item()) != 0:
-        raise RuntimeError("an attention index fell outside the cache during the bench")
+    ops.raise_for_status(path.status, "timed steps")
     ms_step = ms_total / args.steps
     tok_s = world * args.batch * args.steps / (ms_total / 1e3)
     us_layer = ms_step * 1e3 / args.layers
@@ -411,6 +488,11 @@ def main():
         log("end-to-end (host buffers)")
         e2e = measure_e2e(args, path, inputs, outs, dev, world)
 
+    seq_split = None
+    if args.workload == "cfg2" and not args.no_seq_split:
+        log("config-3 sequence split record")
+        seq_split = seq_split_record(args, rank, world, dev)
+
     line = None
     if rank == 0:
         line = {
@@ -433,7 +515,9 @@ def main():
         }
         if e2e is not None:
             line["e2e"] = e2e
-    if rank == 0 and not args.no_cpu:
+        if seq_split is not None:
+            line["seq_split"] = seq_split
+    if rank == 0 and world == 1 and not args.no_cpu:
         log("CPU baseline sample")
         line["cpu_baseline"] = cpu_baseline_sample(args)
     if world > 1:
@@ -445,24 +529,19 @@ def main():
         print(json.dumps(line), flush=True)
 
 
-def run_cfg3(args, rank, world, dev):
-    """Config 3: batch 1, one context of args.ctx tokens (args.ctx / 4
-    compressed entries), compressed KV and indexer keys split contiguously
-    over the ranks; per layer two all-gathers (candidates, partials) over
-    NCCL.  All 43 layers with their own shards; one step = one decode step
-    of all layers.  "scaling": "strong" (the context is fixed as N grows)."""
+def cfg3_build(args, rank, world, dev, p2p: bool):
+    """One long context (args.ctx tokens, args.ctx / 4 compressed entries),
+    its compressed KV and indexer keys split contiguously over ``world``
+    ranks; returns (shard, path, inputs, outs, comm)."""
     import torch
-    import torch.distributed as dist
     from dsv4attn.dist import P2PComm, SeqShard, SeqSplitPath, TorchDistComm
     from dsv4attn.layer import LayerInputs
     from dsv4attn.tables import PathArgs
     pa = PathArgs(index_topk=args.topk)
     T_total = args.ctx // 4
     max_seq = args.ctx + 4096
-    log(f"cfg3: building {args.layers} sharded layers (T={T_total}, rank {rank}/{world})")
-    p2p = world > 1 and args.comm == "p2p"
     shard = SeqShard(pa, 1, T_total, rank, world, dev, k=args.topk, n_layers=args.layers, max_seq_len=max_seq,
-                     peer_exchange=p2p)
+                     peer_exchange=p2p and world > 1)
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     for L in shard.layers:
         L.kv.normal_(generator=g)
@@ -481,7 +560,17 @@ def run_cfg3(args, rank, world, dev):
         inputs.append(x)
     outs = [torch.empty(1, 64, 512, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
     comm = (P2PComm(shard) if p2p else TorchDistComm()) if world > 1 else None
-    path = SeqSplitPath(shard, comm)
+    return shard, SeqSplitPath(shard, comm), inputs, outs, comm
+
+
+def cfg3_measure(args, rank, world, dev, p2p: bool = True, sample_clocks: bool = True):
+    """Time config 3 (sequence split over ``world`` ranks; every rank of the
+    default process group takes part when world > 1) as a CUDA graph of all
+    layers; returns {ms_step, us_per_layer, tok_s, timing, clocks}."""
+    import torch
+    import torch.distributed as dist
+    from dsv4attn import ops
+    shard, path, inputs, outs, comm = cfg3_build(args, rank, world, dev, p2p)
     shard.set_positions(args.ctx - 1)
     torch.cuda.synchronize()
     path.step(inputs, outs)                    # eager warm-up (also sizes the workspace)
@@ -498,7 +587,7 @@ def run_cfg3(args, rank, world, dev):
         with torch.cuda.graph(graph):
             path.step(inputs, outs)
     except Exception as e:                     # capture of the collectives refused: time eagerly
-        log(f"graph capture failed ({type(e).__name__}: {e}); timing eagerly")
+        log(f"cfg3 graph capture failed ({type(e).__name__}: {e}); timing eagerly")
         graph, mode = None, "eager"
         torch.cuda.synchronize()
     shard.set_positions(args.ctx - 1)
@@ -515,9 +604,10 @@ def run_cfg3(args, rank, world, dev):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(int(str(dev).split(":")[-1]))
-    clocks.start()
-    time.sleep(0.3)
+    clocks = ClockSampler(int(str(dev).split(":")[-1])) if sample_clocks else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -529,27 +619,52 @@ def run_cfg3(args, rank, world, dev):
     e1.record(st)
     torch.cuda.synchronize()
     ms_total = e0.elapsed_time(e1)
-    clk = clocks.stop()
+    clk = clocks.stop() if clocks else None
     if world > 1:
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
-    if int(shard.status.item()) != 0:
-        raise RuntimeError(f"device status {int(shard.status.item())} during the cfg3 bench")
+    ops.raise_for_status(shard.status, "cfg3 steps")
     ms_step = ms_total / args.steps
-    us_layer = ms_step * 1e3 / args.layers
-    # algorithmic bytes per layer-step of the whole job: all keys once, the
-    # selected rows once, q/o, scores written and read once
+    if world > 1:
+        dist.barrier()
+    del graph
+    torch.cuda.synchronize()
+    if comm is not None:
+        if world > 1:
+            dist.barrier()
+        comm.close()
+    return {"ms_step": ms_step, "us_per_layer": ms_step * 1e3 / args.layers, "tok_s": 1e3 / ms_step,
+            "timing": mode, "clocks": clk}
+
+
+def cfg3_cpu_baseline(args, seconds=12.0):
+    """CPU oracle of config 3: one decode step of one layer of the single
+    long context (all compressed entries, no split), scaled to args.layers."""
+    return cpu_baseline_sample(args, seconds=seconds, n_seq=1)
+
+
+def run_cfg3(args, rank, world, dev):
+    """Config 3: batch 1, one context of args.ctx tokens (args.ctx / 4
+    compressed entries), compressed KV and indexer keys split contiguously
+    over the ranks; per layer two exchanges (candidates, partials) over
+    NVLink peer memory (--comm p2p) or NCCL all-gathers.  All 43 layers with
+    their own shards; one step = one decode step of all layers.  "scaling":
+    "strong" (the context is fixed as N grows)."""
+    import torch.distributed as dist
+    T_total = args.ctx // 4
+    p2p = args.comm == "p2p"
+    log(f"cfg3: building {args.layers} sharded layers (T={T_total}, rank {rank}/{world})")
+    r = cfg3_measure(args, rank, world, dev, p2p=p2p)
     W, k, D, Di = 128, args.topk, 512, 128
-    t_act = T_total
-    per_layer = t_act * Di * 2 + (W + k) * D * 2 + 64 * D * 2 * 2 + 64 * Di * 2 + 2 * t_act * 4
+    per_layer = T_total * Di * 2 + (W + k) * D * 2 + 64 * D * 2 * 2 + 64 * Di * 2 + 2 * T_total * 4
     hbm, hbm_kind = peaks()
-    gbs = per_layer / (us_layer * 1e-6) / 1e9
+    gbs = per_layer / (r["us_per_layer"] * 1e-6) / 1e9
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(1e3 / ms_step, 2), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "us_per_layer": round(us_layer, 2), "higher_is_better": True, "scaling": "strong",
+            "metric": METRIC, "value": round(r["tok_s"], 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_step"], 4),
+            "us_per_layer": round(r["us_per_layer"], 2), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) shards/inputs, indexer weights N(0,0.02))",
             "config": {"workload": f"cfg3 long-context decode: batch 1, ctx {args.ctx} ({T_total} compressed), "
@@ -558,21 +673,54 @@ def run_cfg3(args, rank, world, dev):
                        "parallelism": f"sequence split x{world} ("
                                       + ("peer-memory exchange over NVLink" if p2p else
                                          ("NCCL all-gather" if world > 1 else "no exchange")) + ")",
-                       "timing": mode},
+                       "timing": r["timing"]},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm * world, "unit": "GB/s",
                          "frac": round(gbs / (hbm * world), 4), "traffic": None,
                          "peak_kind": f"{hbm_kind} x {world} GPUs",
                          "algorithmic_bytes_per_layer": per_layer},
-            "clocks": clk,
+            "clocks": r["clocks"],
         }
+        if world == 1 and not args.no_cpu:
+            log("CPU baseline sample")
+            line["cpu_baseline"] = cfg3_cpu_baseline(args)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
-        del graph
-        torch.cuda.synchronize()
-        dist.barrier()
-        comm.close()
         dist.destroy_process_group()
+
+
+def seq_split_record(args, rank, world, dev):
+    """Config 3 beside the default run (the sequence split the scaling target
+    is set on): the N-way split over every rank, and on rank 0 alone the
+    1-GPU step it is compared with.  Returns the sub-object for rank 0's line
+    (None elsewhere)."""
+    import copy
+    import torch
+    import torch.distributed as dist
+    a3 = copy.copy(args)
+    a3.ctx, a3.topk, a3.layers = 262144, 2048, args.layers
+    a3.steps, a3.warmup = max(10, args.steps), max(3, args.warmup)
+    one = None
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        one = cfg3_measure(a3, 0, 1, dev, p2p=False, sample_clocks=False)
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        split = cfg3_measure(a3, rank, world, dev, p2p=True, sample_clocks=False)
+        torch.cuda.empty_cache()
+    else:
+        split = one
+    if rank != 0:
+        return None
+    return {"workload": f"cfg3 long-context decode: batch 1, ctx {a3.ctx} ({a3.ctx // 4} compressed), "
+                        f"top-{a3.topk} + window 128, {a3.layers} layers, sequence split",
+            "n_gpus": world, "us_per_layer": round(split["us_per_layer"], 2), "tok_s": round(split["tok_s"], 2),
+            "us_per_layer_1gpu": round(one["us_per_layer"], 2), "tok_s_1gpu": round(one["tok_s"], 2),
+            "efficiency": round(one["ms_step"] / (world * split["ms_step"]), 4),
+            "exchange": "peer-memory stores over NVLink" if world > 1 else "none",
+            "scaling": "strong", "timing": split["timing"]}
 
 
 def run_cfg1(args, rank, world, dev):
@@ -637,7 +785,8 @@ def run_cfg1(args, rank, world, dev):
             "config": {"workload": f"cfg1 compressor emit path: batch {B}, d {d}, ratio {r}, [32,4,512] state, "
                                    f"{steps} steps, emit every 4th ({n_emit} emitted rows per sequence)",
                        "global_batch": B, "parallelism": "replicas"},
-            "note": "one compressor launch + one position advance per step, graph-replayed; launch-bound"}),
+            "note": "one compressor launch + one position advance per step, graph-replayed; launch-bound",
+            **({"cpu_baseline": cpu_baseline_cfg1()} if world == 1 and not args.no_cpu else {})}),
             flush=True)
 
 
@@ -728,8 +877,7 @@ def run_cfg4(args, rank, world, dev):
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
-    if int(ch.status.item()) != 0:
-        raise RuntimeError(f"device status {int(ch.status.item())} during the cfg4 bench")
+    ops.raise_for_status(ch.status, "cfg4 chunk")
     ms_chunk = ms_total / args.steps
     fl = ch.flops(T)
     pk = None
@@ -757,6 +905,9 @@ def run_cfg4(args, rank, world, dev):
                          "flops": fl, "kernels_ms": {k: round(v, 3) for k, v in kt.items()}},
             "clocks": clk,
         }
+        if world == 1 and not args.no_cpu:
+            log("CPU baseline sample")
+            line["cpu_baseline"] = cpu_baseline_cfg4()
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

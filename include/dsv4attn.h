@@ -41,6 +41,18 @@ enum {
 int dsa_version(void);
 const char* dsa_last_error(void);
 
+/* Spin budget of every bounded device-side wait in this library (mbarrier
+ * waits of the attention and indexer kernels, grid barriers of the wide
+ * top-k, peer flags of dsa_p2p_wait), in SM clock cycles; cycles <= 0
+ * restores the default of 2e9 (about one second).  A wait that runs out
+ * sets bit 2 of the call's status word (where it has one) and the kernel
+ * ends instead of hanging, so the context stays usable.  Read at each launch
+ * (host-side, process-wide); kernels already captured in a CUDA graph keep
+ * the value of their capture.  No counterpart in the reference (its device
+ * waits are inside ttnn). */
+int dsa_set_wait_limit(long long cycles);
+long long dsa_get_wait_limit(void);
+
 /* ---------------------------------------------------------------- attn.kv */
 
 /* Block-wise max-abs FP8-E4M3 round trip of an [M, N] bf16 matrix along N.
@@ -292,8 +304,9 @@ int dsa_shard_local_indices(const int32_t* sel, int64_t ld_sel, int k, const int
  *   local), then release-store *epoch into the G flags flag_ptrs[g] once all
  *   of that destination's stores are visible system-wide.  done: G local
  *   zero-initialised counters (left zeroed).
- * dsa_p2p_wait: wait (acquire, bounded ~1 s; a timeout sets status bit 2)
- *   until flags[i] >= *epoch for all i < G.
+ * dsa_p2p_wait: wait (acquire, bounded by the wait limit below; a timeout
+ *   sets status bit 2 and the kernel returns) until flags[i] >= *epoch for
+ *   all i < G.
  * dsa_counter_bump: *counter += 1 on the device (the per-step epoch).
  * Replaces the ttnn.all_gather / all_reduce collectives the reference's
  * multi-device path issues (inference.py:5274-5275) for the split of
@@ -358,11 +371,17 @@ int dsa_sparse_attn(const void* q, const void* kv, int64_t kv_bstride, int64_t k
  * library reserves in device memory on every GPU that loads it and keeps
  * until the process exits.  Shapes whose partials need more than 8 MiB
  * (dsa_sparse_attn_workspace_size() > 8 MiB) are rejected with
- * DSA_ERR_WORKSPACE.  The first call on a device looks up the array's
- * device address; make that first call before any stream capture.  All
- * calls share the one array, so calls that overlap on the GPU (other
- * streams, other host threads) race on it.  This entry point has no
- * counterpart in the reference. */
+ * DSA_ERR_WORKSPACE.  The partials take nsplit * B * S * 64 * 514 * 4
+ * bytes, so about 63 (query row, key split) pairs fit: a few decode rows
+ * or one long context do, config 2's 64-sequence decode (2 splits per row,
+ * 16.8 MB) does not and must use dsa_sparse_attn with a workspace.  The
+ * first call on a device looks up the array's device address and caches it
+ * for the life of the process; make that first call before any stream
+ * capture, and do not use this entry point across a device reset
+ * (cudaDeviceReset) or a destroyed and recreated primary context, which
+ * would leave the cached address stale.  All calls share the one array, so
+ * calls that overlap on the GPU (other streams, other host threads) race on
+ * it.  This entry point has no counterpart in the reference. */
 int dsa_sparse_attn_noalloc(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,
                             const int32_t* idx, int64_t ld_idx, const float* sink, void* out,
                             float* lse, int B, int S, int H, int D, int K, float scale,

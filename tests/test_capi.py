@@ -77,6 +77,17 @@ def test_host_validation_rejects_bad_shapes_without_launch():
     assert "flags" in _lib.last_error()
 
 
+def test_attention_rejects_row_count_overflow():
+    from dsv4attn import _lib
+    L = _lib.lib()
+    B, S = 1 << 20, 1 << 12                      # B * S * 64 overflows a 32-bit row index
+    assert L.dsa_sparse_attn_workspace_size(B, S, 64, 512, 2176) == 0
+    rc = L.dsa_sparse_attn(16, 16, 512, 1, 16, 2176, 16, 16, None, B, S, 64, 512, 2176, 1.0, None, 0, None, None)
+    assert rc == _lib.DSA_ERR_ARG and "too many" in _lib.last_error()
+    rc = L.dsa_sparse_attn_noalloc(16, 16, 512, 1, 16, 2176, 16, 16, None, B, S, 64, 512, 2176, 1.0, None, None)
+    assert rc == _lib.DSA_ERR_ARG and "too many" in _lib.last_error()
+
+
 def test_workspace_queries_are_pure_host():
     from dsv4attn import _lib
     L = _lib.lib()

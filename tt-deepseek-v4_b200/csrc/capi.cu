@@ -3,6 +3,7 @@
 
 #include "common.cuh"
 #include "tma.cuh"
+#include <atomic>
 #include <mutex>
 
 namespace dsa {
@@ -17,6 +18,10 @@ void set_error(const char* fmt, ...) {
 }
 
 void clear_error() { g_err[0] = 0; }
+
+static std::atomic<long long> g_wait_limit{2000000000ll};
+
+long long wait_limit_cycles() { return g_wait_limit.load(std::memory_order_relaxed); }
 
 int num_sms() {
   static int cached[64] = {0};
@@ -65,3 +70,11 @@ bool make_2d_bf16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
 extern "C" int dsa_version(void) { return 100; }  // 0.1.0
 
 extern "C" const char* dsa_last_error(void) { return dsa::g_err; }
+
+extern "C" int dsa_set_wait_limit(long long cycles) {
+  dsa::clear_error();
+  dsa::g_wait_limit.store(cycles > 0 ? cycles : 2000000000ll, std::memory_order_relaxed);
+  return DSA_OK;
+}
+
+extern "C" long long dsa_get_wait_limit(void) { return dsa::wait_limit_cycles(); }

@@ -41,6 +41,12 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 
 int num_sms();  // cached per device
 
+// Spin budget, in SM clock cycles, of every bounded device-side wait the
+// library's kernels take (mbarrier waits, grid barriers, peer flags); set
+// with dsa_set_wait_limit, about one second by default.  Passed to each
+// kernel as an argument at launch.
+long long wait_limit_cycles();
+
 // ----------------------------------------------------------- conversions
 __device__ __forceinline__ float bf2f(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float x) { return __float2bfloat16_rn(x); }

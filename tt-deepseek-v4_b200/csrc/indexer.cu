@@ -59,6 +59,7 @@ static int indexer_score_run(const void* q, const void* k, const float* w, float
       return DSA_ERR_CUDA;
     }
     idxpf::Args a{};
+    a.wait_limit = wait_limit_cycles();
     a.w = w;
     a.score = score;
     a.t_valid = t_valid;
@@ -84,6 +85,7 @@ static int indexer_score_run(const void* q, const void* k, const float* w, float
       return DSA_ERR_CUDA;
     }
     idxtc::Args a{};
+    a.wait_limit = wait_limit_cycles();
     a.w = w;
     a.score = score;
     a.t_valid = t_valid;

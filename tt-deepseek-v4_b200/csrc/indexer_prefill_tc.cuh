@@ -61,6 +61,7 @@ struct Args {
   float* score;           // [S, ld_score]
   const int32_t* t_valid; // [S] or null
   int32_t* status;
+  long long wait_limit;   // spin budget of every bounded wait, SM cycles
   int S, T, tiles, items_per_cta;
   int64_t ld_score;
 };
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_prefill_tc_kernel(const Ar
       for (; next_live(item, g, t0, lim, cur_g); ++item) {
         if (g != qg) {
           // q of a new group: the previous group's MMAs must have finished
-          if (gi > 0) tc::mbar_wait(smem_u32(&aux->q_empty), (gi - 1) & 1, a.status, 2);
+          if (gi > 0) tc::mbar_wait(smem_u32(&aux->q_empty), (gi - 1) & 1, a.status, 2, a.wait_limit);
           const uint32_t qb = smem_u32(&aux->q_full);
           tma::mbar_arrive_expect_tx(qb, kQBytes);
           tma::load_2d(sbase + kOffQ, &tm_q, 0, g * N, qb);
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_prefill_tc_kernel(const Ar
           ++gi;
         }
         const int s = it % NS;
-        if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2);
+        if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2, a.wait_limit);
         const uint32_t st = sbase + s * kKeyBytes;
         const uint32_t fb = smem_u32(&aux->full[s]);
         tma::mbar_arrive_expect_tx(fb, kKeyBytes);
@@ -162,13 +163,13 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_prefill_tc_kernel(const Ar
       for (; next_live(item, g, t0, lim, cur_g); ++item) {
         if (g != qg) {
           if (gi > 0) tc::mma_commit(smem_u32(&aux->q_empty));  // after every MMA of the previous group
-          tc::mbar_wait(smem_u32(&aux->q_full), gi & 1, a.status, 2);
+          tc::mbar_wait(smem_u32(&aux->q_full), gi & 1, a.status, 2, a.wait_limit);
           qg = g;
           ++gi;
         }
         const int s = it % NS, acc = it & 1;
-        tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2);
-        if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2);
+        tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2, a.wait_limit);
+        if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2, a.wait_limit);
         tc::fence_after_sync();
         const uint32_t st = sbase + s * kKeyBytes;
 #pragma unroll
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_prefill_tc_kernel(const Ar
       }
       // drain: every MMA has completed before TMEM is released
       tc::mma_commit(smem_u32(&aux->w_full));
-      tc::mbar_wait(smem_u32(&aux->w_full), 0, a.status, 2);
+      tc::mbar_wait(smem_u32(&aux->w_full), 0, a.status, 2, a.wait_limit);
     }
     __syncwarp();
   } else {
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_prefill_tc_kernel(const Ar
         qg = g;
       }
       const int acc = it & 1;
-      tc::mbar_wait(smem_u32(&aux->acc_full[acc]), (it >> 1) & 1, a.status, 2);
+      tc::mbar_wait(smem_u32(&aux->acc_full[acc]), (it >> 1) & 1, a.status, 2, a.wait_limit);
       tc::fence_after_sync();
       const int t = t0 + quarter * 32 + lane;
 #pragma unroll 1

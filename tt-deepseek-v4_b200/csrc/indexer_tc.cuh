@@ -56,6 +56,7 @@ struct Args {
   float* score;
   const int32_t* t_valid;
   int32_t* status;
+  long long wait_limit;   // spin budget of every bounded wait, SM cycles
   int B, T, tiles_per_seq, items_per_cta;
   int balanced;           // B <= kMaxSeqBalanced: split the live tiles evenly (items_per_cta unused)
   // The key cache and t_valid were complete before the previous kernel on
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
       int b, t0, t_lim;
       while (walk.next(b, t0, t_lim)) {
         const int s = it % NS;
-        if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2);
+        if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2, a.wait_limit);
         const uint32_t st = sbase + s * kStageBytes;
         const uint32_t fb = smem_u32(&aux->full[s]);
         tma::mbar_arrive_expect_tx(fb, kStageBytes);
@@ -248,8 +249,8 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
       int b, t0, t_lim;
       while (walk.next(b, t0, t_lim)) {
         const int s = it % NS, acc = it & 1;
-        tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2);
-        if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2);
+        tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2, a.wait_limit);
+        if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2, a.wait_limit);
         tc::fence_after_sync();
         const uint32_t st = sbase + s * kStageBytes;
 #pragma unroll
@@ -281,7 +282,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
         for (int h = 0; h < H; ++h) wv[h] = __ldg(a.w + int64_t(b) * H + h);
         cur_b = b;
       }
-      tc::mbar_wait(smem_u32(&aux->acc_full[acc]), (it >> 1) & 1, a.status, 2);
+      tc::mbar_wait(smem_u32(&aux->acc_full[acc]), (it >> 1) & 1, a.status, 2, a.wait_limit);
       tc::fence_after_sync();
       float v0[32], v1[32];
       tc::tmem_ld32(trow + 64 * acc, v0);

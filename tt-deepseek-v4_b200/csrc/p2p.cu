@@ -28,7 +28,6 @@ namespace p2p {
 
 constexpr int kThreads = 512;
 constexpr size_t kChunk = 32 * 1024;       // bytes one CTA stores to one destination
-constexpr long long kSpinCycles = 2000000000ll;  // ~1 s
 constexpr int kStatusTimeout = 2;
 
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
@@ -66,13 +65,13 @@ __global__ void __launch_bounds__(kThreads) publish_kernel(const uint4* __restri
 
 // One warp: lane i < G waits until flags[i] >= epoch.
 __global__ void wait_kernel(const uint32_t* __restrict__ flags, int G, const uint32_t* __restrict__ epoch,
-                            int32_t* __restrict__ status) {
+                            int32_t* __restrict__ status, long long spin) {
   const int i = threadIdx.x;
   const uint32_t e = *epoch;
   if (i < G) {
     const long long t0 = clock64();
     while (ld_acquire_sys_u32(flags + i) < e) {
-      if (clock64() - t0 > kSpinCycles) {
+      if (clock64() - t0 > spin) {
         if (status) atomicOr(status, kStatusTimeout);
         break;
       }
@@ -202,7 +201,8 @@ extern "C" int dsa_p2p_wait(const uint32_t* flags, int G, const uint32_t* epoch,
                             dsa_stream_t stream) {
   clear_error();
   DSA_CHECK_ARG(flags && epoch && G > 0 && G <= 32, "p2p_wait: bad arguments");
-  p2p::wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, G, epoch, status);
+  p2p::wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, G, epoch, status,
+                                                                         wait_limit_cycles());
   DSA_CHECK_LAUNCH("p2p_wait");
   return DSA_OK;
 }

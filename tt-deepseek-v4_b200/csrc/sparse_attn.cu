@@ -160,6 +160,8 @@ static int check_common(const void* q, const void* kv, int64_t kv_bstride, int64
   DSA_CHECK_ARG(q && kv && idx, "sparse_attn: null q/kv/idx");
   DSA_CHECK_ARG(H == kSaH && D == kSaD, "sparse_attn: built for H=64, D=512 (got H=%d D=%d)", H, D);
   DSA_CHECK_ARG(B >= 0 && S >= 1 && K >= 0 && kv_rows > 0, "sparse_attn: bad B/S/K/kv_rows");
+  DSA_CHECK_ARG(int64_t(B) * S <= INT32_MAX / kSaH, "sparse_attn: B*S = %lld query rows is too many",
+                (long long)B * S);
   DSA_CHECK_ARG(kv_bstride >= kv_rows * D && kv_bstride % 8 == 0, "sparse_attn: bad kv batch stride");
   DSA_CHECK_ARG(ld_idx >= K, "sparse_attn: ld_idx < K");
   DSA_CHECK_ARG(aligned(q, 16) && aligned(kv, 16), "sparse_attn: q/kv must be 16-byte aligned");
@@ -173,6 +175,8 @@ using namespace dsa;
 extern "C" size_t dsa_sparse_attn_workspace_size(int B, int S, int H, int D, int K) {
   (void)H;
   (void)D;
+  // shapes the attention rejects (B*S beyond its row limit) need no workspace
+  if (B < 0 || S < 1 || int64_t(B) * S > INT32_MAX / kSaH) return 0;
   const int M = B * S;
   return ws_bytes_for(plan_splits(M, K), M);
 }
@@ -204,6 +208,7 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   t.K = K;
   t.tiles_per_split = p.tiles_per_split;
   t.scale_log2 = scale * kLog2e;
+  t.wait_limit = wait_limit_cycles();
   t.trace = g_trace;
   float* ws_ml = nullptr;
   float* ws_o = nullptr;
@@ -356,6 +361,8 @@ extern "C" int dsa_sparse_attn_noalloc(const void* q, const void* kv, int64_t kv
   clear_error();
   DSA_CHECK_ARG(sink && out, "sparse_attn_noalloc: null sink/out");
   DSA_CHECK_ARG(B >= 0 && S >= 1 && K >= 0, "sparse_attn_noalloc: bad B/S/K");
+  DSA_CHECK_ARG(int64_t(B) * S <= INT32_MAX / kSaH, "sparse_attn_noalloc: B*S = %lld query rows is too many",
+                (long long)B * S);
   const size_t need = dsa_sparse_attn_workspace_size(B, S, H, D, K);
   if (need > kNoAllocScratchBytes) {
     set_error("sparse_attn_noalloc: this shape needs %zu bytes of scratch, above the built-in maximum of %zu "

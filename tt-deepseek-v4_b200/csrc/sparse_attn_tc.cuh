@@ -125,6 +125,7 @@ struct Args {
   int S, M, K, tiles_per_split;
   float scale_log2;
   int final_mode;
+  long long wait_limit;  // spin budget of every bounded wait, SM cycles
   long long* trace;  // optional: per-tile clock64 stamps of CTA (0, 0), see kTr*
 };
 
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
 
   auto wait = [&](const uint64_t* bar, uint32_t parity) {
     if (*abort_flag) return;
-    if (!tc::mbar_wait(smem_u32(bar), parity, a.status, kStatusTimeout)) *abort_flag = 1;
+    if (!tc::mbar_wait(smem_u32(bar), parity, a.status, kStatusTimeout, a.wait_limit)) *abort_flag = 1;
   };
   // whole-warp wait with one polling lane
   auto warp_wait = [&](const uint64_t* bar, uint32_t parity) {
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         }
         if (did) {
           last = clock64();
-        } else if (*abort_flag || clock64() - last > tc::kWaitCycles) {
+        } else if (*abort_flag || clock64() - last > a.wait_limit) {
           if (!*abort_flag && a.status) atomicOr(a.status, kStatusTimeout);
           *abort_flag = 1;
           break;
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       }
       // every MMA of this CTA has completed before TMEM is released
       tc::mma_commit(smem_u32(&aux->mma_done));
-      tc::mbar_wait(smem_u32(&aux->mma_done), 0, a.status, kStatusTimeout);
+      tc::mbar_wait(smem_u32(&aux->mma_done), 0, a.status, kStatusTimeout, a.wait_limit);
     }
     __syncwarp();
   } else if (warp < 4) {

@@ -1,5 +1,5 @@
 // TMA (cp.async.bulk.tensor) helpers for sm_100a: tensor-map encoding on the
-// host and 2-D tile / 4-row gather loads that complete on an mbarrier.
+// host and 2-D tile loads that complete on an mbarrier.
 // Every load here reads this GPU's own memory into its own CTA only.
 #pragma once
 
@@ -32,25 +32,6 @@ __device__ __forceinline__ void load_2d(uint32_t dst, const CUtensorMap* map, in
           dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
-}
-
-// four rows r0..r3, columns [x, x + box_cols): 4 x box_cols elements into dst
-__device__ __forceinline__ void gather4(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t r0, int32_t r1,
-                                        int32_t r2, int32_t r3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-      "%4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
-      : "memory");
-}
-
-// L2 prefetch of four rows (no shared-memory destination, no completion)
-__device__ __forceinline__ void prefetch_gather4(const CUtensorMap* map, int32_t x, int32_t r0, int32_t r1, int32_t r2,
-                                                 int32_t r3) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile::gather4 [%0, {%1, %2, %3, %4, %5}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {

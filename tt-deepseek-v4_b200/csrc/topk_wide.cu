@@ -38,7 +38,6 @@ constexpr int kThreads = 512;
 constexpr int kBins = 4096;
 constexpr int kLevels = 3;
 constexpr int kMaxPerThread = 8;
-constexpr long long kSpinCycles = 2000000000ll;  // ~1 s at 1.9 GHz
 constexpr int kStatusTimeout = 2;
 constexpr int kCap = 24;                 // level-0 bin keys one CTA may publish
 constexpr int kMaxCtasPerRow = 148;
@@ -67,7 +66,7 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
 // release semantics after the CTA's __syncthreads, which orders the whole
 // CTA's prior writes; waiters poll the generation with acquire loads.
 // False on timeout.
-__device__ bool grid_barrier(uint32_t* bar, unsigned nctas, int32_t* status, volatile int* s_ok) {
+__device__ bool grid_barrier(uint32_t* bar, unsigned nctas, int32_t* status, volatile int* s_ok, long long spin) {
   uint32_t* count = bar;
   uint32_t* gen = bar + 1;
   __syncthreads();
@@ -83,7 +82,7 @@ __device__ bool grid_barrier(uint32_t* bar, unsigned nctas, int32_t* status, vol
       int polls = 0;
       while (ld_acquire_u32(gen) == g) {
         if (++polls > 256) __nanosleep(32);
-        if (clock64() - t0 > kSpinCycles) {
+        if (clock64() - t0 > spin) {
           ok = 0;
           if (status) atomicOr(status, kStatusTimeout);
           break;
@@ -168,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
     const int32_t* __restrict__ t_active, int T, int k, int win, int mask_mode, int per_cta, int seg_len,
     int64_t seg_stride,
     int32_t* __restrict__ out_idx, float* __restrict__ out_score, int64_t ld_out, RowWs* __restrict__ rows,
-    uint32_t* __restrict__ counts, unsigned long long* __restrict__ cands, int32_t* __restrict__ status) {
+    uint32_t* __restrict__ counts, unsigned long long* __restrict__ cands, int32_t* __restrict__ status,
+    long long spin) {
   __shared__ uint32_t s_hist[kBins];
   __shared__ unsigned long long s_cand[kCandSmem];
   __shared__ uint32_t s_w[33];
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
   __syncthreads();
   for (int i = tid; i < kBins; i += kThreads)
     if (s_hist[i]) atomicAdd(&rw->hist[0][i], s_hist[i]);
-  if (!grid_barrier(bar, nctas, status, &s_ok)) return;
+  if (!grid_barrier(bar, nctas, status, &s_ok, spin)) return;
   uint32_t above;
   const uint32_t d0 = find_bin<kBins / kThreads, true>(rw->hist[0], kBins, uint32_t(k), &above, s_w, &s_res,
                                                        &s_above);
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
       }
     }
   }
-  if (!grid_barrier(bar, nctas, status, &s_ok)) return;
+  if (!grid_barrier(bar, nctas, status, &s_ok, spin)) return;
   // level-0 histogram: every CTA read it before the barrier above
   for (int i = c * kThreads + tid; i < kBins; i += cpr * kThreads) rw->hist[0][i] = 0u;
 
@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
     __syncthreads();
     for (int i = tid; i < kBins; i += kThreads)
       if (s_hist[i]) atomicAdd(&rw->hist[level][i], s_hist[i]);
-    if (!grid_barrier(bar, nctas, status, &s_ok)) return;
+    if (!grid_barrier(bar, nctas, status, &s_ok, spin)) return;
     uint32_t ab;
     const uint32_t dd = find_bin<kBins / kThreads, true>(rw->hist[level], kBins, need, &ab, s_w, &s_res, &s_above);
     need -= ab;
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_wide_kernel(
     crow[kCountWords * c + 2] = cg2;
     crow[kCountWords * c + 3] = cq2;
   }
-  if (!grid_barrier(bar, nctas, status, &s_ok)) return;
+  if (!grid_barrier(bar, nctas, status, &s_ok, spin)) return;
   for (int i = c * kThreads + tid; i < (kLevels - 1) * kBins; i += cpr * kThreads) (&rw->hist[1][0])[i] = 0u;
   uint32_t pg = 0, pq = 0;
   if (tid < c) {
@@ -508,7 +508,7 @@ extern "C" int dsa_topk_wide(const float* score, int64_t ld_score, const int32_t
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, wide::topk_wide_kernel, score, ld_score, ids, ld_ids, t_active, T, k, win,
                                      mask_mode, per_cta, seg_len, seg_stride, out_idx, out_score, ld_out, rows,
-                                     counts, cands, status);
+                                     counts, cands, status, wait_limit_cycles());
   if (e != cudaSuccess) {
     set_error("topk_wide: launch failed: %s", cudaGetErrorString(e));
     return DSA_ERR_CUDA;

@@ -59,6 +59,32 @@ class Workspace:
 
 _default_ws: dict = {}
 
+# bits of the device status words the kernels set (the ``status`` tensors)
+STATUS_BAD_INDEX = 1   # an attention index fell outside the cache (clamped)
+STATUS_TIMEOUT = 2     # a bounded device wait ran out (lost arrival, missing peer)
+
+
+def set_wait_limit(cycles: int) -> int:
+    """Set the spin budget (SM clock cycles) of every bounded device wait
+    of the library (``dsa_set_wait_limit``; <= 0 restores ~1 s); returns
+    the previous budget.  Kernels already captured in a graph keep theirs."""
+    L = lib()
+    prev = int(L.dsa_get_wait_limit())
+    check(L.dsa_set_wait_limit(int(cycles)), "set_wait_limit")
+    return prev
+
+
+def raise_for_status(status: torch.Tensor, what: str) -> None:
+    """Read a device status word (synchronises) and map it to the
+    reference's error types: TimeoutError when a bounded wait ran out,
+    RuntimeError for any other device error."""
+    v = int(status.reshape(-1)[0].item())
+    if v & STATUS_TIMEOUT:
+        raise TimeoutError(f"{what}: a bounded device wait ran out (status {v}); "
+                           "a peer or an arrival never came")
+    if v:
+        raise RuntimeError(f"{what}: device status {v} (bit 1: an index fell outside the cache)")
+
 
 def _ws(device, nbytes: int, ws: Workspace | None) -> Workspace:
     if ws is None:
