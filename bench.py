@@ -914,6 +914,44 @@ def run_cfg4(args, rank, world, dev):
         dist.destroy_process_group()
 
 
+class gpu_local_numa:
+    """While active, the calling thread runs on the CPUs next to ``dev``
+    (NVML's CPU affinity of the GPU, read-only use of NVML), so pinned host
+    buffers allocated meanwhile get their pages on the GPU's own NUMA node
+    (first touch); the previous affinity is restored on exit.  A no-op where
+    NVML or sched_setaffinity is unavailable."""
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.prev = None
+        self.cpus = None
+
+    def __enter__(self):
+        try:
+            import torch
+            import pynvml
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            n = os.cpu_count() or 1
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (n + 63) // 64)
+            cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1 and 64 * i + b < n}
+            pynvml.nvmlShutdown()
+            if cpus:
+                self.prev = os.sched_getaffinity(0)
+                os.sched_setaffinity(0, cpus)
+                self.cpus = cpus
+        except Exception:  # noqa: BLE001 - best effort: no NVML, no affinity API, no permission
+            self.prev = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            os.sched_setaffinity(0, self.prev)
+        return False
+
+
 def measure_e2e(args, path, inputs, outs, dev, world):
     """Same metric through the public API with HOST buffers: every step copies
     all 43 layers' inputs from pinned host memory and reads all outputs back.
@@ -924,12 +962,17 @@ def measure_e2e(args, path, inputs, outs, dev, world):
     import torch
     from dsv4attn.layer import LayerInputs
     B, nl = args.batch, args.layers
-    host_flat, host_in = LayerInputs.packed(path.args, B, nl, pin=True)
+    out_shape = (nl,) + tuple(outs[0].shape)
+    # the pinned buffers live on this GPU's NUMA node (ranks spread over both
+    # sockets' memory instead of all copying through one)
+    with gpu_local_numa(dev) as numa:
+        host_flat, host_in = LayerInputs.packed(path.args, B, nl, pin=True)
+        host_out = torch.empty(out_shape, dtype=outs[0].dtype, pin_memory=True)
+        host_flat.zero_()
+        host_out.zero_()
     for h, x in zip(host_in, inputs):
         for a, b in zip(h.tensors(), x.tensors()):
             a.copy_(b)
-    out_shape = (nl,) + tuple(outs[0].shape)
-    host_out = torch.empty(out_shape, dtype=outs[0].dtype, pin_memory=True)
     sets, graphs = [], []
     saved = path.graph
     for _ in range(2):
@@ -990,6 +1033,8 @@ def measure_e2e(args, path, inputs, outs, dev, world):
         del g
     return {"value": round(world * B * n / (ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": h2d_bytes,
             "d2h_bytes_per_step": d2h_bytes, "steps": n, "ms_per_step": round(ms / n, 4),
+            "host_numa": (f"pinned buffers allocated from the {len(numa.cpus)} CPUs local to the GPU"
+                          if numa.cpus else "no NUMA placement (NVML affinity unavailable)"),
             "note": "pinned host inputs of all 43 layers H2D + all outputs D2H every step, pipelined with compute"}
 
 
