@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-seq-split", action="store_true",
                     help="skip the config-3 sequence-split record that the default (cfg2) run adds")
+    ap.add_argument("--no-projections", action="store_true",
+                    help="skip the record of the projections around the path that the default (cfg2) run adds")
     ap.add_argument("--breakdown", action="store_true", help="print per-kernel timings to stderr")
     ap.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg2",
                     help="cfg0: one layer, batch 1, 4096-token context; cfg1: compressor emit path alone; "
@@ -493,6 +495,11 @@ def main():
         log("config-3 sequence split record")
         seq_split = seq_split_record(args, rank, world, dev)
 
+    projections = None
+    if args.workload == "cfg2" and rank == 0 and not args.no_projections:
+        log("projections record")
+        projections = projections_record(args, dev)
+
     line = None
     if rank == 0:
         line = {
@@ -517,6 +524,8 @@ def main():
             line["e2e"] = e2e
         if seq_split is not None:
             line["seq_split"] = seq_split
+        if projections is not None:
+            line["projections"] = projections
     if rank == 0 and world == 1 and not args.no_cpu:
         log("CPU baseline sample")
         line["cpu_baseline"] = cpu_baseline_sample(args)
@@ -718,9 +727,90 @@ def seq_split_record(args, rank, world, dev):
                         f"top-{a3.topk} + window 128, {a3.layers} layers, sequence split",
             "n_gpus": world, "us_per_layer": round(split["us_per_layer"], 2), "tok_s": round(split["tok_s"], 2),
             "us_per_layer_1gpu": round(one["us_per_layer"], 2), "tok_s_1gpu": round(one["tok_s"], 2),
-            "efficiency": round(one["ms_step"] / (world * split["ms_step"]), 4),
             "exchange": "peer-memory stores over NVLink" if world > 1 else "none",
             "scaling": "strong", "timing": split["timing"]}
+
+
+# the per-layer decode projections at DeepSeek-V4-Flash dims (dim 4096, q_lora
+# 1024, 64 x 512 heads, 8 wo_a groups of o_lora 1024, indexer 64 x 128):
+# (name, output rows over all groups, K per group, groups)
+PROJECTIONS = (("wq_a", 1024, 4096, 1), ("wq_b", 32768, 1024, 1), ("wkv", 512, 4096, 1),
+               ("compressor wkv|wgate", 2048, 4096, 1), ("indexer compressor wkv|wgate", 512, 4096, 1),
+               ("indexer wq_b + q rotary", 8192, 1024, 1), ("weights_proj", 64, 4096, 1),
+               ("wo_a (8 groups)", 8192, 4096, 8), ("wo_b", 4096, 8192, 1))
+
+
+def projections_record(args, dev, reps=20):
+    """The projections either side of the path (the step before it and the
+    one after) through dsa_linear at config-2's batch: per projection the
+    median CUDA-event time with L2 flushed before every launch, weight bytes
+    over that time against the HBM peak, and cuBLAS (torch.matmul / bmm) on
+    the same operands beside it as the library reference point."""
+    import torch
+    from dsv4attn import ops
+    B = args.batch
+    hbm, _ = peaks()
+    g = torch.Generator(device=dev).manual_seed(99)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream()
+
+    def med(fn):
+        # one launch captured in a CUDA graph, so host-side launch work is
+        # not inside the events
+        side = torch.cuda.Stream()
+        side.wait_stream(st)
+        with torch.cuda.stream(side):
+            fn()
+        st.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        ts = []
+        for i in range(reps + 3):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            graph.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+            if i >= 3:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        return sorted(ts)[len(ts) // 2]
+
+    rows, tot, tot_lib, tot_bytes = {}, 0.0, 0.0, 0
+    cos = sin = pos = None
+    for name, NT, K, G in PROJECTIONS:
+        w = (torch.randn(NT, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+        x = torch.randn(B, G * K, device=dev, generator=g).to(torch.bfloat16)
+        y = torch.empty(B, NT, dtype=torch.bfloat16, device=dev)
+        rope = None
+        if "rotary" in name:
+            cos = torch.rand(args.ctx + 8, 32, device=dev)
+            sin = torch.rand(args.ctx + 8, 32, device=dev)
+            pos = torch.full((B,), args.ctx - 1, dtype=torch.int32, device=dev)
+            rope = (cos, sin, pos, 128, 64)
+        wp = ops.pack_linear_weight(w, groups=G)
+        t = med(lambda: ops.linear(x, wp, out=y, rope=rope))
+        if G == 1:
+            t_lib = med(lambda: torch.matmul(x, w.t()))
+        else:
+            wv = w.view(G, NT // G, K).transpose(1, 2)
+            t_lib = med(lambda: torch.bmm(x.view(B, G, K).transpose(0, 1), wv))
+        nbytes = NT * K * 2 + B * G * K * 2 + B * NT * 2
+        rows[name] = {"us": round(t, 2), "gbs": round(nbytes / t / 1e3, 1), "cublas_us": round(t_lib, 2)}
+        tot += t
+        tot_lib += t_lib
+        tot_bytes += nbytes
+        del w, wp, x, y
+    del flush
+    torch.cuda.empty_cache()
+    return {"batch": B, "us_per_layer": round(tot, 2), "cublas_us_per_layer": round(tot_lib, 2),
+            "bytes_per_layer": tot_bytes, "gbs": round(tot_bytes / tot / 1e3, 1),
+            "frac": round(tot_bytes / tot / 1e3 / hbm, 4), "peak": hbm,
+            "timing": "each projection alone, graph-replayed, L2 flushed before every launch, median of "
+                      f"{reps}; bytes = weights + activations in + result out",
+            "kernels": rows}
 
 
 def run_cfg1(args, rank, world, dev):

@@ -53,6 +53,40 @@ const char* dsa_last_error(void);
 int dsa_set_wait_limit(long long cycles);
 long long dsa_get_wait_limit(void);
 
+/* ------------------------------------------------ projections around the path */
+
+/* Y[b, g*N + n] = bf16(sum_k X[b, g*K + k] W[g*N + n, k]) for b < B, n < N,
+ * g < G: the decode-step projections as one weight-streaming tcgen05 kernel.
+ * X [B, ld_x] bf16 (row stride ld_x >= G*K, a multiple of 8, 16-byte
+ * aligned), K a multiple of 64; w_packed = W [G*N, K] in the tile layout of
+ * dsa_linear_pack (16-byte aligned).
+ * Y [B, ld_y]: bf16, or with out_f32 the fp32 value of the bf16 result.
+ * rope_dim > 0: interleaved rotary (pairs 2i, 2i+1) on the last rope_dim
+ * columns of every head_dim block of Y, applied to the bf16 product with
+ * cos/sin [n_pos, rope_dim/2] fp32 at position pos[b] and rounded again;
+ * positions outside [0, n_pos) are clamped and set status bit 1.
+ * Replaces the reference's DeviceColLinear / DeviceRowLinear matmuls at the
+ * path's edges: the fused compressor wkv || wgate (inference.py:4954-4966),
+ * the indexer's wq_b + rotary Lk-D-idx-q kernel and weights_proj
+ * (5177-5185, 5226-5258), wq_a / wq_b / wkv (5934-5960), the head-grouped
+ * wo_a (G groups) and wo_b (6096-6126). */
+int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, void* y, int64_t ld_y, int B, int N, int K,
+               int G, int out_f32, const float* cos, const float* sin, int n_pos, const int32_t* pos,
+               int head_dim, int rope_dim, int32_t* status, dsa_stream_t stream);
+
+/* Bytes of the tile layout of a W [G*N, K] (0 for invalid sizes): G x
+ * ceil(N/128) x K/64 tiles of 16 KB. */
+size_t dsa_linear_packed_bytes(int N, int K, int G);
+
+/* Stores W [G*N, K] bf16 row-major (16-byte aligned) once, at weight-load
+ * time, as the tiles dsa_linear streams: per (group, 128-row tile, 64-wide
+ * k-block) 16 KB holding the 128 rows (zero past N) x 64 k in the 128-byte
+ * swizzled K-major order of the tensor cores' shared-memory operand, tiles in
+ * (group, row tile, k-block) order.  The reference's equivalent is the
+ * conversion of its weights to the device's tiled layout when the
+ * DeviceColLinear modules are built (inference.py:4954-4966, 5934-5953). */
+int dsa_linear_pack(const void* w, int N, int K, int G, void* packed, size_t packed_bytes, dsa_stream_t stream);
+
 /* ---------------------------------------------------------------- attn.kv */
 
 /* Block-wise max-abs FP8-E4M3 round trip of an [M, N] bf16 matrix along N.

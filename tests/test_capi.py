@@ -121,3 +121,15 @@ def test_product_rope_tables_match_reference(golden):
     c, s = rope_cos_sin(PathArgs(), int(rows.max()) + 1, compressed=True)
     np.testing.assert_allclose(c[rows].numpy(), golden["freqs_cmp_cos"], atol=2e-6, rtol=0)
     np.testing.assert_allclose(s[rows].numpy(), golden["freqs_cmp_sin"], atol=2e-6, rtol=0)
+
+
+def test_linear_packed_bytes_is_host_arithmetic():
+    """The tile layout's size is G x ceil(N/128) x K/64 tiles of 16 KB; K not
+    a multiple of 64 (or a non-positive size) gives 0."""
+    from dsv4attn import _lib
+    L = _lib.lib()
+    assert L.dsa_linear_packed_bytes(128, 64, 1) == 16384
+    assert L.dsa_linear_packed_bytes(200, 128, 1) == 2 * 2 * 16384
+    assert L.dsa_linear_packed_bytes(1024, 4096, 8) == 8 * 8 * 64 * 16384
+    assert L.dsa_linear_packed_bytes(64, 96, 1) == 0
+    assert L.dsa_linear_packed_bytes(0, 64, 1) == 0

@@ -28,8 +28,8 @@ CUDA graph (the reference's trace capture, inference.py:7498-7543).
 
 The weight projections around the path (wq_a, wq_b, wkv, the compressor's
 wkv/wgate, weights_proj, wo_a, wo_b) are plain GEMMs and run through
-``DeviceLinear`` (cuBLAS via torch.matmul); everything between them is the
-native library.  Errors follow the reference: ``ValueError`` for shapes,
+``DeviceLinear`` (the library's weight-streaming tcgen05 kernel,
+``dsa_linear``); everything between them is the native library too.  Errors follow the reference: ``ValueError`` for shapes,
 ``RuntimeError`` for unallocated state (inference.py:4394-4397, 4949-4952).
 """
 
@@ -106,7 +106,10 @@ def _freqs_tables(freqs_cis: torch.Tensor, device):
 
 
 class DeviceLinear:
-    """``y = x @ W^T`` on the device (a plain cuBLAS GEMM, outside the path).
+    """``y = x @ W^T`` on the device: the weight-streaming tcgen05 kernel of
+    ``dsa_linear`` (bf16 result; ``out_dtype=F32`` gives the fp32 value of
+    it).  Replaces the reference's DeviceColLinear matmuls
+    (inference.py:4954-4966, 5934-5960, 6126).
 
     ``fused(device, [w_a, w_b])`` concatenates weights along the output dim
     and records ``_fused_*_out`` widths like the reference's fused
@@ -117,8 +120,9 @@ class DeviceLinear:
         w = weight_bf16(weight)
         if scale != 1.0:
             w = (w.float() * scale).to(BF16)
-        self.weight = w.to(self.device).contiguous()
-        self.out_dim, self.in_dim = self.weight.shape
+        self.out_dim, self.in_dim = w.shape
+        # stored once in the tile layout the projection kernel streams
+        self.weight = ops.pack_linear_weight(w.to(self.device).contiguous())
         self.out_dtype = out_dtype
 
     @classmethod
@@ -129,11 +133,16 @@ class DeviceLinear:
             setattr(lin, f"_fused_{n}_out", w.shape[0])
         return lin
 
-    def forward_device(self, x: torch.Tensor) -> torch.Tensor:
+    def forward_device(self, x: torch.Tensor, rope: tuple | None = None, status=None) -> torch.Tensor:
+        """``rope=(cos, sin, pos, head_dim, rope_dim)`` rotates the last
+        rope_dim columns of every head_dim block of the result (the
+        reference's Lk-D-idx-q fusion of wq_b and the q rotary)."""
         if x.shape[-1] != self.in_dim:
             raise ValueError(f"input dim {x.shape[-1]} != weight in_dim {self.in_dim}")
-        y = torch.matmul(x.to(BF16), self.weight.t())
-        return y if self.out_dtype == BF16 else y.to(self.out_dtype)
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.in_dim).to(BF16).contiguous()
+        y = ops.linear(x2, self.weight, out_f32=self.out_dtype != BF16, rope=rope, status=status)
+        return y.reshape(*lead, self.out_dim)
 
     __call__ = forward_device
 
@@ -418,9 +427,10 @@ class DeviceIndexer(torch.nn.Module):
             raise ValueError("DeviceIndexer.forward_device_score requires start_pos_tt "
                              "(no host->device upload inside the trace body).")
         H, Di, rd = self.n_heads, self.head_dim, self.rope_head_dim
-        q = self.wq_b.forward_device(qr_tt).reshape(B, H * Di)
         pos = self.dc._pos_for(start_pos_tt, B)
-        ops.head_norm_rope(q, H, Di, self.cos, self.sin, pos, rope_dim=rd, norm=False, out=q, status=self.status)
+        # wq_b with the q rotary in its epilogue (the Lk-D-idx-q fusion)
+        q = self.wq_b.forward_device(qr_tt.reshape(B, -1), rope=(self.cos, self.sin, pos, Di, rd),
+                                     status=self.status).reshape(B, H * Di)
         self.dc.forward_device(x_tt, B, start_pos, start_pos_tt)
         w = self.weights_proj.forward_device(x_tt).reshape(B, H).float().contiguous()
         cache = self.dc.kv_cache_tt
@@ -484,7 +494,9 @@ class DeviceAttention(torch.nn.Module):
                              f"heads*head_dim {self.n_heads * self.head_dim}")
         self.wo_a_in_per_group = in_per_group
         # [G, in, R] so that o [G, B, in] @ w -> [G, B, R]
-        self.wo_a_w = wo_a.view(self.n_groups, self.o_lora_rank, in_per_group).transpose(1, 2).contiguous().to(dev)
+        # [G*R, in_per_group], tiled for the projection kernel: group g reads
+        # columns [g in_per_group, (g+1) in_per_group) of o
+        self.wo_a_w = ops.pack_linear_weight(wo_a.contiguous().to(dev), groups=self.n_groups)
         kv_shape = tuple(attn.kv_cache.shape)
         if len(kv_shape) != 3:
             raise ValueError(f"expected attn.kv_cache to be 3D [B, kv_cache_size, D], got {kv_shape}")
@@ -631,7 +643,6 @@ class DeviceAttention(torch.nn.Module):
         # output side: inverse rotary, grouped wo_a, wo_b
         ops.head_norm_rope(o, H, D, self.cos, self.sin, pos, rope_dim=rd, norm=False, inverse=True, out=o,
                            status=self.status)
-        og = o.view(B, self.n_groups, self.wo_a_in_per_group).transpose(0, 1)
-        a = torch.bmm(og, self.wo_a_w)  # [G, B, R]
-        a = a.transpose(0, 1).reshape(B, self.n_groups * self.o_lora_rank)
+        # head-grouped wo_a: group g of o (its heads' dims) against its R rows
+        a = ops.linear(o.reshape(B, H * D), self.wo_a_w)
         return self.wo_b(a).view(B, 1, self.dim)

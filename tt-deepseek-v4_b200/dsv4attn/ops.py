@@ -96,6 +96,86 @@ def _ws(device, nbytes: int, ws: Workspace | None) -> Workspace:
     return ws
 
 
+# ------------------------------------------------------- projections
+
+class LinearWeight:
+    """A projection weight W [G*N, K] stored once in the tile layout the
+    kernel streams (dsa_linear_pack): ``packed`` is a uint8 device tensor,
+    ``N`` rows per group, ``K`` inputs per group, ``G`` groups."""
+
+    __slots__ = ("packed", "N", "K", "G")
+
+    def __init__(self, packed: torch.Tensor, N: int, K: int, G: int):
+        self.packed, self.N, self.K, self.G = packed, N, K, G
+
+    @property
+    def device(self):
+        return self.packed.device
+
+    @property
+    def shape(self):
+        return (self.G * self.N, self.K)
+
+
+def pack_linear_weight(w: torch.Tensor, groups: int = 1) -> LinearWeight:
+    """W [G*N, K] bf16 (CUDA, contiguous, K a multiple of 64) -> LinearWeight."""
+    _need(w, "w", BF16)
+    _contig(w, "w")
+    if w.dim() != 2 or w.shape[0] % groups:
+        raise ValueError(f"w {tuple(w.shape)} does not form {groups} groups")
+    N, K = w.shape[0] // groups, w.shape[1]
+    nbytes = lib().dsa_linear_packed_bytes(N, K, groups)
+    if nbytes == 0:
+        raise ValueError(f"w [{w.shape[0]}, {K}]: K must be a multiple of 64")
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+    check(lib().dsa_linear_pack(w.data_ptr(), N, K, groups, packed.data_ptr(), nbytes, _stream(w)), "linear_pack")
+    return LinearWeight(packed, N, K, groups)
+
+
+def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, groups: int = 1,
+           out_f32: bool = False, rope: tuple | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+    """``y[b, g*N + n] = bf16(x[b, g*K:(g+1)*K] . W[g*N + n])`` on the tensor
+    cores (dsa_linear): x [B, G*K] bf16 (row stride a multiple of 8), ``w`` a
+    LinearWeight (its groups win over ``groups``) or W [G*N, K] bf16, which is
+    packed for this call, K a multiple of 64 -> y [B, G*N] bf16, or fp32 of
+    the bf16 value with ``out_f32``.  ``rope=(cos, sin, pos, head_dim,
+    rope_dim)``: interleaved rotary on the last rope_dim columns of every
+    head_dim block, at per-row positions ``pos`` [B] int32."""
+    _need(x, "x", BF16)
+    if not isinstance(w, LinearWeight):
+        w = pack_linear_weight(w, groups)
+    _need(w.packed, "w")
+    groups, N, K = w.G, w.N, w.K
+    GN = groups * N
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be [B, G*K] with contiguous rows")
+    B = x.shape[0]
+    if x.shape[1] != groups * K:
+        raise ValueError(f"x [{B}, {x.shape[1]}] does not match {groups} groups of K={K}")
+    if out is None:
+        out = torch.empty(B, GN, dtype=F32 if out_f32 else BF16, device=x.device)
+    _need(out, "out", F32 if out_f32 else BF16)
+    if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] < B or out.shape[1] < GN:
+        raise ValueError("out must be [B, G*N] with contiguous rows")
+    cos = sin = pos = None
+    n_pos = head_dim = rope_dim = 0
+    if rope is not None:
+        cos, sin, pos, head_dim, rope_dim = rope
+        _need(cos, "cos", F32)
+        _need(sin, "sin", F32)
+        _need(pos, "pos", I32)
+        _contig(pos, "pos")
+        if pos.numel() < B or cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] * 2 != rope_dim:
+            raise ValueError("rope: pos needs one entry per row and cos/sin [n_pos, rope_dim/2]")
+        _contig(cos, "cos")
+        _contig(sin, "sin")
+        n_pos = cos.shape[0]
+    check(lib().dsa_linear(x.data_ptr(), x.stride(0), w.packed.data_ptr(), out.data_ptr(), out.stride(0), B, N, K,
+                           groups, int(out_f32), _ptr(cos), _ptr(sin), n_pos, _ptr(pos), head_dim, rope_dim,
+                           _ptr(status), _stream(x)), "linear")
+    return out
+
+
 # ------------------------------------------------------------------ attn.kv
 
 def act_quant_block(x: torch.Tensor, block: int = 64, fp8_max: float = 448.0, eps: float = 1e-4,
