@@ -56,6 +56,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 
 namespace dsa {
 namespace lin {
@@ -179,48 +180,66 @@ __device__ __forceinline__ void mbar_wait_cluster(uint32_t bar, uint32_t parity,
   }
 }
 
-// bf16 rounding, then the rotary of a rope column (x = this row's value,
-// partner = its pair's, taken by every lane of the warp)
-__device__ __forceinline__ float finish(const Args& a, int bb, int n, bool rope, int kpair, int lane, float v) {
-  float x = bf2f(f2bf(v));  // the matmul's bf16 result
-  if (a.rope_dim > 0) {
-    // every lane takes part in the shuffle; only rope columns use it
-    const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-    if (rope && bb < a.B) {
-      int p = a.pos[bb];
-      if (p < 0 || p >= a.n_pos) {
-        if (a.status && lane == 0) atomicOr(a.status, 1);
-        p = p < 0 ? 0 : a.n_pos - 1;
+// The epilogue runs 4 warps on an SM: its speed is instruction latency, so
+// values are finished and stored CNT at a time with independent chains
+// (one CTA per SM leaves nothing else to hide a serial chain behind).
+//
+// bf16 rounding of CNT token rows' values of this thread's weight row, then
+// (kRope, rope columns) the interleaved rotary: the pair partner is the
+// neighbouring lane's value of the same token row.
+template <bool kRope, int CNT>
+__device__ __forceinline__ void finish_rows(const Args& a, int b0, int n, bool rope, int kpair, int lane, float* v) {
+#pragma unroll
+  for (int i = 0; i < CNT; ++i) v[i] = bf2f(f2bf(v[i]));  // the matmul's bf16 result
+  if constexpr (kRope) {
+    float partner[CNT];
+#pragma unroll
+    for (int i = 0; i < CNT; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
+    if (rope) {
+      const int half = a.rope_dim >> 1;
+      bool bad = false;
+#pragma unroll
+      for (int i = 0; i < CNT; ++i) {
+        int p = a.pos[min(b0 + i, a.B - 1)];
+        if (b0 + i < a.B && (p < 0 || p >= a.n_pos)) bad = true;
+        p = min(max(p, 0), a.n_pos - 1);
+        const float cs = a.cos[int64_t(p) * half + kpair];
+        const float sn = a.sin[int64_t(p) * half + kpair];
+        // pair (a, c) = (even, odd): a cos - c sin, a sin + c cos
+        v[i] = (n & 1) ? __fadd_rn(__fmul_rn(partner[i], sn), __fmul_rn(v[i], cs))
+                       : __fsub_rn(__fmul_rn(v[i], cs), __fmul_rn(partner[i], sn));
       }
-      const float cs = a.cos[int64_t(p) * (a.rope_dim / 2) + kpair];
-      const float sn = a.sin[int64_t(p) * (a.rope_dim / 2) + kpair];
-      // pair (a, c) = (even, odd): a cos - c sin, a sin + c cos
-      x = (n & 1) ? __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(x, cs))
-                  : __fsub_rn(__fmul_rn(x, cs), __fmul_rn(partner, sn));
+      if (bad && a.status) atomicOr(a.status, 1);
     }
   }
-  return x;
 }
 
-// the value of Y[bb, col]: into the staging tile row `srow` (TMA store), or
-// straight to Y
-__device__ __forceinline__ void put(const Args& a, uint8_t* ostage, int srow, int nr, int bb, int64_t col, bool n_ok,
-                                    float x) {
+// CNT finished values of rows [b0, b0 + CNT): into the staging tile rows
+// [srow, srow + CNT) (TMA store), or straight to Y (rows below B only)
+template <bool kF32, int CNT>
+__device__ __forceinline__ void put_rows(const Args& a, uint8_t* ostage, int srow, int nr, int b0, int64_t col,
+                                         bool n_ok, const float* v) {
+  using T = typename std::conditional<kF32, float, __nv_bfloat16>::type;
   if (a.tma_store) {
-    if (a.out_f32) {
-      reinterpret_cast<float*>(ostage)[srow * TILE_N + nr] = bf2f(f2bf(x));
-    } else {
-      reinterpret_cast<__nv_bfloat16*>(ostage)[srow * TILE_N + nr] = f2bf(x);
+    T* o = reinterpret_cast<T*>(ostage) + srow * TILE_N + nr;
+#pragma unroll
+    for (int i = 0; i < CNT; ++i) {
+      if constexpr (kF32) o[i * TILE_N] = bf2f(f2bf(v[i]));
+      else o[i * TILE_N] = f2bf(v[i]);
     }
-  } else if (n_ok && bb < a.B) {
-    if (a.out_f32) {
-      static_cast<float*>(a.y)[int64_t(bb) * a.ld_y + col] = bf2f(f2bf(x));
-    } else {
-      static_cast<__nv_bfloat16*>(a.y)[int64_t(bb) * a.ld_y + col] = f2bf(x);
+  } else if (n_ok) {
+    T* o = static_cast<T*>(a.y) + int64_t(b0) * a.ld_y + col;
+#pragma unroll
+    for (int i = 0; i < CNT; ++i) {
+      if (b0 + i < a.B) {
+        if constexpr (kF32) o[i * a.ld_y] = bf2f(f2bf(v[i]));
+        else o[i * a.ld_y] = f2bf(v[i]);
+      }
     }
   }
 }
 
+template <bool kRope, bool kF32>
 __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
                                                                const __grid_constant__ CUtensorMap tm_x,
                                                                const __grid_constant__ CUtensorMap tm_y) {
@@ -367,9 +386,8 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
           float v[32];
           tc::tmem_ld32(trow + uint32_t(kMaxB) * acc + c0, v);
           tc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            put(a, ostage, c0 + i, nr, c0 + i, col, n_ok, finish(a, c0 + i, n, rope, kpair, lane, v[i]));
+          finish_rows<kRope, 32>(a, c0, n, rope, kpair, lane, v);
+          put_rows<kF32, 32>(a, ostage, c0, nr, c0, col, n_ok, v);
         }
         tc::fence_before_sync();
         __syncwarp();
@@ -389,9 +407,9 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
         float v[32];
         tc::tmem_ld32(trow + uint32_t(kMaxB) * acc + c0, v);
         tc::tmem_wait_ld();
+        float* pr = part + c0 * TILE_N + nr;  // part holds Bp rows: no guard
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c0 + i < a.B) part[(c0 + i) * TILE_N + nr] = v[i];
+        for (int i = 0; i < 32; ++i) pr[i * TILE_N] = v[i];
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -410,10 +428,28 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
         }
       }
       mbar_wait_cluster(smem_u32(&aux->ready), li & 1, a.status, a.wait_limit);
-      for (int bb = b_lo; bb < b_hi; ++bb) {
-        float s = 0.f;
-        for (int q = 0; q < C; ++q) s += recv[(q * R + (bb - b_lo)) * TILE_N + nr];
-        put(a, ostage, bb - b_lo, nr, bb, col, n_ok, finish(a, bb, n, rope, kpair, lane, s));
+      // 8 owned rows at a time, 8 independent sums, C slots in rank order
+      const int nrows = b_hi - b_lo;
+      for (int lb0 = 0; lb0 < nrows; lb0 += 8) {
+        float v[8];
+        const float* rp[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[j] = 0.f;
+          rp[j] = recv + min(lb0 + j, R - 1) * TILE_N + nr;  // rows past the slice: any in-slot row
+        }
+        for (int q = 0; q < C; ++q) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += rp[j][q * R * TILE_N];
+        }
+        finish_rows<kRope, 8>(a, b_lo + lb0, n, rope, kpair, lane, v);
+        if (lb0 + 8 <= nrows) {
+          put_rows<kF32, 8>(a, ostage, lb0, nr, b_lo + lb0, col, n_ok, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (lb0 + j < nrows) put_rows<kF32, 1>(a, ostage, lb0 + j, nr, b_lo + lb0 + j, col, n_ok, v + j);
+        }
       }
       if (a.tma_store) tc::fence_proxy_async();
       tc::named_bar_sync(1, 128);
@@ -475,7 +511,7 @@ int max_clusters(int C) {
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel<false, false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         n = 0;
       }
@@ -556,8 +592,11 @@ extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, voi
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_dev[dev]) {
-    cudaFuncSetAttribute(lin::linear_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lin::kSmemBytes);
-    cudaFuncSetAttribute(lin::linear_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    for (auto k : {lin::linear_tc_kernel<false, false>, lin::linear_tc_kernel<false, true>,
+                   lin::linear_tc_kernel<true, false>, lin::linear_tc_kernel<true, true>}) {
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, lin::kSmemBytes);
+      cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    }
     attr_dev[dev] = 1;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -649,7 +688,9 @@ extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, voi
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = C > 1 ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, lin::linear_tc_kernel, a, tm_x, tm_y);
+    auto kern = rope_dim > 0 ? (out_f32 ? lin::linear_tc_kernel<true, true> : lin::linear_tc_kernel<true, false>)
+                             : (out_f32 ? lin::linear_tc_kernel<false, true> : lin::linear_tc_kernel<false, false>);
+    cudaLaunchKernelEx(&cfg, kern, a, tm_x, tm_y);
     DSA_CHECK_LAUNCH("linear");
   }
   return DSA_OK;
