@@ -740,23 +740,52 @@ PROJECTIONS = (("wq_a", 1024, 4096, 1), ("wq_b", 32768, 1024, 1), ("wkv", 512, 4
                ("wo_a (8 groups)", 8192, 4096, 8), ("wo_b", 4096, 8192, 1))
 
 
-def projections_record(args, dev, reps=20):
+def projections_record(args, dev, reps=10, copies=4):
     """The projections either side of the path (the step before it and the
-    one after) through dsa_linear at config-2's batch: per projection the
-    median CUDA-event time with L2 flushed before every launch, weight bytes
-    over that time against the HBM peak, and cuBLAS (torch.matmul / bmm) on
-    the same operands beside it as the library reference point."""
+    one after) through dsa_linear at config-2's batch.  `copies` layers'
+    worth of projections with their own weights (so nothing is re-read from
+    L2) run back to back from one CUDA graph; the time per layer is the
+    graph's CUDA-event time over `copies`, median of `reps`.  The same chain
+    per projection gives each one's time.  cuBLAS (torch.matmul / bmm) on the
+    same operands, chained the same way, is the library reference point."""
     import torch
     from dsv4attn import ops
     B = args.batch
     hbm, _ = peaks()
     g = torch.Generator(device=dev).manual_seed(99)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream()
+    cos = torch.rand(args.ctx + 8, 32, device=dev, generator=g)
+    sin = torch.rand(args.ctx + 8, 32, device=dev, generator=g)
+    pos = torch.full((B,), args.ctx - 1, dtype=torch.int32, device=dev)
 
-    def med(fn):
-        # one launch captured in a CUDA graph, so host-side launch work is
-        # not inside the events
+    layers = []
+    for _ in range(copies):
+        ents = []
+        for name, NT, K, G in PROJECTIONS:
+            w = (torch.randn(NT, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+            x = torch.randn(B, G * K, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty(B, NT, dtype=torch.bfloat16, device=dev)
+            rope = (cos, sin, pos, 128, 64) if "rotary" in name else None
+            ents.append((name, NT, K, G, w, ops.pack_linear_weight(w, groups=G), x, y, rope))
+        layers.append(ents)
+
+    def native(only=None):
+        for ents in layers:
+            for name, NT, K, G, w, wp, x, y, rope in ents:
+                if only is None or name == only:
+                    ops.linear(x, wp, out=y, rope=rope)
+
+    def cublas(only=None):
+        for ents in layers:
+            for name, NT, K, G, w, wp, x, y, rope in ents:
+                if only is not None and name != only:
+                    continue
+                if G == 1:
+                    torch.matmul(x, w.t(), out=y)
+                else:
+                    torch.bmm(x.view(B, G, K).transpose(0, 1), w.view(G, NT // G, K).transpose(1, 2))
+
+    def per_layer_us(fn):
         side = torch.cuda.Stream()
         side.wait_stream(st)
         with torch.cuda.stream(side):
@@ -766,50 +795,36 @@ def projections_record(args, dev, reps=20):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
         ts = []
-        for i in range(reps + 3):
-            flush.zero_()
+        for _ in range(reps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
             graph.replay()
             e1.record(st)
             torch.cuda.synchronize()
-            if i >= 3:
-                ts.append(e0.elapsed_time(e1) * 1e3)
+            ts.append(e0.elapsed_time(e1) * 1e3 / copies)
+        del graph
         return sorted(ts)[len(ts) // 2]
 
-    rows, tot, tot_lib, tot_bytes = {}, 0.0, 0.0, 0
-    cos = sin = pos = None
+    rows, tot_bytes = {}, 0
     for name, NT, K, G in PROJECTIONS:
-        w = (torch.randn(NT, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
-        x = torch.randn(B, G * K, device=dev, generator=g).to(torch.bfloat16)
-        y = torch.empty(B, NT, dtype=torch.bfloat16, device=dev)
-        rope = None
-        if "rotary" in name:
-            cos = torch.rand(args.ctx + 8, 32, device=dev)
-            sin = torch.rand(args.ctx + 8, 32, device=dev)
-            pos = torch.full((B,), args.ctx - 1, dtype=torch.int32, device=dev)
-            rope = (cos, sin, pos, 128, 64)
-        wp = ops.pack_linear_weight(w, groups=G)
-        t = med(lambda: ops.linear(x, wp, out=y, rope=rope))
-        if G == 1:
-            t_lib = med(lambda: torch.matmul(x, w.t()))
-        else:
-            wv = w.view(G, NT // G, K).transpose(1, 2)
-            t_lib = med(lambda: torch.bmm(x.view(B, G, K).transpose(0, 1), wv))
         nbytes = NT * K * 2 + B * G * K * 2 + B * NT * 2
+        t = per_layer_us(lambda: native(name))
+        t_lib = per_layer_us(lambda: cublas(name))
         rows[name] = {"us": round(t, 2), "gbs": round(nbytes / t / 1e3, 1), "cublas_us": round(t_lib, 2)}
-        tot += t
-        tot_lib += t_lib
         tot_bytes += nbytes
-        del w, wp, x, y
-    del flush
+    tot = per_layer_us(native)
+    tot_lib = per_layer_us(cublas)
+    del layers
     torch.cuda.empty_cache()
     return {"batch": B, "us_per_layer": round(tot, 2), "cublas_us_per_layer": round(tot_lib, 2),
             "bytes_per_layer": tot_bytes, "gbs": round(tot_bytes / tot / 1e3, 1),
             "frac": round(tot_bytes / tot / 1e3 / hbm, 4), "peak": hbm,
-            "timing": "each projection alone, graph-replayed, L2 flushed before every launch, median of "
-                      f"{reps}; bytes = weights + activations in + result out",
+            "timing": f"graph of {copies} layers' projections with their own weights, back to back; "
+                      f"median of {reps}; bytes = weights + activations in + result out",
             "kernels": rows}
 
 

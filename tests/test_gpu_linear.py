@@ -49,7 +49,8 @@ def _check(y, x, w, G):
 @pytest.mark.parametrize("B,N,K,G", [(1, 384, 256, 1), (2, 200, 128, 1), (7, 128, 64, 1), (64, 512, 1024, 1),
                                      (130, 256, 192, 1), (3, 64, 256, 8), (5, 256, 128, 4), (64, 1024, 512, 8),
                                      (1, 64, 4096, 1), (4, 25600, 1024, 1), (16, 1024, 4096, 8), (128, 320, 2048, 1),
-                                     (3, 100, 128, 2), (5, 36, 512, 3), (70, 96, 1024, 2)])
+                                     (3, 100, 128, 2), (5, 36, 512, 3), (70, 96, 1024, 2), (40, 384, 64, 1),
+                                     (72, 256, 64, 1), (128, 512, 4096, 1), (100, 2048, 8192, 1)])
 def test_linear_matches_oracle(cuda_dev, B, N, K, G):
     from dsv4attn import ops
     g = torch.Generator().manual_seed(B * 1000 + N + K + G)
@@ -77,7 +78,7 @@ def test_linear_strided_rows_and_out(cuda_dev):
     assert bool((out[:, 320:].cpu() == 7.0).all())
 
 
-@pytest.mark.parametrize("B,N,K", [(33, 64, 512), (64, 64, 4096), (3, 300, 128)])
+@pytest.mark.parametrize("B,N,K", [(33, 64, 512), (64, 64, 4096), (3, 300, 128), (48, 256, 64), (128, 256, 4096)])
 def test_linear_out_f32_is_the_bf16_value(cuda_dev, B, N, K):
     from dsv4attn import ops
     g = torch.Generator().manual_seed(6)
@@ -107,7 +108,8 @@ def test_linear_unaligned_output_rows(cuda_dev):
     assert bool((out[:, 128:].cpu() == 0).all())
 
 
-@pytest.mark.parametrize("B,H,Dh,rd,K", [(5, 4, 128, 64, 128), (64, 64, 128, 64, 1024), (130, 2, 64, 32, 64)])
+@pytest.mark.parametrize("B,H,Dh,rd,K", [(5, 4, 128, 64, 128), (64, 64, 128, 64, 1024), (130, 2, 64, 32, 64),
+                                         (40, 4, 128, 64, 64), (45, 8, 128, 64, 1024)])
 def test_linear_fused_rotary_bit_exact(cuda_dev, B, H, Dh, rd, K):
     from dsv4attn import ops
     g = torch.Generator().manual_seed(B + H + Dh)

@@ -85,6 +85,8 @@ struct Args {
   uint32_t part_off;         // split > 1: this CTA's partial [Bp][128] fp32
   uint32_t recv_off;         // split > 1: the owned rows' partials [C][R][128] fp32
   uint32_t out_off;          // Y staging [rows][128] (bf16 or fp32)
+  uint32_t rope_off;         // rotary factors (cos, sin) [rope_rows][rope_dim / 2] of the finished rows
+  int rope_rows;
   uint32_t aux_off;
   int out_f32;
   const float* cos;
@@ -138,7 +140,6 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- cluster helpers (distributed shared memory)
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -188,7 +189,7 @@ __device__ __forceinline__ void mbar_wait_cluster(uint32_t bar, uint32_t parity,
 // (kRope, rope columns) the interleaved rotary: the pair partner is the
 // neighbouring lane's value of the same token row.
 template <bool kRope, int CNT>
-__device__ __forceinline__ void finish_rows(const Args& a, int b0, int n, bool rope, int kpair, int lane, float* v) {
+__device__ __forceinline__ void finish_rows(const float2* rtab, int half, int n, bool rope, int kpair, float* v) {
 #pragma unroll
   for (int i = 0; i < CNT; ++i) v[i] = bf2f(f2bf(v[i]));  // the matmul's bf16 result
   if constexpr (kRope) {
@@ -196,22 +197,45 @@ __device__ __forceinline__ void finish_rows(const Args& a, int b0, int n, bool r
 #pragma unroll
     for (int i = 0; i < CNT; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);
     if (rope) {
-      const int half = a.rope_dim >> 1;
-      bool bad = false;
 #pragma unroll
       for (int i = 0; i < CNT; ++i) {
-        int p = a.pos[min(b0 + i, a.B - 1)];
-        if (b0 + i < a.B && (p < 0 || p >= a.n_pos)) bad = true;
-        p = min(max(p, 0), a.n_pos - 1);
-        const float cs = a.cos[int64_t(p) * half + kpair];
-        const float sn = a.sin[int64_t(p) * half + kpair];
+        const float2 f = rtab[i * half + kpair];  // (cos, sin) of token row i at this pair
         // pair (a, c) = (even, odd): a cos - c sin, a sin + c cos
-        v[i] = (n & 1) ? __fadd_rn(__fmul_rn(partner[i], sn), __fmul_rn(v[i], cs))
-                       : __fsub_rn(__fmul_rn(v[i], cs), __fmul_rn(partner[i], sn));
+        v[i] = (n & 1) ? __fadd_rn(__fmul_rn(partner[i], f.y), __fmul_rn(v[i], f.x))
+                       : __fsub_rn(__fmul_rn(v[i], f.x), __fmul_rn(partner[i], f.y));
       }
-      if (bad && a.status) atomicOr(a.status, 1);
     }
   }
+}
+
+// (cos, sin) of every (token row, rotary pair) the CTA finishes, gathered
+// once per launch into shared memory by the epilogue warps while the weight
+// stream runs: rows [b0, b0 + rows); positions outside [0, n_pos) clamped
+// and flagged (status bit 1)
+__device__ __forceinline__ void load_rope_table(const Args& a, float2* rtab, int b0, int rows, int t) {
+  const int half = a.rope_dim >> 1;
+  const int total = rows * half;
+  bool bad = false;
+  for (int i0 = t; i0 < total; i0 += 128 * 8) {
+    int p[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 128;
+      const int b = b0 + (i < total ? i / half : 0);
+      p[u] = a.pos[min(b, a.B - 1)];
+      if (i < total && b < a.B && (p[u] < 0 || p[u] >= a.n_pos)) bad = true;
+      p[u] = min(max(p[u], 0), a.n_pos - 1);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * 128;
+      if (i < total) {
+        const int k = i % half;
+        rtab[i] = make_float2(a.cos[int64_t(p[u]) * half + k], a.sin[int64_t(p[u]) * half + k]);
+      }
+    }
+  }
+  if (bad && a.status) atomicOr(a.status, 1);
 }
 
 // CNT finished values of rows [b0, b0 + CNT): into the staging tile rows
@@ -361,6 +385,13 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
     const int R = a.rows_per;
     const int b_lo = rank * R, b_hi = min(a.B, b_lo + R);
     const bool lead = tid == 64;
+    const float2* rtab = reinterpret_cast<const float2*>(smem + a.rope_off);
+    const int half = a.rope_dim >> 1;
+    if constexpr (kRope) {
+      // the finished rows: all Bp (C = 1) or the owned slice
+      load_rope_table(a, reinterpret_cast<float2*>(smem + a.rope_off), C > 1 ? b_lo : 0, a.rope_rows, tid - 64);
+      tc::named_bar_sync(1, 128);
+    }
     if (lead && a.tma_store) tma::prefetch_map(&tm_y);
     if (C > 1) cluster_wait();
     int li = 0;
@@ -386,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
           float v[32];
           tc::tmem_ld32(trow + uint32_t(kMaxB) * acc + c0, v);
           tc::tmem_wait_ld();
-          finish_rows<kRope, 32>(a, c0, n, rope, kpair, lane, v);
+          finish_rows<kRope, 32>(rtab + c0 * half, half, n, rope, kpair, v);
           put_rows<kF32, 32>(a, ostage, c0, nr, c0, col, n_ok, v);
         }
         tc::fence_before_sync();
@@ -442,7 +473,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[j] += rp[j][q * R * TILE_N];
         }
-        finish_rows<kRope, 8>(a, b_lo + lb0, n, rope, kpair, lane, v);
+        finish_rows<kRope, 8>(rtab + lb0 * half, half, n, rope, kpair, v);
         if (lb0 + 8 <= nrows) {
           put_rows<kF32, 8>(a, ostage, lb0, nr, b_lo + lb0, col, n_ok, v);
         } else {
@@ -457,7 +488,7 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
       // this CTA's received partials are consumed: every sender may send again
       if (warp == 2 && lane < C) mbar_arrive_cluster(mapa(smem_u32(&aux->freed), lane));
     }
-    if (lead) bulk_wait_all();
+    if (lead) bulk_wait_read();  // the Y tiles have left shared memory
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -603,8 +634,7 @@ extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, voi
   const int n_tiles = (N + lin::TILE_N - 1) / lin::TILE_N;
   const int items = G * n_tiles;
   const int nkb = K / lin::KBW;
-  const int C = lin::pick_split(items, nkb);
-  const int n_cl = std::min(items, C == 1 ? num_sms() : lin::max_clusters(C));
+  const int C_pick = lin::pick_split(items, nkb);
   // token rows in chunks of up to kMaxB (one accumulator column each)
   for (int b0 = 0; b0 < B; b0 += lin::kMaxB) {
     const int nb = std::min(lin::kMaxB, B - b0);
@@ -619,26 +649,40 @@ extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, voi
     a.K = K;
     a.G = G;
     a.n_tiles = n_tiles;
-    a.split = C;
-    a.rows_per = (nb + C - 1) / C;
-    a.stage_bytes = uint32_t(lin::kWBytes + a.Bp * lin::KBW * 2);
     const int es = out_f32 ? 4 : 2;
-    // Y tiles leave through a TMA store when Y's rows and groups start on
-    // 16-byte boundaries; otherwise element by element
     const int64_t y_off = int64_t(b0) * ld_y * es;
-    a.tma_store = aligned(y, 16) && (ld_y * es) % 16 == 0 && (G == 1 || (int64_t(N) * es) % 16 == 0) ? 1 : 0;
-    const int out_rows = C > 1 ? a.rows_per : a.Bp;
-    const uint32_t part_bytes = C > 1 ? uint32_t(a.Bp) * lin::TILE_N * 4 : 0;
-    const uint32_t recv_bytes = C > 1 ? uint32_t(C * a.rows_per) * lin::TILE_N * 4 : 0;
-    const uint32_t out_bytes = a.tma_store ? (uint32_t(out_rows) * lin::TILE_N * es + 127u) & ~127u : 0;
-    const uint32_t fixed = uint32_t(1024 + lin::kAuxBytes) + part_bytes + recv_bytes + out_bytes;
-    a.n_stages = fixed < uint32_t(lin::kSmemBytes)
-                     ? std::min<int>(lin::kMaxStages, int((uint32_t(lin::kSmemBytes) - fixed) / a.stage_bytes))
-                     : 0;
-    a.part_off = uint32_t(a.n_stages) * a.stage_bytes;
-    a.recv_off = a.part_off + part_bytes;
-    a.out_off = a.recv_off + recv_bytes;
-    a.aux_off = a.out_off + out_bytes;
+    // the picked split, or a smaller one where its buffers leave the weight
+    // ring fewer than 2 stages (large B with a deep split)
+    int C = C_pick;
+    for (;; --C) {
+      a.split = C;
+      a.rows_per = (nb + C - 1) / C;
+      a.stage_bytes = uint32_t(lin::kWBytes + a.Bp * lin::KBW * 2);
+      // Y tiles leave through a TMA store when Y's rows and groups start on
+      // 16-byte boundaries; otherwise element by element
+      a.tma_store = aligned(y, 16) && (ld_y * es) % 16 == 0 && (G == 1 || (int64_t(N) * es) % 16 == 0) ? 1 : 0;
+      // rows the epilogue touches: accumulator columns go 32 at a time (C = 1,
+      // and the partial writes of C > 1), owned rows 8 at a time (C > 1)
+      const int rows32 = (a.Bp + 31) / 32 * 32;
+      const int done_rows = C > 1 ? (a.rows_per + 7) / 8 * 8 : rows32;
+      a.rope_rows = done_rows;
+      const uint32_t part_bytes = C > 1 ? uint32_t(rows32) * lin::TILE_N * 4 : 0;
+      const uint32_t recv_bytes = C > 1 ? uint32_t(C * a.rows_per) * lin::TILE_N * 4 : 0;
+      const uint32_t out_bytes = a.tma_store ? (uint32_t(done_rows) * lin::TILE_N * es + 127u) & ~127u : 0;
+      const uint32_t rope_bytes = rope_dim > 0 ? uint32_t(done_rows) * uint32_t(rope_dim / 2) * 8u : 0;
+      const uint32_t fixed = uint32_t(1024 + lin::kAuxBytes) + part_bytes + recv_bytes + out_bytes + rope_bytes;
+      a.n_stages = fixed < uint32_t(lin::kSmemBytes)
+                       ? std::min<int>(lin::kMaxStages, int((uint32_t(lin::kSmemBytes) - fixed) / a.stage_bytes))
+                       : 0;
+      a.part_off = uint32_t(a.n_stages) * a.stage_bytes;
+      a.recv_off = a.part_off + part_bytes;
+      a.out_off = a.recv_off + recv_bytes;
+      a.rope_off = a.out_off + out_bytes;
+      a.aux_off = (a.rope_off + rope_bytes + 15u) & ~15u;
+      if (C == 1 || (a.n_stages >= 2 && lin::max_clusters(C) > 0)) break;
+    }
+    const int n_cl = std::min(items, C == 1 ? num_sms() : lin::max_clusters(C));
+    const int out_rows = C > 1 ? a.rows_per : a.Bp;  // the Y box
     a.out_f32 = out_f32;
     a.cos = cos;
     a.sin = sin;
