@@ -11,9 +11,17 @@ stage, each function citing the reference lines it follows.  See
 
 Parity pinning: the reference's own CPU forward passes were deleted from
 ``inference.py`` and its device path needs ttnn/tt-lang/Tenstorrent hardware,
-so the path cannot be executed here end to end.  The oracle is pinned in two
-ways (tests/test_oracle_*.py):
+so the path cannot be executed here end to end on its device.  The oracle is
+pinned in three ways (tests/test_oracle_*.py):
 
+* against the reference's own device op chains - ``_device_act_quant_block``,
+  ``DeviceAttention._indexer_topk_body`` and the verbatim chain of
+  tt-lang-kernels/mega/test_lk_d_topk.py, ``DeviceSparseAttn.forward_device``,
+  the indexer score reference, ``DeviceCompressorOverlap`` /
+  ``DeviceCompressorNoOverlap`` - run unmodified on CPU through a test-only
+  torch stand-in for ``ttnn`` (fp32 policy) by
+  ``tests/golden/make_ref_chains.py``, committed as
+  ``tests/golden/ref_chains.npz``;
 * against the reference's surviving pure-torch helpers, imported from the
   reference with a stub ``ttl`` module by ``tests/golden/make_golden.py``
   (window-index table, slot-shift matrix, softmax-sum-norm masks, YaRN
@@ -24,9 +32,9 @@ ways (tests/test_oracle_*.py):
   the compressor softmax, a single valid index for sparse attention, values
   on the e4m3 grid for act_quant).
 
-The ttnn arithmetic itself (``ttnn.topk``, ``ttnn.matmul``...) is not pinned
-against the library (tt-metal is not vendored, its version is unpinned):
-parity is "partially pinned" in that sense.
+What stays unpinned is the Tenstorrent device arithmetic itself
+(``ttnn.topk``'s tie order, bf16 device rounding): the chain fixtures are the
+reference's algorithms evaluated in fp32 on bf16-valued inputs.
 """
 
 from .path import *  # noqa: F401,F403
