@@ -405,10 +405,11 @@ int dsa_sparse_attn(const void* q, const void* kv, int64_t kv_bstride, int64_t k
  * library reserves in device memory on every GPU that loads it and keeps
  * until the process exits.  Shapes whose partials need more than 8 MiB
  * (dsa_sparse_attn_workspace_size() > 8 MiB) are rejected with
- * DSA_ERR_WORKSPACE.  The partials take nsplit * B * S * 64 * 514 * 4
- * bytes, so about 63 (query row, key split) pairs fit: a few decode rows
- * or one long context do, config 2's 64-sequence decode (2 splits per row,
- * 16.8 MB) does not and must use dsa_sparse_attn with a workspace.  The
+ * DSA_ERR_WORKSPACE.  The partials take nsplit * B * S * 64 * (2 * 4 + 512 * 2)
+ * bytes (fp32 m and l, the bf16 o / l), so about 127 (query row, key split)
+ * pairs fit: a few decode rows or one long context do, config 2's
+ * 64-sequence decode (2 splits per row, 8.45 MB) does not and must use
+ * dsa_sparse_attn with a workspace.  The
  * first call on a device looks up the array's device address and caches it
  * for the life of the process; make that first call before any stream
  * capture, and do not use this entry point across a device reset

@@ -21,7 +21,11 @@ constexpr int kSaH = 64;
 constexpr int kSaD = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Merge of the split-K partials of each query row: final mode writes
+// Merge of the split-K partials of each query row.  Partials come as fp32
+// (m, l, unnormalised o) - the sequence split's exchanged partials - or, for
+// the library's own split-K workspace (kNormBF16), as fp32 (m, l) with the
+// bf16 o / l, half the bytes to write and read back; the weight of a
+// partial is then l e^{m - M} instead of e^{m - M}.  Final mode writes
 // o = sum_p o_p e^{m_p - M} / L with the sink in L; partial mode writes
 // (M, L, sum_p o_p e^{m_p-M}) without the sink.  One warp per (query row,
 // head, slice of DPL * 32 output dims): the split statistics are reduced
@@ -31,9 +35,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 // more warps for the few-row case (a single long context), where the
 // combine would otherwise run on M * 8 CTAs.
 constexpr int kCombineWarps = 8;
-template <int DPL>
+template <int DPL, bool kNormBF16>
 __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
-    const float* __restrict__ part_ml, const float* __restrict__ part_o, const float* __restrict__ sink, int P, int M,
+    const float* __restrict__ part_ml, const void* __restrict__ part_o, const float* __restrict__ sink, int P, int M,
     int H, int D, int64_t ml_ps, int64_t o_ps, int final_mode, __nv_bfloat16* __restrict__ out,
     float* __restrict__ lse, float* __restrict__ out_ml, float* __restrict__ out_o) {
   const int m = blockIdx.x, lane = threadIdx.x & 31;
@@ -63,17 +67,34 @@ __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
 #pragma unroll 4
   for (int p = 0; p < P; ++p) {
     const float mp = ml(p, 0);
-    const float w = (mp == -INFINITY) ? 0.f : expf(mp - Mx);
-    const float4* src = reinterpret_cast<const float4*>(part_o + int64_t(p) * o_ps + (int64_t(m) * H + h) * D + d0);
-    float4 v[DPL / 4];
+    float w = (mp == -INFINITY) ? 0.f : expf(mp - Mx);
+    const int64_t off = int64_t(p) * o_ps + (int64_t(m) * H + h) * D + d0;
+    if constexpr (kNormBF16) {
+      w *= ml(p, 1);
+      // DPL bf16 values = DPL / 4 8-byte words
+      const uint2* src = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(part_o) + off);
+      uint2 v[DPL / 4];
 #pragma unroll
-    for (int i = 0; i < DPL / 4; ++i) v[i] = __ldg(src + i);
+      for (int i = 0; i < DPL / 4; ++i) v[i] = __ldg(src + i);
 #pragma unroll
-    for (int i = 0; i < DPL / 4; ++i) {
-      acc[4 * i + 0] = fmaf(w, v[i].x, acc[4 * i + 0]);
-      acc[4 * i + 1] = fmaf(w, v[i].y, acc[4 * i + 1]);
-      acc[4 * i + 2] = fmaf(w, v[i].z, acc[4 * i + 2]);
-      acc[4 * i + 3] = fmaf(w, v[i].w, acc[4 * i + 3]);
+      for (int i = 0; i < DPL / 4; ++i) {
+        acc[4 * i + 0] = fmaf(w, __uint_as_float(v[i].x << 16), acc[4 * i + 0]);
+        acc[4 * i + 1] = fmaf(w, __uint_as_float(v[i].x & 0xffff0000u), acc[4 * i + 1]);
+        acc[4 * i + 2] = fmaf(w, __uint_as_float(v[i].y << 16), acc[4 * i + 2]);
+        acc[4 * i + 3] = fmaf(w, __uint_as_float(v[i].y & 0xffff0000u), acc[4 * i + 3]);
+      }
+    } else {
+      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(part_o) + off);
+      float4 v[DPL / 4];
+#pragma unroll
+      for (int i = 0; i < DPL / 4; ++i) v[i] = __ldg(src + i);
+#pragma unroll
+      for (int i = 0; i < DPL / 4; ++i) {
+        acc[4 * i + 0] = fmaf(w, v[i].x, acc[4 * i + 0]);
+        acc[4 * i + 1] = fmaf(w, v[i].y, acc[4 * i + 1]);
+        acc[4 * i + 2] = fmaf(w, v[i].z, acc[4 * i + 2]);
+        acc[4 * i + 3] = fmaf(w, v[i].w, acc[4 * i + 3]);
+      }
     }
   }
   if (final_mode) {
@@ -100,19 +121,18 @@ __global__ void __launch_bounds__(32 * kCombineWarps) lse_combine_kernel(
 
 // Launch of the combine: DPL = 4 (4 CTAs per 8 heads) when the rows alone
 // would leave most SMs idle.
-static void launch_lse_combine(const float* part_ml, const float* part_o, const float* sink, int P, int M, int H,
-                               int D, int final_mode, __nv_bfloat16* out, float* lse, float* out_ml, float* out_o,
-                               cudaStream_t st, int64_t ml_ps = -1, int64_t o_ps = -1) {
+static void launch_lse_combine(const float* part_ml, const void* part_o, bool norm_bf16, const float* sink, int P,
+                               int M, int H, int D, int final_mode, __nv_bfloat16* out, float* lse, float* out_ml,
+                               float* out_o, cudaStream_t st, int64_t ml_ps = -1, int64_t o_ps = -1) {
   const int hb = (H + kCombineWarps - 1) / kCombineWarps;
   if (ml_ps < 0) ml_ps = int64_t(M) * H * 2;
   if (o_ps < 0) o_ps = int64_t(M) * H * D;
-  if (int64_t(M) * hb < 2 * num_sms()) {
-    launch_pdl(lse_combine_kernel<4>, dim3(M, hb, D / 128), dim3(32 * kCombineWarps), 0, st, part_ml, part_o, sink, P,
-               M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
-  } else {
-    launch_pdl(lse_combine_kernel<16>, dim3(M, hb, D / 512), dim3(32 * kCombineWarps), 0, st, part_ml, part_o, sink,
-               P, M, H, D, ml_ps, o_ps, final_mode, out, lse, out_ml, out_o);
-  }
+  const bool few = int64_t(M) * hb < 2 * num_sms();
+  const dim3 grid(M, hb, few ? D / 128 : D / 512);
+  auto k = few ? (norm_bf16 ? lse_combine_kernel<4, true> : lse_combine_kernel<4, false>)
+               : (norm_bf16 ? lse_combine_kernel<16, true> : lse_combine_kernel<16, false>);
+  launch_pdl(k, grid, dim3(32 * kCombineWarps), 0, st, part_ml, part_o, sink, P, M, H, D, ml_ps, o_ps, final_mode,
+             out, lse, out_ml, out_o);
 }
 
 struct SplitPlan {
@@ -140,7 +160,8 @@ static SplitPlan plan_splits(int M, int K) {
 }
 
 static size_t ws_bytes_for(const SplitPlan& p, int M) {
-  return p.nsplit <= 1 ? 0 : size_t(p.nsplit) * M * kSaH * (2 + kSaD) * sizeof(float);
+  // per (split, row, head): fp32 (m, l) and the bf16 o / l
+  return p.nsplit <= 1 ? 0 : size_t(p.nsplit) * M * kSaH * (2 * sizeof(float) + kSaD * sizeof(__nv_bfloat16));
 }
 
 static void ensure_attr() {
@@ -211,7 +232,7 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   t.wait_limit = wait_limit_cycles();
   t.trace = g_trace;
   float* ws_ml = nullptr;
-  float* ws_o = nullptr;
+  __nv_bfloat16* ws_o = nullptr;
   if (p.nsplit > 1) {
     const size_t need = ws_bytes_for(p, M);
     if (ws == nullptr || ws_bytes < need) {
@@ -219,10 +240,10 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
       return DSA_ERR_WORKSPACE;
     }
     ws_ml = static_cast<float*>(ws);
-    ws_o = ws_ml + size_t(p.nsplit) * M * kSaH * 2;
+    ws_o = reinterpret_cast<__nv_bfloat16*>(ws_ml + size_t(p.nsplit) * M * kSaH * 2);
     t.final_mode = 0;
     t.part_ml = ws_ml;
-    t.part_o = ws_o;
+    t.part_ob = ws_o;
   } else if (final_mode) {
     t.final_mode = 1;
     t.out = static_cast<__nv_bfloat16*>(out);
@@ -243,7 +264,7 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
              row_stride);
   DSA_CHECK_LAUNCH("sparse_attn");
   if (p.nsplit > 1) {
-    launch_lse_combine(ws_ml, ws_o, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
+    launch_lse_combine(ws_ml, ws_o, true, sink, p.nsplit, M, kSaH, kSaD, final_mode ? 1 : 0,
                        static_cast<__nv_bfloat16*>(out), lse, part_ml_out, part_o_out, st);
     DSA_CHECK_LAUNCH("sparse_attn(combine)");
   }
@@ -279,7 +300,7 @@ extern "C" int dsa_lse_combine(const float* part_ml, const float* part_o, const 
   DSA_CHECK_ARG(D == kSaD, "lse_combine: built for D=%d (got %d)", kSaD, D);
   DSA_CHECK_ARG(aligned(part_o, 16) && aligned(out, 16), "lse_combine: part_o / out must be 16-byte aligned");
   if (M == 0) return DSA_OK;
-  launch_lse_combine(part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
+  launch_lse_combine(part_ml, part_o, false, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
                      nullptr, reinterpret_cast<cudaStream_t>(stream));
   DSA_CHECK_LAUNCH("lse_combine");
   return DSA_OK;
@@ -296,7 +317,7 @@ extern "C" int dsa_lse_combine_strided(const float* part_ml, int64_t ml_pstride,
                 "lse_combine_strided: partial strides must cover M*H*2 / M*H*D floats (o stride a multiple of 4)");
   DSA_CHECK_ARG(aligned(part_o, 16) && aligned(out, 16), "lse_combine_strided: part_o / out must be 16-byte aligned");
   if (M == 0) return DSA_OK;
-  launch_lse_combine(part_ml, part_o, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
+  launch_lse_combine(part_ml, part_o, false, sink, P, M, H, D, 1, static_cast<__nv_bfloat16*>(out), nullptr, nullptr,
                      nullptr, reinterpret_cast<cudaStream_t>(stream), ml_pstride, o_pstride);
   DSA_CHECK_LAUNCH("lse_combine_strided");
   return DSA_OK;

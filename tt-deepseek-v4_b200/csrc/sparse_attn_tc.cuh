@@ -121,6 +121,7 @@ struct Args {
   float* lse;
   float* part_ml;
   float* part_o;
+  __nv_bfloat16* part_ob;  // non-null: the split partial as bf16 O / l (the library's own split-K workspace)
   int32_t* status;
   int S, M, K, tiles_per_split;
   float scale_log2;
@@ -557,7 +558,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
           const int64_t base = int64_t(split) * a.M + mrow;
           a.part_ml[(base * H + h) * 2 + 0] = (mh == -INFINITY) ? -INFINITY : mh * kLn2;
           a.part_ml[(base * H + h) * 2 + 1] = lh;
-          aux->f[h] = 1.f;
+          aux->f[h] = a.part_ob ? (lh > 0.f ? 1.f / lh : 0.f) : 1.f;
         }
       }
     }
@@ -591,6 +592,10 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         __nv_bfloat16* om = a.out + int64_t(mrow) * H * D + d;
 #pragma unroll
         for (int i = 0; i < 32; ++i) om[(32 * hf + i) * D] = f2bf(o[i] * aux->f[32 * hf + i]);
+      } else if (a.part_ob) {
+        __nv_bfloat16* pb = a.part_ob + (int64_t(split) * a.M + mrow) * H * D + d;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pb[(32 * hf + i) * D] = f2bf(o[i] * aux->f[32 * hf + i]);
       } else {
         float* po = a.part_o + (int64_t(split) * a.M + mrow) * H * D + d;
 #pragma unroll
