@@ -235,7 +235,8 @@ def time_kernels(path, inputs, outs, reps=3):
         res[name] = best
         del g
 
-    run("sparse_attn", lambda: [ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, path.scale, out=o, ws=L.ws)
+    run("sparse_attn", lambda: [ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, path.scale, out=o, ws=L.ws,
+                                                lead_cols=L.win, lead_ready=True)
                                 for L, x, o in zip(path.layers, inputs, outs)])
     run("indexer_score", lambda: [ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score,
                                                     t_valid=path.t_active) for L, x in zip(path.layers, inputs)])

@@ -397,6 +397,26 @@ int dsa_sparse_attn(const void* q, const void* kv, int64_t kv_bstride, int64_t k
                     void* workspace, size_t workspace_bytes, int32_t* status,
                     dsa_stream_t stream);
 
+/* dsa_sparse_attn with a scheduling hint.  lead_cols (a multiple of 64,
+ * < K; 0 = none): the first lead_cols index columns of every row (in this
+ * path the window ring slots, written before the top-k).  With
+ * DSA_LEAD_READY the caller guarantees that the kernel this launch may
+ * overlap (the previous kernel on the stream, under programmatic dependent
+ * launch) writes neither q, nor those index columns, nor the kv rows they
+ * name, and that every other writer of them completed before this launch;
+ * each key split then takes one 64-entry lead tile first and requests it,
+ * with q, before waiting for that kernel, and the rest of the row in even
+ * runs.  Same results
+ * as dsa_sparse_attn (up to fp32 summation order across splits); the
+ * workspace size is the same.  Has no counterpart in the reference (its
+ * device path is one ttnn op chain per call). */
+enum { DSA_LEAD_READY = 1 };
+int dsa_sparse_attn_ex(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,
+                       const int32_t* idx, int64_t ld_idx, const float* sink, void* out,
+                       float* lse, int B, int S, int H, int D, int K, float scale,
+                       void* workspace, size_t workspace_bytes, int lead_cols, unsigned flags,
+                       int32_t* status, dsa_stream_t stream);
+
 /* Allocation-free variant of dsa_sparse_attn, for callers that cannot
  * allocate device memory where they call the attention (a runtime that owns
  * a fixed device arena, a plugin running inside another framework's memory

@@ -356,3 +356,40 @@ def test_sparse_attn_peaked_softmax(cuda_dev):
     assert int(status.item()) == 0
     assert float(want.float().abs().max()) > 0.5
     assert rel_err(got, want) < ATTN_REL, rel_err(got, want)
+
+
+@pytest.mark.parametrize("B,N,K,lead", [(64, 2048, 2176, 128), (1, 70000, 2176, 128), (4, 4224, 640, 128),
+                                        (3, 900, 256, 64), (2, 600, 130, 128)])
+def test_sparse_attn_lead_tiles_match_oracle(cuda_dev, B, N, K, lead):
+    """dsa_sparse_attn_ex with DSA_LEAD_READY (each key split takes one
+    window tile first, requested before the dependency wait): the same
+    output and log-sum-exp as the oracle, including a lead tile whose
+    entries are partly masked, and shapes where the lead mapping does not
+    apply (fewer splits than lead tiles) and the plain mapping runs."""
+    from dsv4attn import ops
+    q, kv, idx, sink = _attn_case(B, 1, N, K, seed=3 * N + K)
+    idx[:, :, 5] = -1
+    scale = 512 ** -0.5
+    want = O.sparse_attn(q, kv, idx, sink, scale)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    lse = torch.empty(B, 64, device=cuda_dev)
+    lse0 = torch.empty(B, 64, device=cuda_dev)
+    qd, kvd, idd, sd = q.to(cuda_dev), kv.to(cuda_dev), idx.to(cuda_dev), sink.to(cuda_dev)
+    got = ops.sparse_attn(qd, kvd, idd, sd, scale, lse=lse, status=status, lead_cols=lead, lead_ready=True).cpu()
+    plain = ops.sparse_attn(qd, kvd, idd, sd, scale, lse=lse0).cpu()
+    assert int(status.item()) == 0
+    torch.testing.assert_close(got.float(), want.float(), rtol=2e-2, atol=2e-2)
+    assert rel_err(got, want) < ATTN_REL
+    # the two differ by the bf16 rounding of differently composed split partials
+    torch.testing.assert_close(got.float(), plain.float(), rtol=2e-2, atol=4e-3)
+    torch.testing.assert_close(lse.cpu(), lse0.cpu(), rtol=1e-4, atol=1e-4)
+
+
+def test_sparse_attn_ex_rejects_bad_lead(cuda_dev):
+    from dsv4attn import _lib
+    q, kv, idx, sink = (t.to(cuda_dev) for t in _attn_case(1, 1, 300, 64, seed=1))
+    out = torch.empty_like(q)
+    L = _lib.lib()
+    rc = L.dsa_sparse_attn_ex(q.data_ptr(), kv.data_ptr(), 300 * 512, 300, idx.data_ptr(), 64, sink.data_ptr(),
+                              out.data_ptr(), None, 1, 1, 64, 512, 64, 0.05, None, 0, 128, 1, None, None)
+    assert rc != 0 and "lead_cols" in _lib.last_error()

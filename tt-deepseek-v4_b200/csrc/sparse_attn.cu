@@ -205,7 +205,8 @@ extern "C" size_t dsa_sparse_attn_workspace_size(int B, int S, int H, int D, int
 static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows, const int32_t* idx,
                            int64_t ld_idx, const float* sink, void* out, float* lse, float* part_ml_out,
                            float* part_o_out, int B, int S, int H, int D, int K, float scale, void* ws,
-                           size_t ws_bytes, int32_t* status, cudaStream_t st, bool final_mode) {
+                           size_t ws_bytes, int32_t* status, cudaStream_t st, bool final_mode, int lead_cols = 0,
+                           unsigned flags = 0) {
   int rc = check_common(q, kv, kv_bstride, kv_rows, idx, ld_idx, B, S, H, D, K);
   if (rc) return rc;
   const int M = B * S;
@@ -228,6 +229,19 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   t.M = M;
   t.K = K;
   t.tiles_per_split = p.tiles_per_split;
+  // lead tiles: one per split, first, when the caller names leading index
+  // columns that are ready early (requested before the dependency wait)
+  if ((flags & DSA_LEAD_READY) && lead_cols > 0 && lead_cols % satc::TK == 0 && lead_cols < K &&
+      p.nsplit >= lead_cols / satc::TK) {
+    const int lead_tiles = lead_cols / satc::TK;
+    const int rest_tiles = (K - lead_cols + satc::TK - 1) / satc::TK;
+    const int rest_tps = (rest_tiles + p.nsplit - 1) / p.nsplit;
+    if (1 + rest_tps <= satc::kMaxTilesPerSplit) {
+      t.lead_tiles = lead_tiles;
+      t.rest_tps = rest_tps;
+      t.early = 1;
+    }
+  }
   t.scale_log2 = scale * kLog2e;
   t.wait_limit = wait_limit_cycles();
   t.trace = g_trace;
@@ -269,6 +283,19 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
     DSA_CHECK_LAUNCH("sparse_attn(combine)");
   }
   return DSA_OK;
+}
+
+extern "C" int dsa_sparse_attn_ex(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,
+                                  const int32_t* idx, int64_t ld_idx, const float* sink, void* out, float* lse, int B,
+                                  int S, int H, int D, int K, float scale, void* workspace, size_t workspace_bytes,
+                                  int lead_cols, unsigned flags, int32_t* status, dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG(sink && out, "sparse_attn: null sink/out");
+  DSA_CHECK_ARG(lead_cols >= 0 && lead_cols <= K, "sparse_attn: lead_cols %d outside [0, K]", lead_cols);
+  DSA_CHECK_ARG((flags & ~unsigned(DSA_LEAD_READY)) == 0, "sparse_attn: unknown flags 0x%x", flags);
+  return sparse_attn_run(q, kv, kv_bstride, kv_rows, idx, ld_idx, sink, out, lse, nullptr, nullptr, B, S, H, D, K,
+                         scale, workspace, workspace_bytes, status, reinterpret_cast<cudaStream_t>(stream), true,
+                         lead_cols, flags);
 }
 
 extern "C" int dsa_sparse_attn(const void* q, const void* kv, int64_t kv_bstride, int64_t kv_rows,

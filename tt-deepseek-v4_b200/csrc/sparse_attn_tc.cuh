@@ -124,6 +124,13 @@ struct Args {
   __nv_bfloat16* part_ob;  // non-null: the split partial as bf16 O / l (the library's own split-K workspace)
   int32_t* status;
   int S, M, K, tiles_per_split;
+  // lead tiles: with lead_tiles > 0, split s < lead_tiles takes the 64
+  // entries [64 s, 64 s + 64) of the index row as its first tile, and every
+  // split then a contiguous run of rest_tps tiles of the entries after
+  // 64 lead_tiles.  early: those lead entries, q and the kv rows they name
+  // were complete before the previous kernel on the stream began, so the
+  // lead tile and q are requested before the dependency wait.
+  int lead_tiles, rest_tps, early;
   float scale_log2;
   int final_mode;
   long long wait_limit;  // spin budget of every bounded wait, SM cycles
@@ -212,9 +219,13 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int mrow = blockIdx.y, split = blockIdx.x;
   const int b = mrow / a.S;
-  const int j_begin = split * a.tiles_per_split * TK;
-  const int j_end = min(a.K, j_begin + a.tiles_per_split * TK);
-  const int n = j_end > j_begin ? (j_end - j_begin + TK - 1) / TK : 0;
+  // this split's tiles: an optional lead tile, then the run [j_begin, j_end)
+  const bool has_lead = split < a.lead_tiles;
+  const int n_lead = has_lead ? 1 : 0;
+  const int j_begin = a.lead_tiles > 0 ? a.lead_tiles * TK + split * a.rest_tps * TK : split * a.tiles_per_split * TK;
+  const int j_end = max(j_begin, min(a.K, j_begin + (a.lead_tiles > 0 ? a.rest_tps : a.tiles_per_split) * TK));
+  const int n = n_lead + (j_end > j_begin ? (j_end - j_begin + TK - 1) / TK : 0);
+  const bool early_lead = a.early && has_lead;
   const int32_t* idxr = a.idx + int64_t(mrow) * a.ld_idx;
   int32_t* s_idx = reinterpret_cast<int32_t*>(smem + kOffIdx);
 #ifdef DSA_ATTN_TRACE
@@ -243,41 +254,83 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     tc::mbar_init(smem_u32(&aux->mma_done), 1);
     tc::mbar_fence_init();
   }
-  // set-up above touches no global memory; the index list and q are the
-  // previous kernels' outputs
-  pdl_wait();
-  pdl_launch_dependents();
+  // the barriers are initialised before any thread arrives on them (the
+  // lead tile's copies may start before the dependency wait)
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
   // The query block into the last ring slot (free until Q' is in TMEM).
   const uint32_t sQstage = sRing + (NT - 1) * kTileBytes;
-  if (tid == 32) {
-    tma::prefetch_map(&tm_q);
-    tma::mbar_arrive_expect_tx(smem_u32(&aux->q_tma), H * D * 2);
+  auto load_q = [&]() {
+    if (tid == 32) {
+      tma::prefetch_map(&tm_q);
+      tma::mbar_arrive_expect_tx(smem_u32(&aux->q_tma), H * D * 2);
 #pragma unroll
-    for (int kb = 0; kb < KB; ++kb)
-      tma::load_2d(sQstage + kb * (H * 128), &tm_q, kb * 64, mrow * H, smem_u32(&aux->q_tma));
+      for (int kb = 0; kb < KB; ++kb)
+        tma::load_2d(sQstage + kb * (H * 128), &tm_q, kb * 64, mrow * H, smem_u32(&aux->q_tma));
+    }
+  };
+  // index-row position of staged entry e (e < n * TK): the lead tile's 64
+  // entries, then the run; -1 past the run's end
+  auto index_at = [&](int e) -> int {
+    if (e < n_lead * TK) return __ldg(idxr + split * TK + e);
+    const int j = j_begin + e - n_lead * TK;
+    return j < j_end ? __ldg(idxr + j) : -1;
+  };
+  const __nv_bfloat16* kvb = a.kv + int64_t(b) * kv_row_base_stride * D;
+  // producers: the 16-B copies of tile t's rows pw, pw + P, ... into its slot
+  auto issue_tile = [&](int t, int pw) {
+    const int slot = t % NT;
+    const uint32_t dst = sRing + slot * kTileBytes;
+    for (int r = pw; r < TK; r += kProducerWarps) {
+      const int id = s_idx[t * TK + r];
+      const bool ok = id >= 0;
+      const __nv_bfloat16* src = kvb + int64_t(ok ? id : 0) * D;
+      cp_async16(dst + chunk_off(r, lane), src + lane * 8, ok ? 16 : 0);
+      cp_async16(dst + chunk_off(r, lane + 32), src + (lane + 32) * 8, ok ? 16 : 0);
+    }
+    // this lane's arrival fires when its copies of the tile have landed
+    tc::cp_async_arrive_noinc(smem_u32(&aux->full[slot]));
+    if (pw == 0 && lane == 0) SA_TRACE(kTrIssue, t);
+  };
+  // staged entry: -1 for masked / padding slots, out-of-range rows clamped
+  // (and reported through status), one validity bit per entry (whole warps)
+  auto stage = [&](int e, int id) {
+    if (id >= a.kv_rows) {
+      if (a.status) atomicOr(a.status, kStatusBadIndex);
+      id = int(a.kv_rows - 1);
+    }
+    s_idx[e] = id < 0 ? -1 : id;
+    const uint32_t bits = __ballot_sync(0xffffffffu, id >= 0);
+    if (lane == 0) aux->vmask[e >> 5] = bits;
+  };
+  if (early_lead) {
+    // before the dependency wait: q and the lead tile
+    load_q();
+    if (tid < TK) stage(tid, index_at(tid));
+    __syncthreads();
+    if (is_producer_warp(warp)) issue_tile(0, producer_index(warp));
+  } else if (a.early) {
+    load_q();
   }
-  // The split's index list, staged once: -1 for masked / padding slots,
-  // out-of-range rows clamped (and reported through status), plus one
-  // validity bit per index.  All loads are issued before the first store.
+  pdl_wait();
+  pdl_launch_dependents();
+  if (!a.early) load_q();
+  // The rest of the split's index list, staged once.  All loads are issued
+  // before the first store.
   {
+    const int e0 = early_lead ? TK : 0;
     int ids[kIdxPerThread];
 #pragma unroll
     for (int k = 0; k < kIdxPerThread; ++k) {
       const int e = tid + k * THREADS;
-      ids[k] = (e < n * TK && j_begin + e < j_end) ? __ldg(idxr + j_begin + e) : -1;
+      ids[k] = (e >= e0 && e < n * TK) ? index_at(e) : -1;
     }
 #pragma unroll
     for (int k = 0; k < kIdxPerThread; ++k) {
       const int e = tid + k * THREADS;
-      if (e < n * TK) {  // whole warps: n * TK is a multiple of 64
-        int id = ids[k];
-        if (id >= a.kv_rows) {
-          if (a.status) atomicOr(a.status, kStatusBadIndex);
-          id = int(a.kv_rows - 1);
-        }
-        s_idx[e] = id < 0 ? -1 : id;
-        const uint32_t bits = __ballot_sync(0xffffffffu, id >= 0);
-        if (lane == 0) aux->vmask[e >> 5] = bits;
+      if (e >= e0 && e < n * TK) {  // whole warps: n * TK and e0 are multiples of 64
+        stage(e, ids[k]);
       }
     }
   }
@@ -308,26 +361,13 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     // Tiles 0 .. NT-2 are requested first; the last slot holds the query
     // block until every thread has moved its part of Q' (q_full).
     const int pw = producer_index(warp);
-    const __nv_bfloat16* kvb = a.kv + int64_t(b) * kv_row_base_stride * D;
-    for (int t = 0; t < n; ++t) {
+    for (int t = early_lead ? 1 : 0; t < n; ++t) {
       if (t == NT - 1) {
         q_part();
         warp_wait(&aux->q_full, 0);
       }
-      const int slot = t % NT;
-      if (t >= NT) warp_wait(&aux->empty[slot], ((t / NT) - 1) & 1);
-      const uint32_t dst = sRing + slot * kTileBytes;
-      // rows pw, pw + P, ...: lane copies 16-B chunks lane and lane + 32
-      for (int r = pw; r < TK; r += kProducerWarps) {
-        const int id = s_idx[t * TK + r];
-        const bool ok = id >= 0;
-        const __nv_bfloat16* src = kvb + int64_t(ok ? id : 0) * D;
-        cp_async16(dst + chunk_off(r, lane), src + lane * 8, ok ? 16 : 0);
-        cp_async16(dst + chunk_off(r, lane + 32), src + (lane + 32) * 8, ok ? 16 : 0);
-      }
-      // this lane's arrival fires when its copies of the tile have landed
-      tc::cp_async_arrive_noinc(smem_u32(&aux->full[slot]));
-      if (pw == 0 && lane == 0) SA_TRACE(kTrIssue, t);
+      if (t >= NT) warp_wait(&aux->empty[t % NT], ((t / NT) - 1) & 1);
+      issue_tile(t, pw);
     }
     if (n < NT) q_part();
     cp_async_wait<0>();

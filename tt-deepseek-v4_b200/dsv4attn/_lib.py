@@ -61,6 +61,8 @@ PROTOTYPES = {
     "dsa_shard_local_indices": (I32, [P, I64, I32, P, I64, I32, I32, I32, I32, I32, P, I64, I32, P]),
     "dsa_sparse_attn_workspace_size": (SZ, [I32, I32, I32, I32, I32]),
     "dsa_sparse_attn": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
+    "dsa_sparse_attn_ex": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, SZ, I32,
+                                 ctypes.c_uint, P, P]),
     "dsa_sparse_attn_noalloc": (I32, [P, P, I64, I64, P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P, P]),
     "dsa_sparse_attn_partial": (I32, [P, P, I64, I64, P, I64, P, P, I32, I32, I32, I32, I32, F32, P, SZ, P, P]),
     "dsa_lse_combine": (I32, [P, P, P, P, I32, I32, I32, I32, P]),

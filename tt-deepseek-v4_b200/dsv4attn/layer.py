@@ -242,7 +242,11 @@ class DecodePath:
         ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws,
                          refresh=(x.iq, L.idx_cache, x.iw))
         main.wait_stream(side)
-        ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, self.scale, out=out, ws=L.ws, status=self.status)
+        # the window columns of idx, q and the window rows were written before
+        # the top-k began (side branch, inputs): each key split requests its
+        # window tile before waiting for the top-k
+        ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, self.scale, out=out, ws=L.ws, status=self.status,
+                        lead_cols=W, lead_ready=True)
 
     def step(self, inputs: list[LayerInputs], outs: list[torch.Tensor], advance: bool = True) -> None:
         for L, x, o in zip(self.layers, inputs, outs):

@@ -588,11 +588,18 @@ def _attn_shapes(q, kv, idx):
     return B, S, H, D, K, kv, kv_bstride, idx2
 
 
+LEAD_READY = 1
+
+
 def sparse_attn(q, kv, idx, sink, scale: float, out=None, lse=None, ws: Workspace | None = None,
-                status=None) -> torch.Tensor:
+                status=None, lead_cols: int = 0, lead_ready: bool = False) -> torch.Tensor:
     """Sink-softmax sparse attention (inference.py:4459-4501).  q [B,S,H,D] or
     [B,H,D] bf16; kv [B,N,D] or [N,D] bf16; idx [B,S,K] / [B,K] int32 with -1
-    = masked; sink [H] fp32."""
+    = masked; sink [H] fp32.  ``lead_cols``/``lead_ready``: the first
+    lead_cols index columns (the window slots), q and the kv rows they name
+    are not written by the previous kernel on the stream and were complete
+    before this launch (dsa_sparse_attn_ex with DSA_LEAD_READY): they are
+    requested before the kernel waits for that one."""
     B, S, H, D, K, kv3, kv_bstride, idx2 = _attn_shapes(q, kv, idx)
     if kv3.shape[0] == 1 and B > 1:
         raise ValueError("a shared [N, D] kv needs B == 1; pass [B, N, D]")
@@ -602,6 +609,12 @@ def sparse_attn(q, kv, idx, sink, scale: float, out=None, lse=None, ws: Workspac
     L = lib()
     need = L.dsa_sparse_attn_workspace_size(B, S, H, D, K)
     w = _ws(q.device, need, ws) if need else None
+    if lead_ready and lead_cols > 0:
+        check(L.dsa_sparse_attn_ex(q.data_ptr(), kv3.data_ptr(), kv_bstride, kv3.shape[1], idx2.data_ptr(),
+                                   idx2.stride(0), sink.data_ptr(), out.data_ptr(), _ptr(lse), B, S, H, D, K, scale,
+                                   w.buf.data_ptr() if w else None, w.nbytes if w else 0, lead_cols, LEAD_READY,
+                                   _ptr(status), _stream(q)), "sparse_attn")
+        return out
     check(L.dsa_sparse_attn(q.data_ptr(), kv3.data_ptr(), kv_bstride, kv3.shape[1], idx2.data_ptr(),
                             idx2.stride(0), sink.data_ptr(), out.data_ptr(), _ptr(lse), B, S, H, D, K, scale,
                             w.buf.data_ptr() if w else None, w.nbytes if w else 0, _ptr(status), _stream(q)),
