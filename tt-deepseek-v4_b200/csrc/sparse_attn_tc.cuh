@@ -32,9 +32,13 @@
 //               128 B at a time only ~4.7 TB/s, so each row is read once,
 //               whole.  A tile completes on its slot's mbarrier through
 //               cp.async.mbarrier.arrive.
-//   warp 4      MMA issuer (one thread), ready-first: PV(t) as soon as P(t)
-//               is written (it frees the tile's slot), else S(t) as soon as
-//               tile t has landed and the softmax has read S(t-1).
+//   warp 8      S issuer (one thread): S(t) as soon as tile t has landed and
+//               the softmax has read S(t-1).
+//   warp 4      PV issuer (one thread): PV(t) as soon as P(t) is written (it
+//               frees the tile's slot).  The tensor pipe spends ~90 cycles
+//               on each of these MMAs whatever its shape, so a tile's 32
+//               MMAs bound the tile rate; two issuers keep both kinds queued
+//               (one ready-first issuer: ~3.1K cycles a tile, two: ~2.9K).
 //   warps 0-3   softmax.  Warp w owns heads 16w..16w+15: per 16 keys, two
 //               16x256b TMEM loads (the two dim halves) give thread i the
 //               scores of heads 16w + i/4 and 16w + 8 + i/4 for keys
@@ -75,9 +79,10 @@ constexpr int kTileBytes = KB * kSlabBytes;           // 64 KB
 // keys as 128 rows of 128 B: rows 32q..32q+15 = low half of keys
 // 16q..16q+15, rows 32q+16..32q+31 = their high half.
 constexpr int kPairBytes = 2 * kSlabBytes;            // 16 KB
-// 16 warps, four per scheduler (warp % 4): softmax 0-3, MMA issuer 4, and the
-// producers on the schedulers of warps 1-3 only (5-7, 9-11, 13-15), so the
-// MMA issuer shares its scheduler with one softmax warp; warps 8 and 12 idle.
+// 16 warps, four per scheduler (warp % 4): softmax 0-3, PV issuer 4, S
+// issuer 8, and the producers on the schedulers of warps 1-3 only (5-7,
+// 9-11, 13-15), so the issuers share their scheduler with one softmax warp;
+// warp 12 idles (it moves its part of Q' and joins the drain).
 constexpr int kProducerWarps = 9;
 constexpr int kMmaWarp = 4;
 constexpr int THREADS = 512;
@@ -251,7 +256,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tc::mbar_init(smem_u32(&aux->p_full[s]), 1);
       tc::mbar_init(smem_u32(&aux->pv_done[s]), 1);
     }
-    tc::mbar_init(smem_u32(&aux->mma_done), 1);
+    tc::mbar_init(smem_u32(&aux->mma_done), 2);  // one commit from each issuer
     tc::mbar_fence_init();
   }
   // the barriers are initialised before any thread arrives on them (the
@@ -372,73 +377,34 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     if (n < NT) q_part();
     cp_async_wait<0>();
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ PV issuer
     q_part();
     if (lane == 0 && n > 0) {
       const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
-      const uint32_t k_lo = tc::desc_lo(sRing, 16);          // K-major: LBO unused
       const uint32_t v_lo = tc::desc_lo(sRing, kPairBytes);  // MN-major: LBO = the next 64 dims (next pair block)
       const uint32_t p_lo = tc::desc_lo(sP, 16);             // K-major rows of 64 keys per head
       wait(&aux->q_full, 0);
       tc::fence_after_sync();
-      // Ready-first issue: PV(np) as soon as P(np) is written (it frees the
-      // tile's slot for the next copy), else S(ns) as soon as tile ns has
-      // landed and the softmax has read S(ns - 1).  Keeping MMAs queued
-      // avoids the ~700-cycle drain and refill of the tensor pipe that a
-      // wait between dependent batches costs.
-      int ns = 0, np = 0;
-      long long last = clock64();
-      while (np < n) {
-        bool did = false;
-        if (np < ns && tc::mbar_test_wait(smem_u32(&aux->p_full[np & 1]), (np >> 1) & 1)) {
-          tc::fence_after_sync();
-          const uint32_t vs = v_lo + (np % NT) * (kTileBytes / 16);
-          const uint32_t ps = p_lo + (np & 1) * (kPBytes / 16);
-          // PV(np): 16 MMAs of M=128 dims x N=64 heads x K=16 keys.  Dims
-          // 128jb.. are k-blocks 2jb, 2jb+1: pair blocks 2 (jb % 2) and the
-          // next, half jb / 2; keys 16kk.. are the 16 rows at 32kk + 16 half.
+      // PV issuer: PV(np) as soon as P(np) is written (S runs from warp 8)
+      for (int np = 0; np < n; ++np) {
+        wait(&aux->p_full[np & 1], (np >> 1) & 1);
+        if (*abort_flag) break;
+        tc::fence_after_sync();
+        const uint32_t vs = v_lo + (np % NT) * (kTileBytes / 16);
+        const uint32_t ps = p_lo + (np & 1) * (kPBytes / 16);
 #pragma unroll
-          for (int jb = 0; jb < KB / 2; ++jb) {
+        for (int jb = 0; jb < KB / 2; ++jb) {
 #pragma unroll
-            for (int kk = 0; kk < TK / 16; ++kk) {
-              const uint32_t off = (jb & 1) * 2 * kPairBytes + (jb >> 1) * 2048 + kk * 4096;
-              const uint64_t ad = tc::desc_pack(vs + off / 16, hi);
-              const uint64_t bd = tc::desc_pack(ps + (kk * 32) / 16, hi);
-              tc::mma_bf16(tmem + kColO + H * jb, ad, bd, kIdescPV, (np > 0 || kk > 0) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < TK / 16; ++kk) {
+            const uint32_t off = (jb & 1) * 2 * kPairBytes + (jb >> 1) * 2048 + kk * 4096;
+            const uint64_t ad = tc::desc_pack(vs + off / 16, hi);
+            const uint64_t bd = tc::desc_pack(ps + (kk * 32) / 16, hi);
+            tc::mma_bf16(tmem + kColO + H * jb, ad, bd, kIdescPV, (np > 0 || kk > 0) ? 1u : 0u);
           }
-          tc::mma_commit(smem_u32(&aux->empty[np % NT]));
-          tc::mma_commit(smem_u32(&aux->pv_done[np & 1]));
-          SA_TRACE(kTrPV, np);
-          ++np;
-          did = true;
-        } else if (ns < n && ns < np + NT && tc::mbar_test_wait(smem_u32(&aux->full[ns % NT]), (ns / NT) & 1) &&
-                   (ns == 0 || tc::mbar_test_wait(smem_u32(&aux->s_free), (ns - 1) & 1))) {
-          tc::fence_after_sync();
-          SA_TRACE(kTrMmaGot, ns);
-          const uint32_t ks0 = k_lo + (ns % NT) * (kTileBytes / 16);
-          // S(ns): 16 block-diagonal MMAs of M=128 x N=128 x K=16 over the
-          // four pair blocks; Q' column 32j + 8ks holds the same dims
-#pragma unroll
-          for (int j = 0; j < KB / 2; ++j) {
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t bd = tc::desc_pack(ks0 + (j * kPairBytes + ks * 32) / 16, hi);
-              tc::mma_bf16_ts(tmem + kColS, tmem + kColQ + 32 * j + 8 * ks, bd, kIdescS, (j | ks) ? 1u : 0u);
-            }
-          }
-          tc::mma_commit(smem_u32(&aux->s_full));
-          SA_TRACE(kTrS, ns);
-          ++ns;
-          did = true;
         }
-        if (did) {
-          last = clock64();
-        } else if (*abort_flag || clock64() - last > a.wait_limit) {
-          if (!*abort_flag && a.status) atomicOr(a.status, kStatusTimeout);
-          *abort_flag = 1;
-          break;
-        }
+        tc::mma_commit(smem_u32(&aux->empty[np % NT]));
+        tc::mma_commit(smem_u32(&aux->pv_done[np & 1]));
+        SA_TRACE(kTrPV, np);
       }
       // every MMA of this CTA has completed before TMEM is released
       tc::mma_commit(smem_u32(&aux->mma_done));
@@ -602,8 +568,38 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         }
       }
     }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ S issuer
+    q_part();
+    if (lane == 0 && n > 0) {
+      const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
+      const uint32_t k_lo = tc::desc_lo(sRing, 16);  // K-major: LBO unused
+      wait(&aux->q_full, 0);
+      tc::fence_after_sync();
+      for (int ns = 0; ns < n; ++ns) {
+        wait(&aux->full[ns % NT], (ns / NT) & 1);
+        if (ns > 0) wait(&aux->s_free, (ns - 1) & 1);
+        if (*abort_flag) break;
+        tc::fence_after_sync();
+        SA_TRACE(kTrMmaGot, ns);
+        const uint32_t ks0 = k_lo + (ns % NT) * (kTileBytes / 16);
+#pragma unroll
+        for (int j = 0; j < KB / 2; ++j) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t bd = tc::desc_pack(ks0 + (j * kPairBytes + ks * 32) / 16, hi);
+            tc::mma_bf16_ts(tmem + kColS, tmem + kColQ + 32 * j + 8 * ks, bd, kIdescS, (j | ks) ? 1u : 0u);
+          }
+        }
+        tc::mma_commit(smem_u32(&aux->s_full));
+        SA_TRACE(kTrS, ns);
+      }
+      tc::mma_commit(smem_u32(&aux->mma_done));
+      tc::mbar_wait(smem_u32(&aux->mma_done), 0, a.status, kStatusTimeout, a.wait_limit);
+    }
+    __syncwarp();
   } else {
-    // ------------------------------------------------------------ idle warps 8, 12
+    // ------------------------------------------------------------ idle warp 12
     q_part();
   }
   // -------------------------------------------------------------- O^T drain
