@@ -34,11 +34,12 @@
 //               cp.async.mbarrier.arrive.
 //   warp 8      S issuer (one thread): S(t) as soon as tile t has landed and
 //               the softmax has read S(t-1).
-//   warp 4      PV issuer (one thread): PV(t) as soon as P(t) is written (it
-//               frees the tile's slot).  The tensor pipe spends ~90 cycles
-//               on each of these MMAs whatever its shape, so a tile's 32
-//               MMAs bound the tile rate; two issuers keep both kinds queued
-//               (one ready-first issuer: ~3.1K cycles a tile, two: ~2.9K).
+//   warps 4, 12 PV issuers (one thread each, output dims 0-255 / 256-511):
+//               PV(t) as soon as P(t) is written (it frees the tile's slot
+//               once both halves completed).  A tcgen05.mma of these shapes
+//               costs ~90 cycles; issuing S and the two PV halves from three
+//               threads keeps them from queueing behind one another (one
+//               ready-first issuer: ~3.1K cycles a tile).
 //   warps 0-3   softmax.  Warp w owns heads 16w..16w+15: per 16 keys, two
 //               16x256b TMEM loads (the two dim halves) give thread i the
 //               scores of heads 16w + i/4 and 16w + 8 + i/4 for keys
@@ -79,10 +80,9 @@ constexpr int kTileBytes = KB * kSlabBytes;           // 64 KB
 // keys as 128 rows of 128 B: rows 32q..32q+15 = low half of keys
 // 16q..16q+15, rows 32q+16..32q+31 = their high half.
 constexpr int kPairBytes = 2 * kSlabBytes;            // 16 KB
-// 16 warps, four per scheduler (warp % 4): softmax 0-3, PV issuer 4, S
-// issuer 8, and the producers on the schedulers of warps 1-3 only (5-7,
-// 9-11, 13-15), so the issuers share their scheduler with one softmax warp;
-// warp 12 idles (it moves its part of Q' and joins the drain).
+// 16 warps, four per scheduler (warp % 4): softmax 0-3, PV issuers 4 and 12,
+// S issuer 8, and the producers on the schedulers of warps 1-3 only (5-7,
+// 9-11, 13-15), so the issuers share their scheduler with one softmax warp.
 constexpr int kProducerWarps = 9;
 constexpr int kMmaWarp = 4;
 constexpr int THREADS = 512;
@@ -248,15 +248,15 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     tc::mbar_init(smem_u32(&aux->q_full), THREADS);  // every thread stores its part of Q'
     for (int s = 0; s < NT; ++s) {
       tc::mbar_init(smem_u32(&aux->full[s]), 32 * kProducerWarps);  // one cp.async arrival per producer lane
-      tc::mbar_init(smem_u32(&aux->empty[s]), 1);
+      tc::mbar_init(smem_u32(&aux->empty[s]), 2);  // both PV issuers' commits
     }
     tc::mbar_init(smem_u32(&aux->s_full), 1);
     tc::mbar_init(smem_u32(&aux->s_free), 4);
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(smem_u32(&aux->p_full[s]), 1);
-      tc::mbar_init(smem_u32(&aux->pv_done[s]), 1);
+      tc::mbar_init(smem_u32(&aux->pv_done[s]), 2);
     }
-    tc::mbar_init(smem_u32(&aux->mma_done), 2);  // one commit from each issuer
+    tc::mbar_init(smem_u32(&aux->mma_done), 3);  // one commit from each issuer
     tc::mbar_fence_init();
   }
   // the barriers are initialised before any thread arrives on them (the
@@ -376,9 +376,11 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     }
     if (n < NT) q_part();
     cp_async_wait<0>();
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ PV issuer
+  } else if (warp == kMmaWarp || warp == 12) {
+    // ------------------------------------------------------------ PV issuers
+    // warp 4: output dims 0-255 (O^T blocks 0, 1), warp 12: dims 256-511
     q_part();
+    const int jb0 = warp == kMmaWarp ? 0 : 2;
     if (lane == 0 && n > 0) {
       const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
       const uint32_t v_lo = tc::desc_lo(sRing, kPairBytes);  // MN-major: LBO = the next 64 dims (next pair block)
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         const uint32_t vs = v_lo + (np % NT) * (kTileBytes / 16);
         const uint32_t ps = p_lo + (np & 1) * (kPBytes / 16);
 #pragma unroll
-        for (int jb = 0; jb < KB / 2; ++jb) {
+        for (int jb = jb0; jb < jb0 + 2; ++jb) {
 #pragma unroll
           for (int kk = 0; kk < TK / 16; ++kk) {
             const uint32_t off = (jb & 1) * 2 * kPairBytes + (jb >> 1) * 2048 + kk * 4096;
@@ -404,7 +406,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         }
         tc::mma_commit(smem_u32(&aux->empty[np % NT]));
         tc::mma_commit(smem_u32(&aux->pv_done[np & 1]));
-        SA_TRACE(kTrPV, np);
+        if (jb0 == 0) SA_TRACE(kTrPV, np);
       }
       // every MMA of this CTA has completed before TMEM is released
       tc::mma_commit(smem_u32(&aux->mma_done));
@@ -598,9 +600,6 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tc::mbar_wait(smem_u32(&aux->mma_done), 0, a.status, kStatusTimeout, a.wait_limit);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ idle warp 12
-    q_part();
   }
   // -------------------------------------------------------------- O^T drain
   // Every warp drains part of O^T: warp w reads TMEM lanes 32 (w % 4).. (its
