@@ -739,16 +739,25 @@ PROJECTIONS = (("wq_a", 1024, 4096, 1), ("wq_b", 32768, 1024, 1), ("wkv", 512, 4
                ("compressor wkv|wgate", 2048, 4096, 1), ("indexer compressor wkv|wgate", 512, 4096, 1),
                ("indexer wq_b + q rotary", 8192, 1024, 1), ("weights_proj", 64, 4096, 1),
                ("wo_a (8 groups)", 8192, 4096, 8), ("wo_b", 4096, 8192, 1))
+# the launches DeviceAttention runs them as: the projections of x in one
+# weight, those of q_lora in another (the indexer's q rotary on its columns),
+# then wo_a and wo_b: (name, rows, K, groups, rotary start column or None)
+PROJECTION_LAUNCHES = (("x: wq_a|wkv|compressor wkv|wgate|indexer compressor wkv|wgate|weights_proj",
+                        1024 + 512 + 2048 + 512 + 64, 4096, 1, None),
+                       ("q_lora: wq_b|indexer wq_b + q rotary", 32768 + 8192, 1024, 1, 32768),
+                       ("wo_a (8 groups)", 8192, 4096, 8, None), ("wo_b", 4096, 8192, 1, None))
 
 
 def projections_record(args, dev, reps=10, copies=4):
     """The projections either side of the path (the step before it and the
-    one after) through dsa_linear at config-2's batch.  `copies` layers'
-    worth of projections with their own weights (so nothing is re-read from
-    L2) run back to back from one CUDA graph; the time per layer is the
-    graph's CUDA-event time over `copies`, median of `reps`.  The same chain
-    per projection gives each one's time.  cuBLAS (torch.matmul / bmm) on the
-    same operands, chained the same way, is the library reference point."""
+    one after) through dsa_linear at config-2's batch, in the launches the
+    block runs them as (PROJECTION_LAUNCHES: the projections sharing an
+    input stored as one weight).  `copies` layers' worth with their own
+    weights (so nothing is re-read from L2) run back to back from one CUDA
+    graph; the time per layer is the graph's CUDA-event time over `copies`,
+    median of `reps`.  cuBLAS (torch.matmul / bmm) on the same operands is
+    the library reference point, both as the reference's nine matmuls and
+    as the same four merged ones."""
     import torch
     from dsv4attn import ops
     B = args.batch
@@ -759,24 +768,28 @@ def projections_record(args, dev, reps=10, copies=4):
     sin = torch.rand(args.ctx + 8, 32, device=dev, generator=g)
     pos = torch.full((B,), args.ctx - 1, dtype=torch.int32, device=dev)
 
-    layers = []
-    for _ in range(copies):
-        ents = []
-        for name, NT, K, G in PROJECTIONS:
-            w = (torch.randn(NT, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
-            x = torch.randn(B, G * K, device=dev, generator=g).to(torch.bfloat16)
-            y = torch.empty(B, NT, dtype=torch.bfloat16, device=dev)
-            rope = (cos, sin, pos, 128, 64) if "rotary" in name else None
-            ents.append((name, NT, K, G, w, ops.pack_linear_weight(w, groups=G), x, y, rope))
-        layers.append(ents)
+    def operands(table):
+        layers = []
+        for _ in range(copies):
+            ents = []
+            for ent in table:
+                name, NT, K, G = ent[:4]
+                col0 = ent[4] if len(ent) > 4 else None
+                w = (torch.randn(NT, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+                x = torch.randn(B, G * K, device=dev, generator=g).to(torch.bfloat16)
+                y = torch.empty(B, NT, dtype=torch.bfloat16, device=dev)
+                rope = (cos, sin, pos, 128, 64, col0) if col0 is not None else None
+                ents.append((name, NT, K, G, w, ops.pack_linear_weight(w, groups=G), x, y, rope))
+            layers.append(ents)
+        return layers
 
-    def native(only=None):
+    def native(layers, only=None):
         for ents in layers:
             for name, NT, K, G, w, wp, x, y, rope in ents:
                 if only is None or name == only:
                     ops.linear(x, wp, out=y, rope=rope)
 
-    def cublas(only=None):
+    def cublas(layers, only=None):
         for ents in layers:
             for name, NT, K, G, w, wp, x, y, rope in ents:
                 if only is not None and name != only:
@@ -810,22 +823,30 @@ def projections_record(args, dev, reps=10, copies=4):
         del graph
         return sorted(ts)[len(ts) // 2]
 
+    merged = operands(PROJECTION_LAUNCHES)
     rows, tot_bytes = {}, 0
-    for name, NT, K, G in PROJECTIONS:
+    for name, NT, K, G, _ in PROJECTION_LAUNCHES:
         nbytes = NT * K * 2 + B * G * K * 2 + B * NT * 2
-        t = per_layer_us(lambda: native(name))
-        t_lib = per_layer_us(lambda: cublas(name))
+        t = per_layer_us(lambda: native(merged, name))
+        t_lib = per_layer_us(lambda: cublas(merged, name))
         rows[name] = {"us": round(t, 2), "gbs": round(nbytes / t / 1e3, 1), "cublas_us": round(t_lib, 2)}
         tot_bytes += nbytes
-    tot = per_layer_us(native)
-    tot_lib = per_layer_us(cublas)
-    del layers
+    tot = per_layer_us(lambda: native(merged))
+    tot_lib_merged = per_layer_us(lambda: cublas(merged))
+    del merged
+    torch.cuda.empty_cache()
+    separate = operands(PROJECTIONS)
+    tot_lib = per_layer_us(lambda: cublas(separate))
+    tot_sep = per_layer_us(lambda: native(separate))
+    del separate
     torch.cuda.empty_cache()
     return {"batch": B, "us_per_layer": round(tot, 2), "cublas_us_per_layer": round(tot_lib, 2),
+            "cublas_merged_us_per_layer": round(tot_lib_merged, 2), "native_separate_us_per_layer": round(tot_sep, 2),
             "bytes_per_layer": tot_bytes, "gbs": round(tot_bytes / tot / 1e3, 1),
             "frac": round(tot_bytes / tot / 1e3 / hbm, 4), "peak": hbm,
             "timing": f"graph of {copies} layers' projections with their own weights, back to back; "
-                      f"median of {reps}; bytes = weights + activations in + result out",
+                      f"median of {reps}; bytes = weights + activations in + result out; native = the four "
+                      "launches DeviceAttention runs; cublas = the reference's nine matmuls",
             "kernels": rows}
 
 

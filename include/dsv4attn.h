@@ -62,9 +62,11 @@ long long dsa_get_wait_limit(void);
  * dsa_linear_pack (16-byte aligned).
  * Y [B, ld_y]: bf16, or with out_f32 the fp32 value of the bf16 result.
  * rope_dim > 0: interleaved rotary (pairs 2i, 2i+1) on the last rope_dim
- * columns of every head_dim block of Y, applied to the bf16 product with
- * cos/sin [n_pos, rope_dim/2] fp32 at position pos[b] and rounded again;
- * positions outside [0, n_pos) are clamped and set status bit 1.
+ * columns of every head_dim block of columns [rope_col0, N) of each group of
+ * Y (rope_col0 = 0: all of it; > 0: two projections of one input stored as
+ * one weight, the second rotated), applied to the bf16 product with cos/sin
+ * [n_pos, rope_dim/2] fp32 at position pos[b] and rounded again; positions
+ * outside [0, n_pos) are clamped and set status bit 1.
  * Replaces the reference's DeviceColLinear / DeviceRowLinear matmuls at the
  * path's edges: the fused compressor wkv || wgate (inference.py:4954-4966),
  * the indexer's wq_b + rotary Lk-D-idx-q kernel and weights_proj
@@ -72,7 +74,7 @@ long long dsa_get_wait_limit(void);
  * wo_a (G groups) and wo_b (6096-6126). */
 int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, void* y, int64_t ld_y, int B, int N, int K,
                int G, int out_f32, const float* cos, const float* sin, int n_pos, const int32_t* pos,
-               int head_dim, int rope_dim, int32_t* status, dsa_stream_t stream);
+               int head_dim, int rope_dim, int rope_col0, int32_t* status, dsa_stream_t stream);
 
 /* Bytes of the tile layout of a W [G*N, K] (0 for invalid sizes): G x
  * ceil(N/128) x K/64 tiles of 16 KB. */

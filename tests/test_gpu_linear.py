@@ -147,3 +147,24 @@ def test_linear_rejects_bad_shapes(cuda_dev):
     with pytest.raises(ValueError):
         ops.linear(torch.ones(2, 128, dtype=BF, device=cuda_dev), torch.ones(64, 64, dtype=BF, device=cuda_dev),
                    groups=3)
+
+
+@pytest.mark.parametrize("B,N0,H,Dh,rd,K", [(64, 512, 4, 128, 64, 256), (3, 1024, 2, 128, 64, 128)])
+def test_linear_rotary_from_column_bit_exact(cuda_dev, B, N0, H, Dh, rd, K):
+    """Two projections of one input stored as one weight, the rotary on the
+    second only (rope col0 = N0, the attention's wq_b next to the indexer's
+    wq_b): columns before col0 untouched, the rest bit-exact against the
+    oracle's rotary of the kernel's own unrotated result."""
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B + N0)
+    cos, sin = O.rope_tables(rd, 2048, compressed=True)
+    pos = torch.randint(0, 2048, (B,), generator=g, dtype=torch.int32)
+    x = torch.randn(B, K, generator=g).to(BF).to(cuda_dev)
+    w = (torch.randn(N0 + H * Dh, K, generator=g) * K ** -0.5).to(BF).to(cuda_dev)
+    wp = ops.pack_linear_weight(w)
+    plain = ops.linear(x, wp)
+    roped = ops.linear(x, wp, rope=(cos.to(cuda_dev), sin.to(cuda_dev), pos.to(cuda_dev), Dh, rd, N0))
+    torch.cuda.synchronize()
+    assert torch.equal(roped[:, :N0].cpu(), plain[:, :N0].cpu())
+    want = O.head_norm_rope(plain[:, N0:].cpu(), H, Dh, cos[pos.long()], sin[pos.long()], rope_dim=rd, norm=False)
+    assert torch.equal(roped[:, N0:].cpu().view(torch.int16), want.view(torch.int16))

@@ -229,9 +229,19 @@ def test_device_indexer_score_matches_oracle(cuda_dev):
 
 # -------------------------------------------------------- DeviceAttention
 
-def _block_run(cuda_dev, attn, bw, st, positions, B, seed):
+def _block_run(cuda_dev, attn, bw, st, positions, B, seed, merged=True):
     M = _modules()
+    if not merged:
+        # twins bound beforehand (as the reference's offload binds them): the
+        # block then runs every projection separately
+        comp, ind = attn.compressor, attn.indexer
+        attn._device_compressor = M.DeviceCompressor(cuda_dev, comp, M.DeviceLinear(cuda_dev, comp.wkv),
+                                                     M.DeviceLinear(cuda_dev, comp.wgate), None)
+        ic = ind.compressor
+        attn._device_indexer = M.DeviceIndexer(cuda_dev, ind, M.DeviceCompressor(
+            cuda_dev, ic, M.DeviceLinear(cuda_dev, ic.wkv), M.DeviceLinear(cuda_dev, ic.wgate), None))
     da = M.DeviceAttention(cuda_dev, attn, max_seq_len=st.cos.shape[0])
+    assert (da._merged is not None) == merged
     g = torch.Generator().manual_seed(seed)
     for pos in positions:
         x = torch.randn(B, 1, attn.dim, generator=g).to(BF16)
@@ -248,6 +258,14 @@ def test_device_attention_block_first_steps(cuda_dev):
     B = 2
     attn, bw, st = make_block(seed=11, B=B)
     _block_run(cuda_dev, attn, bw, st, range(0, 10), B, 1)
+
+
+def test_device_attention_block_separate_projections(cuda_dev):
+    """The same block with its compressor / indexer twins bound beforehand:
+    nine separate projection launches instead of the merged ones."""
+    B = 2
+    attn, bw, st = make_block(seed=11, B=B)
+    _block_run(cuda_dev, attn, bw, st, range(0, 6), B, 1, merged=False)
 
 
 def test_device_attention_block_prefilled_selection(cuda_dev):

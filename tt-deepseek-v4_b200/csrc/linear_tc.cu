@@ -94,6 +94,7 @@ struct Args {
   int n_pos;
   const int32_t* pos;
   int head_dim, rope_dim;
+  int rope_col0;             // the rotary covers columns >= rope_col0 of each group, head blocks from there
   int32_t* status;
   long long wait_limit;
 };
@@ -401,8 +402,9 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const Args a,
       const int n = t * TILE_N + nr;  // this thread's weight row
       const bool n_ok = n < a.N;
       // rotary: the interleaved pair (n, n ^ 1) of a rope column of a head
-      const int hd = a.head_dim > 0 ? n % a.head_dim : 0;
-      const bool rope = a.rope_dim > 0 && hd >= a.head_dim - a.rope_dim;
+      const int nn = n - a.rope_col0;
+      const int hd = (a.head_dim > 0 && nn >= 0) ? nn % a.head_dim : 0;
+      const bool rope = a.rope_dim > 0 && nn >= 0 && n < a.N && hd >= a.head_dim - a.rope_dim;
       const int kpair = (hd - (a.head_dim - a.rope_dim)) >> 1;
       const int64_t col = int64_t(g) * a.N + n;
       // the previous item's Y tile has left the staging buffer
@@ -603,7 +605,8 @@ extern "C" int dsa_linear_pack(const void* w, int N, int K, int G, void* packed,
 
 extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, void* y, int64_t ld_y, int B, int N,
                           int K, int G, int out_f32, const float* cos, const float* sin, int n_pos,
-                          const int32_t* pos, int head_dim, int rope_dim, int32_t* status, dsa_stream_t stream) {
+                          const int32_t* pos, int head_dim, int rope_dim, int rope_col0, int32_t* status,
+                          dsa_stream_t stream) {
   clear_error();
   DSA_CHECK_ARG(x && w_packed && y, "linear: null x/w/y");
   DSA_CHECK_ARG(B >= 0 && N > 0 && K > 0 && G >= 1, "linear: bad B/N/K/G");
@@ -615,8 +618,9 @@ extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, voi
   if (rope_dim > 0) {
     DSA_CHECK_ARG(cos && sin && pos && n_pos > 0, "linear: rotary needs cos/sin tables and positions");
     DSA_CHECK_ARG(head_dim > 0 && rope_dim % 2 == 0 && rope_dim <= head_dim && head_dim % 32 == 0 &&
-                      N % head_dim == 0,
-                  "linear: rotary needs head_dim | N, head_dim a multiple of 32, an even rope_dim <= head_dim");
+                      rope_col0 >= 0 && rope_col0 % 2 == 0 && rope_col0 < N && (N - rope_col0) % head_dim == 0,
+                  "linear: rotary needs head_dim | N - rope_col0 (rope_col0 even), head_dim a multiple of 32, "
+                  "an even rope_dim <= head_dim");
   }
   if (B == 0) return DSA_OK;
   static int attr_dev[64] = {};
@@ -690,6 +694,7 @@ extern "C" int dsa_linear(const void* x, int64_t ld_x, const void* w_packed, voi
     a.pos = pos ? pos + b0 : nullptr;
     a.head_dim = rope_dim > 0 ? head_dim : 0;
     a.rope_dim = rope_dim > 0 ? rope_dim : 0;
+    a.rope_col0 = rope_dim > 0 ? rope_col0 : 0;
     a.status = status;
     a.wait_limit = wait_limit_cycles();
     if (n_cl <= 0 || a.n_stages < 2 || a.aux_off + lin::kAuxBytes + 1024 > uint32_t(lin::kSmemBytes)) {

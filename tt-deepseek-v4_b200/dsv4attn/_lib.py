@@ -33,7 +33,7 @@ PROTOTYPES = {
     "dsa_last_error": (ctypes.c_char_p, []),
     "dsa_set_wait_limit": (I32, [ctypes.c_longlong]),
     "dsa_get_wait_limit": (ctypes.c_longlong, []),
-    "dsa_linear": (I32, [P, I64, P, P, I64, I32, I32, I32, I32, I32, P, P, I32, P, I32, I32, P, P]),
+    "dsa_linear": (I32, [P, I64, P, P, I64, I32, I32, I32, I32, I32, P, P, I32, P, I32, I32, I32, P, P]),
     "dsa_linear_packed_bytes": (ctypes.c_size_t, [I32, I32, I32]),
     "dsa_linear_pack": (I32, [P, I32, I32, I32, P, ctypes.c_size_t, P]),
     "dsa_act_quant_block": (I32, [P, P, P, P, I64, I64, I64, I64, I32, F32, F32, P]),

@@ -433,10 +433,18 @@ class DeviceIndexer(torch.nn.Module):
                                      status=self.status).reshape(B, H * Di)
         self.dc.forward_device(x_tt, B, start_pos, start_pos_tt)
         w = self.weights_proj.forward_device(x_tt).reshape(B, H).float().contiguous()
+        return self.score_rows(q, w, B, t_valid)
+
+    def score_rows(self, q_roped, w, B: int, t_valid=None):
+        """The score stage after the projections and the compressor step:
+        q_roped [B, H*Di] bf16 (wq_b output with the q rotary), w [B, H] fp32
+        (weights_proj with its scale).  Returns score [B, 1, T]."""
+        H, Di = self.n_heads, self.head_dim
         cache = self.dc.kv_cache_tt
         T = cache.shape[1]
         score = self._score_buf(B, T)
-        ops.indexer_score(q.view(B, H, Di), cache, w, T, out=score, t_valid=t_valid)
+        ops.indexer_score(q_roped.reshape(B, H, Di).contiguous(), cache, w.reshape(B, H).float().contiguous(), T,
+                          out=score, t_valid=t_valid)
         return score.view(B, 1, T)
 
 
@@ -503,16 +511,29 @@ class DeviceAttention(torch.nn.Module):
         if kv_shape[2] != self.head_dim:
             raise ValueError(f"attn.kv_cache last dim {kv_shape[2]} != head_dim {self.head_dim}")
         self.kv_cache_size = kv_shape[1]
+        made_comp = made_ind = False
         if self.compress_ratio:
             if getattr(attn, "_device_compressor", None) is None:
                 comp = attn.compressor
                 attn._device_compressor = DeviceCompressor(
                     dev, comp, DeviceLinear(dev, comp.wkv), DeviceLinear(dev, comp.wgate), None)
+                made_comp = True
             ind = getattr(attn, "indexer", None)
             if ind is not None and getattr(attn, "_device_indexer", None) is None:
                 ic = ind.compressor
                 idc = DeviceCompressor(dev, ic, DeviceLinear(dev, ic.wkv), DeviceLinear(dev, ic.wgate), None)
                 attn._device_indexer = DeviceIndexer(dev, ind, idc)
+                made_ind = True
+        # The projections that read the same input run as one launch each
+        # when this block built its compressor and indexer twins from the CPU
+        # modules (their weights are then known): x -> wq_a | wkv | compressor
+        # wkv | wgate | indexer compressor wkv | wgate | weights_proj (scaled
+        # as DeviceIndexer scales it), and q_lora -> wq_b | indexer wq_b with
+        # the indexer's q rotary on its columns.  Same values as the separate
+        # projections (each output column is the same dot product).
+        self._merged = None
+        if made_comp and made_ind:
+            self._merged = self._merge_projections(dev, attn, attn.compressor, attn.indexer)
         di = self.device_indexer
         # the indexer's compressor writes into the indexer's own key cache
         # (inference.py:5113-5122) unless it was given one
@@ -521,6 +542,21 @@ class DeviceAttention(torch.nn.Module):
         self.kv_cache_tt = None
         self._indexer_score_in_tt = None
         self._alloc_decode_tensors()
+
+    def _merge_projections(self, dev, attn, comp, ind):
+        ic = ind.compressor
+        wscale = float(ind.softmax_scale) * int(ind.n_heads) ** -0.5
+        wproj = (weight_bf16(ind.weights_proj).float() * wscale).to(BF16)
+        xs = [weight_bf16(attn.wq_a), weight_bf16(attn.wkv), weight_bf16(comp.wkv), weight_bf16(comp.wgate),
+              weight_bf16(ic.wkv), weight_bf16(ic.wgate), wproj]
+        qs = [weight_bf16(attn.wq_b), weight_bf16(ind.wq_b)]
+        if len({w.shape[1] for w in xs}) != 1 or len({w.shape[1] for w in qs}) != 1:
+            return None
+        cuts = [0]
+        for w in xs:
+            cuts.append(cuts[-1] + w.shape[0])
+        return {"x": ops.pack_linear_weight(torch.cat(xs, 0).to(dev).contiguous()), "x_cuts": cuts,
+                "q": ops.pack_linear_weight(torch.cat(qs, 0).to(dev).contiguous()), "q_cut": qs[0].shape[0]}
 
     @property
     def device_compressor(self):
@@ -610,14 +646,33 @@ class DeviceAttention(torch.nn.Module):
         pos = self._pos_tt if not (isinstance(start_pos_tt, torch.Tensor) and start_pos_tt.numel() == B
                                    and start_pos_tt.dtype == I32 and start_pos_tt.is_cuda) else start_pos_tt
         x2 = x_tt.reshape(B, self.dim)
-        # q path: wq_a -> q_norm -> wq_b -> per-head rms (weight = softmax_scale) -> rotary
-        q_lora = wq_a_out_tt.reshape(B, self.q_lora_rank) if wq_a_out_tt is not None else self.wq_a(x2)
-        qr = ops.head_norm_rope(q_lora, 1, self.q_lora_rank, gamma=self.q_norm_gamma, eps=self.eps)
-        q = self.wq_b(qr)
-        ops.head_norm_rope(q, H, D, self.cos, self.sin, pos, rope_dim=rd, weight=self.softmax_scale, eps=self.eps,
-                           out=q, status=self.status)
+        mg = self._merged if wq_a_out_tt is None and di is not None and dc is not None else None
+        if mg is not None:
+            # the projections of x in one launch; slices are strided views
+            xp = ops.linear(x2.to(BF16).contiguous(), mg["x"])
+            c = mg["x_cuts"]
+            q_lora, kv = xp[:, c[0]:c[1]], xp[:, c[1]:c[2]]
+            c_rows = (xp[:, c[2]:c[3]], xp[:, c[3]:c[4]])
+            i_rows = (xp[:, c[4]:c[5]], xp[:, c[5]:c[6]])
+            iw = xp[:, c[6]:c[7]]
+            qr = ops.head_norm_rope(q_lora, 1, self.q_lora_rank, gamma=self.q_norm_gamma, eps=self.eps)
+            # wq_b and the indexer's wq_b in one launch, the indexer q rotary on its columns
+            ipos = di.dc._pos_for(pos, B)
+            qp = ops.linear(qr, mg["q"], rope=(di.cos, di.sin, ipos, di.head_dim, di.rope_head_dim, mg["q_cut"]),
+                            status=di.status)
+            q = ops.head_norm_rope(qp[:, :mg["q_cut"]], H, D, self.cos, self.sin, pos, rope_dim=rd,
+                                   weight=self.softmax_scale, eps=self.eps, status=self.status)
+            iq = qp[:, mg["q_cut"]:]
+        else:
+            # q path: wq_a -> q_norm -> wq_b -> per-head rms (weight = softmax_scale) -> rotary
+            q_lora = wq_a_out_tt.reshape(B, self.q_lora_rank) if wq_a_out_tt is not None else self.wq_a(x2)
+            qr = ops.head_norm_rope(q_lora, 1, self.q_lora_rank, gamma=self.q_norm_gamma, eps=self.eps)
+            q = self.wq_b(qr)
+            ops.head_norm_rope(q, H, D, self.cos, self.sin, pos, rope_dim=rd, weight=self.softmax_scale,
+                               eps=self.eps, out=q, status=self.status)
         # kv path + window write (Lk-D1 + attn.kv_update)
-        kv = self.wkv(x2)
+        if mg is None:
+            kv = self.wkv(x2)
         ops.kv_norm_rope_window_write(kv, self.kv_norm_gamma, self.cos, self.sin, pos, self.kv_cache_tt, W,
                                       eps=self.eps, rope_dim=rd, status=self.status)
         # indices: window ring, then the indexer's top-k
@@ -626,7 +681,11 @@ class DeviceAttention(torch.nn.Module):
         T_active = (start_pos + 1) // self.compress_ratio if self.compress_ratio else 0
         if self.compress_ratio and T_active > 0:
             if di is not None:
-                score = di.forward_device_score(x2, qr, B, start_pos, pos, t_valid=self._t_active_tt)
+                if mg is not None:
+                    di.dc.step_rows(i_rows[0], i_rows[1], B, start_pos, pos)
+                    score = di.score_rows(iq, iw, B, t_valid=self._t_active_tt)
+                else:
+                    score = di.forward_device_score(x2, qr, B, start_pos, pos, t_valid=self._t_active_tt)
                 self._indexer_score_in_tt = score
                 bucket = min(pick_indexer_topk_bucket(T_active), score.shape[-1])
                 k_fixed = min(di.index_topk, bucket)
@@ -636,7 +695,10 @@ class DeviceAttention(torch.nn.Module):
                 parts.append(ramp.unsqueeze(0).expand(B, T_active))
         idx = torch.cat(parts, dim=-1).contiguous() if len(parts) > 1 else win_idx
         if self.compress_ratio:
-            dc.forward_device(x2, B, start_pos, pos)
+            if mg is not None:
+                dc.step_rows(c_rows[0], c_rows[1], B, start_pos, pos)
+            else:
+                dc.forward_device(x2, B, start_pos, pos)
         K = idx.shape[-1]
         idxs_tt, valid_tt = self.sparse_attn_dev._idxs_int_tile_to_idxs_and_mask(idx, B, 1, K)
         o = self.sparse_attn_dev.forward_device(q.view(B, 1, H, D), self.kv_cache_tt, idxs_tt, valid_tt, 1, K)

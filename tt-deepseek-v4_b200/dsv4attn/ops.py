@@ -139,8 +139,9 @@ def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, groups: int = 1,
     LinearWeight (its groups win over ``groups``) or W [G*N, K] bf16, which is
     packed for this call, K a multiple of 64 -> y [B, G*N] bf16, or fp32 of
     the bf16 value with ``out_f32``.  ``rope=(cos, sin, pos, head_dim,
-    rope_dim)``: interleaved rotary on the last rope_dim columns of every
-    head_dim block, at per-row positions ``pos`` [B] int32."""
+    rope_dim[, col0])``: interleaved rotary on the last rope_dim columns of
+    every head_dim block of columns [col0, N) (default 0), at per-row
+    positions ``pos`` [B] int32."""
     _need(x, "x", BF16)
     if not isinstance(w, LinearWeight):
         w = pack_linear_weight(w, groups)
@@ -158,9 +159,10 @@ def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, groups: int = 1,
     if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] < B or out.shape[1] < GN:
         raise ValueError("out must be [B, G*N] with contiguous rows")
     cos = sin = pos = None
-    n_pos = head_dim = rope_dim = 0
+    n_pos = head_dim = rope_dim = col0 = 0
     if rope is not None:
-        cos, sin, pos, head_dim, rope_dim = rope
+        cos, sin, pos, head_dim, rope_dim = rope[:5]
+        col0 = rope[5] if len(rope) > 5 else 0
         _need(cos, "cos", F32)
         _need(sin, "sin", F32)
         _need(pos, "pos", I32)
@@ -171,7 +173,7 @@ def linear(x: torch.Tensor, w, out: torch.Tensor | None = None, groups: int = 1,
         _contig(sin, "sin")
         n_pos = cos.shape[0]
     check(lib().dsa_linear(x.data_ptr(), x.stride(0), w.packed.data_ptr(), out.data_ptr(), out.stride(0), B, N, K,
-                           groups, int(out_f32), _ptr(cos), _ptr(sin), n_pos, _ptr(pos), head_dim, rope_dim,
+                           groups, int(out_f32), _ptr(cos), _ptr(sin), n_pos, _ptr(pos), head_dim, rope_dim, col0,
                            _ptr(status), _stream(x)), "linear")
     return out
 
