@@ -554,8 +554,11 @@ int max_clusters(int C) {
   return cache[dev][C] > 0 ? cache[dev][C] : 0;
 }
 
-// the split with the fewest k-blocks on the busiest CTA (+ a fixed cost per
-// item and per reduction), among those whose clusters fit
+// the split with the fewest k-blocks on the busiest CTA, counting a fixed
+// cost per item (2 k-blocks: set-up and epilogue) and per split reduction
+// (3 more: the partial exchange and the owners' sums), among the splits
+// whose clusters fit.  Measured on B200 at B = 64: 40960 x 1024 (320 items)
+// 24.6 us unsplit against 28.8 us with C = 2 (5 waves of 74 clusters).
 int pick_split(int items, int nkb) {
   int best = 1;
   long best_cost = -1;
@@ -565,7 +568,7 @@ int pick_split(int items, int nkb) {
     const int n_cl = std::min(items, mc);
     const long waves = (items + n_cl - 1) / n_cl;
     const long per = (nkb + C - 1) / C;
-    const long cost = waves * (per + 2) + (C > 1 ? 1 : 0);
+    const long cost = waves * (per + 2 + (C > 1 ? 3 : 0));
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = C;
