@@ -242,6 +242,10 @@ def time_kernels(path, inputs, outs, reps=3):
                                                     t_valid=path.t_active) for L, x in zip(path.layers, inputs)])
     run("indexer_topk", lambda: [ops.indexer_topk(L.score, path.t_active, L.k, L.win, T=L.T_max, mask_mode=1,
                                                   out=L.idx[:, L.win:], ws=L.ws) for L in path.layers])
+    # the newest row's score: the step runs it on the compressor's branch,
+    # beside indexer_score
+    run("indexer_score_newest", lambda: [ops.indexer_score_newest(x.iq, L.idx_cache, x.iw, path.t_active, L.T_max,
+                                                                  out=L.score) for L, x in zip(path.layers, inputs)])
     return res
 
 

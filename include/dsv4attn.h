@@ -227,6 +227,19 @@ int dsa_indexer_score_ex(const void* q, const void* k, const float* w, float* sc
                          const int32_t* t_valid, int B, int H, int Di, int T,
                          int64_t k_bstride, int64_t ld_score, int flags, dsa_stream_t stream);
 
+/* The score of each sequence's newest live compressed row: for each b with
+ * t = min(t_active[b], T) - 1 >= 0, score[b * ld_score + t] = sum_h w[b, h]
+ * relu(q[b, h, :] . k[b * k_bstride + t * 128 + :]) (the score stage of
+ * inference.py:5260-5275 for that one row; H = 64, Di = 128; q, k and the
+ * row stride 8-byte aligned).  A decode step scores the rows before the
+ * newest (dsa_indexer_score_ex with t_valid = t_active - 1) while the
+ * indexer compressor may write the newest row, and calls this after the
+ * compressor on the compressor's stream; the plain top-k then reads every
+ * live score.  Bit-identical to the recompute of dsa_indexer_topk_newest. */
+int dsa_indexer_score_newest(const void* q, const void* k, int64_t k_bstride, const float* w,
+                             const int32_t* t_active, float* score, int64_t ld_score, int B, int T,
+                             dsa_stream_t stream);
+
 /* Top-k of the masked indexer score, the reference's bucketed pad+mask
  * path (inference.py:5823-5851): masked = s - 1e4 * (t >= t_active[b]);
  * select the k largest of masked[b, 0:T]; out = t + win where

@@ -393,3 +393,70 @@ def test_sparse_attn_ex_rejects_bad_lead(cuda_dev):
     rc = L.dsa_sparse_attn_ex(q.data_ptr(), kv.data_ptr(), 300 * 512, 300, idx.data_ptr(), 64, sink.data_ptr(),
                               out.data_ptr(), None, 1, 1, 64, 512, 64, 0.05, None, 0, 128, 1, None, None)
     assert rc != 0 and "lead_cols" in _lib.last_error()
+
+
+@pytest.mark.parametrize("kind", ["gauss", "ties", "const_rows", "wide", "nan", "short"])
+def test_topk_position_order_equals_sorted_selection(cuda_dev, kind):
+    # the position-order top-k (one row per CTA, its own first level) and
+    # the sorted top-k (the general select) pick exactly the same indices:
+    # the k largest, ties to the lowest positions -- no near-tie allowance.
+    # Rows the position-order kernel hands to the general select (constant
+    # rows, huge ranges, NaN, fewer than k live entries) included.
+    from dsv4attn import ops
+    B, T, k, W = 24, 9216, 2048, 128
+    g = torch.Generator().manual_seed(hash(kind) % 1000)
+    s = torch.randn(B, T, generator=g) * (0.8 + torch.rand(B, 1, generator=g)) + 3 * (torch.rand(B, 1, generator=g) - .5)
+    if kind == "ties":
+        s = torch.floor(s * 4) / 4
+    elif kind == "const_rows":
+        s[::3] = 1.0
+    elif kind == "wide":
+        s[:, ::7] = 1e30
+    elif kind == "nan":
+        s[::5, 17] = float("nan")
+    ta = torch.randint(k, T + 1, (B,), generator=g, dtype=torch.int32)
+    if kind == "short":
+        ta = torch.randint(1, k, (B,), generator=g, dtype=torch.int32)
+    sd, tad = s.to(cuda_dev), ta.to(cuda_dev)
+    pos_order = ops.indexer_topk(sd, tad, k, W, mask_mode=1).cpu()
+    srt = ops.indexer_topk(sd, tad, k, W, mask_mode=1, sort_desc=True).cpu()
+    for b in range(B):
+        a = sorted(int(v) for v in pos_order[b] if v >= 0)
+        c = sorted(int(v) for v in srt[b] if v >= 0)
+        assert a == c, f"{kind} row {b}"
+        assert int((pos_order[b] < 0).sum()) == int((srt[b] < 0).sum())
+
+
+@pytest.mark.parametrize("B,T", [(64, 9216), (3, 20000), (5, 640)])
+def test_indexer_score_newest_matches_refresh(cuda_dev, B, T):
+    # the newest live row's score written by its own kernel (the decode
+    # step's side branch) is the value the top-k's refresh recomputes: the
+    # plain top-k then selects exactly what the refresh top-k selects; only
+    # entry t_active - 1 of each row is written
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B + T)
+    k = min(512, T)
+    q = torch.randn(B, 64, 128, generator=g).to(torch.bfloat16).to(cuda_dev)
+    kc = torch.randn(B, T, 128, generator=g).to(torch.bfloat16).to(cuda_dev)
+    w = (0.02 * torch.randn(B, 64, generator=g)).to(cuda_dev)
+    ta = torch.randint(1, T + 1, (B,), generator=g, dtype=torch.int32)
+    ta[0] = T
+    tad = ta.to(cuda_dev)
+    score = torch.full((B, T), 123.0, device=cuda_dev)
+    ops.indexer_score(q, kc, w, T, out=score, t_valid=tad - 1)
+    before = score.clone()
+    ops.indexer_score_newest(q, kc, w, tad, T, out=score)
+    ws = ops.Workspace(cuda_dev, int(ops.lib().dsa_indexer_topk_workspace_size(B, T, k)) or 16)
+    plain = ops.indexer_topk(score, tad, k, 128, T=T, mask_mode=1, ws=ws)
+    refreshed = ops.indexer_topk(before, tad, k, 128, T=T, mask_mode=1, ws=ws, refresh=(q, kc, w))
+    torch.cuda.synchronize()
+    assert torch.equal(plain.cpu(), refreshed.cpu())
+    changed = (score != before).cpu()
+    rows = torch.arange(B)
+    assert bool(changed[rows, (ta - 1).long()].all())
+    changed[rows, (ta - 1).long()] = False
+    assert not bool(changed.any())
+    want = O.indexer_score(q.cpu(), kc.cpu(), w.cpu())
+    got = score.cpu()[rows, (ta - 1).long()]
+    torch.testing.assert_close(got, want[rows, (ta - 1).long()], rtol=1e-3,
+                               atol=1e-3 * float(want.abs().max()))

@@ -13,11 +13,34 @@
 #include "common.cuh"
 #include "indexer_tc.cuh"
 #include "indexer_prefill_tc.cuh"
+#include "indexer_row.cuh"
 
 namespace dsa {
 
 constexpr int kIdxH = 64;        // indexer heads
 constexpr int kIdxD = 128;       // indexer head dim
+
+// The score of each sequence's newest live key row, t = min(t_active[b], T)
+// - 1, written into score[b, t].  A decode step scores the rows before it
+// with the tensor-core kernel while the indexer compressor may still be
+// writing that row; this kernel follows the compressor on its stream, so
+// the top-k finds every live score in place.  indexer_row_score is the
+// top-k's own recompute of the same row (dsa_indexer_topk_newest): the
+// value is bit-identical to it.  One CTA of 8 warps per sequence.
+__global__ void __launch_bounds__(256) indexer_score_newest_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, int64_t k_bstride,
+    const float* __restrict__ w, const int32_t* __restrict__ t_active, float* __restrict__ score, int64_t ld_score,
+    int T) {
+  __shared__ float s_dot[kRowHeads];
+  const int b = blockIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = min(t_active[b], T) - 1;
+  if (t < 0) return;  // uniform across the block
+  const float sc = indexer_row_score(q + int64_t(b) * kRowHeads * kRowDim, k + int64_t(b) * k_bstride +
+                                     int64_t(t) * kRowDim, w + int64_t(b) * kRowHeads, s_dot);
+  if (threadIdx.x == 0) score[int64_t(b) * ld_score + t] = sc;
+}
 
 }  // namespace dsa
 
@@ -120,4 +143,21 @@ extern "C" int dsa_indexer_score_ex(const void* q, const void* k, const float* w
   clear_error();
   DSA_CHECK_ARG((flags & ~DSA_KEYS_READY) == 0, "indexer_score: unknown flags 0x%x", flags);
   return indexer_score_run(q, k, w, score, t_valid, B, H, Di, T, k_bstride, ld_score, flags, stream);
+}
+
+extern "C" int dsa_indexer_score_newest(const void* q, const void* k, int64_t k_bstride, const float* w,
+                                        const int32_t* t_active, float* score, int64_t ld_score, int B, int T,
+                                        dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG(q && k && w && t_active && score, "indexer_score_newest: null pointer");
+  DSA_CHECK_ARG(B >= 0 && T > 0 && ld_score >= T && k_bstride >= int64_t(T) * kIdxD,
+                "indexer_score_newest: need T > 0, ld_score >= T, k_bstride >= T * 128");
+  DSA_CHECK_ARG(aligned(q, 8) && aligned(k, 8) && k_bstride % 4 == 0,
+                "indexer_score_newest: q, k and the key row stride must be 8-byte aligned");
+  if (B == 0) return DSA_OK;
+  launch_pdl(indexer_score_newest_kernel, dim3(B), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+             static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k), k_bstride, w, t_active,
+             score, ld_score, T);
+  DSA_CHECK_LAUNCH("indexer_score_newest");
+  return DSA_OK;
 }

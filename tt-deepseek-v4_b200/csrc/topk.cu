@@ -64,6 +64,10 @@ __device__ __forceinline__ void block_minmax_sum(uint32_t lo, uint32_t hi, uint3
   __syncthreads();
 }
 
+// The bin of s->hist holding the kl-th largest key: s->prefix = bin, s->kgt
+// = keys in the bins above it.  Warp 0 scans; ends with a block barrier.
+__device__ __forceinline__ void pick_bin(int kl, SelectScratch* s);
+
 // Histogram of the live keys (bin_of(key) != kNoBin for index < nl) and the
 // bin holding the kl-th largest: s->prefix = bin, s->kgt = keys above it.
 // Lanes sharing lane 0's bin add with one atomic (clustered scores would
@@ -71,7 +75,7 @@ __device__ __forceinline__ void block_minmax_sum(uint32_t lo, uint32_t hi, uint3
 template <class BinOf>
 __device__ __forceinline__ void hist_pick(const uint32_t (&r)[kKeysPerThread], int nj, int nl, int kl, BinOf bin_of,
                                           SelectScratch* s) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31;
   for (int i = tid; i < 256; i += blockDim.x) s->hist[i] = 0;
   if (tid == 0) s->ncand = 0;
   __syncthreads();
@@ -88,6 +92,11 @@ __device__ __forceinline__ void hist_pick(const uint32_t (&r)[kKeysPerThread], i
     }
   }
   __syncthreads();
+  pick_bin(kl, s);
+}
+
+__device__ __forceinline__ void pick_bin(int kl, SelectScratch* s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp == 0) {
     // lane l owns bins [8l, 8l+8); find the bin of the kl-th largest from the top
     uint32_t h[8], tot = 0;
@@ -519,6 +528,231 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(
                   out_score ? out_score + int64_t(b) * ld_out : nullptr, scratch, &s);
 }
 
+// One row per CTA with the final indices in position order (the decode
+// step's case: T <= kTopkMaxN, no sort).  The same selection as
+// topk_chunk_kernel with one chunk -- the threshold is the k-th largest key,
+// ties go to the lowest positions -- in far fewer instructions (the select
+// is issue-bound at one CTA per row):
+//  * warp w holds positions [w * 32 * per, (w + 1) * 32 * per) in registers,
+//    32 consecutive ones per register (coalesced loads; the compaction counts
+//    and emits from registers);
+//  * the first level's value bins (0..254 over [min, max] of the live keys)
+//    are computed once, by a round-to-integer FMA (x + 1.5 * 2^23 holds
+//    round(x) in its low mantissa bits; monotone in x, so the map stays
+//    exact), and kept in shared memory for the gather;
+//  * the candidates of the chosen bin are ranked by four threads each.
+// Rows the first level cannot settle (fewer than k live keys, equal or
+// non-finite extremes, more than kRankMax keys in the bin) take the general
+// select.
+constexpr uint32_t kRowNoBin = 255;         // masked keys: in no bin
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+__global__ void __launch_bounds__(kTopkThreads) topk_row_kernel(
+    const float* __restrict__ score, int64_t ld_score, const int32_t* __restrict__ t_active, int n, int k, int win,
+    int mask_mode, int32_t* __restrict__ out_idx, float* __restrict__ out_score, int64_t ld_out,
+    const __nv_bfloat16* __restrict__ fq, const __nv_bfloat16* __restrict__ fk, int64_t fk_bstride,
+    const float* __restrict__ fw) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ SelectScratch s;
+  __shared__ uint32_t rank_gt[kRankMax], rank_ge[kRankMax];
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
+  uint8_t* bins = smem + kTopkMaxN * 4;
+  uint32_t* cand = reinterpret_cast<uint32_t*>(smem + kTopkMaxN * 8);
+  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (n + kTopkThreads - 1) / kTopkThreads;
+  const int base = warp * 32 * per + lane;  // r[j] holds position base + 32 j
+  if (tid < 256) s.hist[tid] = 0;
+  if (tid < kRankMax) {
+    rank_gt[tid] = 0;
+    rank_ge[tid] = 0;
+  }
+  if (tid == 0) s.ncand = 0;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int ta = t_active[b];
+  const float* row = score + int64_t(b) * ld_score;
+  const int tf = min(ta, n) - 1;  // the newest live entry
+  const bool fix = fq != nullptr && tf >= 0;
+  uint32_t r[kKeysPerThread];
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    const int i = base + 32 * j;
+    r[j] = (j < per && i < n) ? __float_as_uint(__ldg(row + i)) : 0u;
+  }
+  float fix_score = 0.f;
+  if (fix) {
+    fix_score = indexer_row_score(fq + int64_t(b) * kRowHeads * kRowDim, fk + int64_t(b) * fk_bstride +
+                                  int64_t(tf) * kRowDim, fw + int64_t(b) * kRowHeads, s.fix_dot);
+  }
+  const uint32_t kfloor = float_key(-INFINITY);
+  uint32_t lo = 0xffffffffu, hi = 0u, cnt = 0;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= per) break;
+    const int i = base + 32 * j;
+    if (i < n) {
+      const float v = (fix && i == tf) ? fix_score : __uint_as_float(r[j]);
+      const uint32_t key = float_key(i < ta ? v : (mask_mode ? -INFINITY : __fsub_rn(v, 1.0e4f)));
+      r[j] = key;
+      keys[i] = key;
+      if (key > kfloor) {
+        ++cnt;
+        lo = min(lo, key);
+        hi = max(hi, key);
+      }
+    }
+  }
+  uint32_t mn, mx, n_live;
+  block_minmax_sum(lo, hi, cnt, &s, mn, mx, n_live);
+  const float vmin = key_float(mn), vmax = key_float(mx);
+  const float scale = 254.99f / (vmax - vmin);
+  // uniform across the block: mn, mx, n_live and later s.ncand are shared
+  bool fast = n_live >= uint32_t(k) && mx != mn && isfinite(vmin) && isfinite(vmax) && isfinite(scale) &&
+              scale > 0.f;
+  uint32_t thr = 0;
+  if (fast) {
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      if (j >= per) break;
+      const int i = base + 32 * j;
+      uint32_t bin = kRowNoBin;
+      if (i < n && r[j] > kfloor) {
+        const float d = key_float(r[j]) - vmin;
+        bin = min(__float_as_uint(fmaf(d, scale, kRoundMagic)) - __float_as_uint(kRoundMagic), 254u);
+      }
+      if (i < n) bins[i] = uint8_t(bin);
+      const uint32_t lead = __shfl_sync(0xffffffffu, bin, 0);
+      const unsigned same = __ballot_sync(0xffffffffu, bin == lead);
+      if (bin == lead) {
+        if (lane == __ffs(same) - 1 && lead != kRowNoBin) atomicAdd(&s.hist[lead], uint32_t(__popc(same)));
+      } else if (bin != kRowNoBin) {
+        atomicAdd(&s.hist[bin], 1u);
+      }
+    }
+    __syncthreads();
+    pick_bin(k, &s);
+    const uint32_t bin = s.prefix;
+    const uint32_t kl = uint32_t(k) - s.kgt;
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      if (j >= per) break;
+      const int i = base + 32 * j;
+      const bool hit = i < n && bins[i] == bin;
+      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (m) {
+        uint32_t o = 0;
+        if (lane == 0) o = atomicAdd(&s.ncand, uint32_t(__popc(m)));
+        o = __shfl_sync(0xffffffffu, o, 0);
+        if (hit) cand[o + __popc(m & ((1u << lane) - 1u))] = r[j];
+      }
+    }
+    __syncthreads();
+    const int nc = int(s.ncand);
+    if (nc <= kRankMax) {
+      // the kl-th largest candidate c: fewer than kl candidates above it and
+      // at least kl at or above it; thread t counts candidate t % 256 against
+      // a quarter of the list
+      const int ci = tid & (kRankMax - 1), qt = tid >> 8;
+      if (ci < nc) {
+        const uint32_t c = cand[ci];
+        const int u0 = (nc * qt) >> 2, u1 = (nc * (qt + 1)) >> 2;
+        uint32_t gt = 0, ge = 0;
+        for (int u = u0; u < u1; ++u) {
+          const uint32_t x = cand[u];
+          gt += x > c;
+          ge += x >= c;
+        }
+        if (u1 > u0) {
+          atomicAdd(&rank_gt[ci], gt);
+          atomicAdd(&rank_ge[ci], ge);
+        }
+      }
+      __syncthreads();
+      if (tid < nc && rank_gt[tid] < kl && kl <= rank_ge[tid]) s.prefix = cand[tid];
+      __syncthreads();
+      thr = s.prefix;
+    } else {
+      fast = false;
+    }
+  }
+  if (!fast) {
+    // the general select, over the strided register layout it expects
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      const int i = tid + j * kTopkThreads;
+      r[j] = i < n ? keys[i] : 0u;
+    }
+    kth_key_select(r, keys, n, k, &s, cand);
+    thr = s.prefix;
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      const int i = base + 32 * j;
+      r[j] = (j < per && i < n) ? keys[i] : 0u;
+    }
+  }
+  // compaction: keys above thr, then the lowest-position keys equal to it,
+  // in position order (ballot ranks inside each warp, one scan over the
+  // warps' counts)
+  uint32_t ca = 0, ce = 0;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= per) break;
+    const bool valid = base + 32 * j < n;
+    ca += __popc(__ballot_sync(0xffffffffu, valid && r[j] > thr));
+    ce += __popc(__ballot_sync(0xffffffffu, valid && r[j] == thr));
+  }
+  if (lane == 0) {
+    s.warp_cnt[0][warp] = ca;
+    s.warp_cnt[1][warp] = ce;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t wa = s.warp_cnt[0][lane], we = s.warp_cnt[1][lane];
+    uint32_t xa = wa, xe = we;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t va = __shfl_up_sync(0xffffffffu, xa, o), ve = __shfl_up_sync(0xffffffffu, xe, o);
+      if (lane >= o) {
+        xa += va;
+        xe += ve;
+      }
+    }
+    s.warp_cnt[0][lane] = xa - wa;
+    s.warp_cnt[1][lane] = xe - we;
+    if (lane == 31) s.kgt = xa;  // keys above the threshold, all warps
+  }
+  __syncthreads();
+  uint32_t oa = s.warp_cnt[0][warp], oe = s.warp_cnt[1][warp];
+  const int n_above = int(s.kgt);  // < k by the choice of thr
+  const int n_eq_take = k - n_above;
+  const uint32_t lt = (1u << lane) - 1u;
+  int32_t* orow = out_idx + int64_t(b) * ld_out;
+  float* srow = out_score ? out_score + int64_t(b) * ld_out : nullptr;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= per) break;
+    const int i = base + 32 * j;
+    const bool valid = i < n;
+    const bool above = valid && r[j] > thr, eq = valid && r[j] == thr;
+    const uint32_t ma = __ballot_sync(0xffffffffu, above), me = __ballot_sync(0xffffffffu, eq);
+    int slot = -1;
+    if (above) {
+      slot = int(oa + __popc(ma & lt));
+    } else if (eq) {
+      const int re = int(oe + __popc(me & lt));
+      if (re < n_eq_take) slot = n_above + re;
+    }
+    oa += __popc(ma);
+    oe += __popc(me);
+    if (slot >= 0) {
+      const float f = key_float(r[j]);
+      orow[slot] = f >= -1000.0f ? i + win : -1;
+      if (srow) srow[slot] = f;
+    }
+  }
+}
+
 __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ idx, int64_t ld,
                                       int B, int win) {
   pdl_wait();
@@ -578,7 +812,14 @@ static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_ac
   if (attr_dev != dev) {
     cudaFuncSetAttribute(topk_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk_smem());
     cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, merge_smem());
+    cudaFuncSetAttribute(topk_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk_smem());
     attr_dev = dev;
+  }
+  if (T <= kTopkMaxN && !sort_desc) {
+    launch_pdl(topk_row_kernel, dim3(B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T, k, win,
+               mask_mode, out_idx, out_score, ld_out, fq, fk, fk_bstride, fw);
+    DSA_CHECK_LAUNCH("indexer_topk");
+    return DSA_OK;
   }
   if (T <= kTopkMaxN) {
     launch_pdl(topk_chunk_kernel, dim3(1, B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T, T,

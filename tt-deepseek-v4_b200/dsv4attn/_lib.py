@@ -47,6 +47,7 @@ PROTOTYPES = {
     "dsa_window_indices": (I32, [P, P, I64, I32, I32, P]),
     "dsa_indexer_score": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, P]),
     "dsa_indexer_score_ex": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, I32, P]),
+    "dsa_indexer_score_newest": (I32, [P, P, I64, P, P, P, I64, I32, I32, P]),
     "dsa_indexer_topk": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
     "dsa_indexer_topk_workspace_size": (SZ, [I32, I32, I32]),
     "dsa_indexer_topk_ws": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P, SZ, P]),

@@ -19,6 +19,7 @@ reference's order (inference.py:5888-6093):
     attn.kv          kv_window_write      act_quant(nope) + ring write
     attn.topk        window_indices       ring slots of the window
                      compressor_step      indexer compressor (emit on device)
+                     indexer_score_newest the newest row's score (side branch)
                      indexer_score        relu-weighted multi-head scores
                      indexer_topk         k best compressed rows (+W, -1)
     attn.compress    compressor_step      attention compressor (emit on device)
@@ -30,9 +31,10 @@ needs two traces and host staging per step, inference.py:7498-7543).  The
 window write, the attention compressor and the indexer compressor run on a
 side stream in parallel with the indexer score (a parallel branch of the
 captured graph): the score covers the compressed rows before the newest,
-and the top-k, after the join, recomputes the newest row's score from the
-indexer inputs (dsa_indexer_topk_newest) -- the same selection as scoring
-after the compressor, with the compressor off the critical path.
+the side branch scores the newest row after its compressor
+(dsa_indexer_score_newest), and the top-k runs after the join -- the same
+selection as scoring after the compressor, with the compressor and the
+newest row's score off the critical path.
 """
 
 from __future__ import annotations
@@ -217,6 +219,10 @@ class DecodePath:
             ops.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos,
                                 self.sin, L.idx_cache, 0, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
                                 rope_dim=a.rope_head_dim)
+            # the newest live row's score (t_active - 1), after the
+            # compressor that may have written that row; the main branch
+            # scores the rows before it
+            ops.indexer_score_newest(x.iq, L.idx_cache, x.iw, self.t_active, L.T_max, out=L.score)
         # side branch 2: attn.kv window write, the window ring indices and
         # attn.compress (all three only feed the attention)
         side.wait_stream(main)
@@ -228,9 +234,9 @@ class DecodePath:
                                 rope_dim=a.rope_head_dim)
         # main branch: attn.topk.  The score covers the rows before the
         # newest (t_prev = t_active - 1), which the indexer compressor may be
-        # writing meanwhile; after joining it the top-k recomputes that
-        # row's score from the indexer inputs.  The top-k writes idx[:, W:],
-        # disjoint from the window columns.
+        # writing meanwhile; the compressor's branch scores that row after
+        # it, and the top-k runs after joining it.  The top-k writes
+        # idx[:, W:], disjoint from the window columns.
         # keys_ready: the key rows scored here were written by earlier steps
         # and t_prev before the first layer, so from the second layer on the
         # kernel's first key tiles may be requested before the previous
@@ -239,8 +245,7 @@ class DecodePath:
         ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_prev,
                           keys_ready=L is not self.layers[0])
         main.wait_stream(side_idx)
-        ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws,
-                         refresh=(x.iq, L.idx_cache, x.iw))
+        ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws)
         main.wait_stream(side)
         # the window columns of idx, q and the window rows were written before
         # the top-k began (side branch, inputs): each key split requests its
@@ -274,7 +279,7 @@ class DecodePath:
     def replay(self) -> None:
         self.graph.replay()
 
-    kernels_per_layer = 7  # launches per layer when the split-K combine is not needed
+    kernels_per_layer = 8  # launches per layer when the split-K combine is not needed
 
     def launches_per_step(self) -> int:
         n = 0

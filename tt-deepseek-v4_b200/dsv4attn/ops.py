@@ -396,6 +396,29 @@ def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: in
     return out
 
 
+def indexer_score_newest(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, t_active: torch.Tensor, T: int,
+                         out: torch.Tensor) -> torch.Tensor:
+    """The score of each sequence's newest live row, t = min(t_active, T) - 1,
+    written into ``out[b, t]`` (inference.py:5260-5275 for one row; the value
+    the top-k's ``refresh`` recomputes).  q [B,64,128] bf16, k_cache
+    [B, >=T, 128] bf16 rows contiguous, w [B,64] fp32, out [B, >=T] fp32."""
+    _need(q, "q", BF16)
+    _need(k_cache, "k_cache", BF16)
+    _need(w, "w", F32)
+    _need(t_active, "t_active", I32)
+    _need(out, "out", F32)
+    _contig(q, "q")
+    _contig(w, "w")
+    B = q.shape[0]
+    if q.shape[1:] != (64, 128) or k_cache.dim() != 3 or k_cache.shape[0] < B or k_cache.shape[1] < T \
+            or k_cache.shape[2] != 128 or k_cache.stride(1) != 128 or out.shape[0] < B or out.stride(1) != 1:
+        raise ValueError("indexer_score_newest: q [B,64,128], k_cache [B,>=T,128] rows contiguous, out [B,>=T]")
+    check(lib().dsa_indexer_score_newest(q.data_ptr(), k_cache.data_ptr(), k_cache.stride(0), w.data_ptr(),
+                                         t_active.data_ptr(), out.data_ptr(), out.stride(0), B, T, _stream(q)),
+          "indexer_score_newest")
+    return out
+
+
 def indexer_topk(score: torch.Tensor, t_active: torch.Tensor, k: int, win: int, T: int | None = None,
                  sort_desc: bool = False, mask_mode: int = 0, out: torch.Tensor | None = None,
                  out_score: torch.Tensor | None = None, ws: Workspace | None = None,
