@@ -460,3 +460,20 @@ def test_indexer_score_newest_matches_refresh(cuda_dev, B, T):
     got = score.cpu()[rows, (ta - 1).long()]
     torch.testing.assert_close(got, want[rows, (ta - 1).long()], rtol=1e-3,
                                atol=1e-3 * float(want.abs().max()))
+
+
+def test_sparse_attn_pair_combine_deterministic(cuda_dev):
+    # 64 query rows x 2176 keys run as pairs of key splits that finish the
+    # row between them over distributed shared memory: repeated calls give
+    # identical bits, and every row matches the oracle
+    from dsv4attn import ops
+    B, N, K = 64, 2400, 2176
+    q, kv, idx, sink = _attn_case(B, 1, N, K, seed=77)
+    idx = idx.clone()
+    idx.view(B, K)[::7, -300:] = -1
+    qd, kvd, idd, sd = q.to(cuda_dev), kv.to(cuda_dev), idx.to(cuda_dev), sink.to(cuda_dev)
+    a = ops.sparse_attn(qd, kvd, idd, sd, 512 ** -0.5).cpu()
+    b = ops.sparse_attn(qd, kvd, idd, sd, 512 ** -0.5).cpu()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    want = O.sparse_attn(q, kv, idx, sink, 512 ** -0.5)
+    assert rel_err(a, want) < ATTN_REL

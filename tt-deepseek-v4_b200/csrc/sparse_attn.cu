@@ -247,7 +247,16 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   t.trace = g_trace;
   float* ws_ml = nullptr;
   __nv_bfloat16* ws_o = nullptr;
-  if (p.nsplit > 1) {
+  // two key splits with a final output: the splits of a row run as one
+  // cluster and combine over distributed shared memory (no partials, no
+  // combine launch); the workspace goes unused
+  const bool pair = p.nsplit == 2 && final_mode;
+  if (pair) {
+    t.final_mode = 0;
+    t.pair_combine = 1;
+    t.out = static_cast<__nv_bfloat16*>(out);
+    t.lse = lse;
+  } else if (p.nsplit > 1) {
     const size_t need = ws_bytes_for(p, M);
     if (ws == nullptr || ws_bytes < need) {
       set_error("sparse_attn: needs %zu bytes of workspace (got %zu)", need, ws_bytes);
@@ -273,6 +282,25 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   if (!tma::make_2d_bf16(&tm_q, q, kSaD, uint64_t(M) * kSaH, kSaD * 2, 64, 64)) {
     set_error("sparse_attn: cuTensorMapEncodeTiled failed");
     return DSA_ERR_CUDA;
+  }
+  if (pair) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, M);
+    cfg.blockDim = dim3(satc::THREADS);
+    cfg.dynamicSmemBytes = satc::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, satc::sparse_attn_tc_kernel, t, tm_q, row_stride);
+    DSA_CHECK_LAUNCH("sparse_attn");
+    return DSA_OK;
   }
   launch_pdl(satc::sparse_attn_tc_kernel, dim3(p.nsplit, M), dim3(satc::THREADS), satc::kSmemBytes, st, t, tm_q,
              row_stride);

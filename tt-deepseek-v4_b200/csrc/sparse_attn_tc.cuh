@@ -138,6 +138,10 @@ struct Args {
   int lead_tiles, rest_tps, early;
   float scale_log2;
   int final_mode;
+  // the row's two key splits run as one thread-block cluster and finish
+  // the row between them (see the pair combine at the end of the kernel):
+  // out / lse are written, no partials
+  int pair_combine;
   long long wait_limit;  // spin budget of every bounded wait, SM cycles
   long long* trace;  // optional: per-tile clock64 stamps of CTA (0, 0), see kTr*
 };
@@ -164,6 +168,9 @@ enum : int { kTrTiles = 256, kTrIssue = 0, kTrFull = 1, kTrMmaGot = 2, kTrS = 3,
 struct Aux {
   float alpha[H];                 // rescale factor of the last max update
   float f[H];                     // epilogue scale per head
+  float m_fin[H], l_fin[H];       // pair combine: this split's (m, l) per head, m in log2 units
+  float peer_ml[H];               // pair combine: the peer split's (m, l) of the heads this CTA finishes
+  float coef[2][H / 2];           // pair combine: weight / L of split 0 and split 1 per finished head
   uint32_t vmask[kIdxCap / 32];   // validity bits of the staged indices
   uint64_t q_tma;
   uint64_t q_full;
@@ -209,6 +216,24 @@ __device__ __forceinline__ void q_part_to_tmem(uint32_t sq, uint32_t tmem, int w
   tc::tmem_wait_st();
   tc::fence_before_sync();
   tc::mbar_arrive(smem_u32(q_full));
+}
+
+// distributed shared memory of the pair combine (plain remote stores)
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float x, float y, float z, float w) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y), "f"(z), "f"(w)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float x, float y) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
 }
 
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a,
@@ -555,7 +580,10 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       for (int g = 0; g < 2; ++g) {
         const int h = g ? hb : ha;
         const float mh = g ? m_b : m_a, lh = g ? l_b : l_a;
-        if (a.final_mode) {
+        if (a.pair_combine) {
+          aux->m_fin[h] = mh;
+          aux->l_fin[h] = lh;
+        } else if (a.final_mode) {
           const float sk = a.sink[h] * kLog2e;
           const float Mx = fmaxf(mh, sk);
           const float w = (mh == -INFINITY) ? 0.f : exp2f(mh - Mx);
@@ -609,7 +637,81 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   __syncthreads();
   tc::fence_after_sync();
   if (tid == 0) SA_TRACE(kTrMisc, 3);
-  {
+  if (a.pair_combine) {
+    // ------------------------------------------------------ pair combine
+    // The row's splits 0 and 1 are this cluster's two CTAs (cluster rank =
+    // split).  CTA r finishes heads 32r..32r+31: it sends the other half of
+    // its O^T (thread = output dim d: 32 fp32, 128 B) and the (m, l) of those
+    // heads into the peer's idle ring, then combines its own half with the
+    // peer's: out = (w0 o0 + w1 o1) / L, w_s = 2^(m_s - M),
+    // L = l0 w0 + l1 w1 + 2^(sink - M), M = max(m0, m1, sink) - split 0's
+    // partial first on both CTAs, so the result does not depend on which
+    // CTA finishes which half.
+    const int r = split, pr = split ^ 1;
+    const int sp = warp & 3, jb = warp >> 2;
+    const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
+    const int d = 128 * jb + 32 * sp + lane;
+    const uint32_t row_off = uint32_t(d) * 128u;
+    // (1) both CTAs are past their last MMA and copy: the rings are idle
+    cluster_sync();
+    {
+      float o[32];
+      if (n > 0) {
+        tc::tmem_ld32(tl + kColO + H * jb + 32 * pr, o);
+        tc::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      const uint32_t dst = mapa(sRing + row_off, uint32_t(pr));
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        st_cluster_v4(dst + ((uint32_t(c ^ (d & 7))) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      if (tid < 32) {
+        const int h = 32 * pr + tid;
+        st_cluster_v2(mapa(smem_u32(&aux->peer_ml[2 * tid]), uint32_t(pr)), aux->m_fin[h], aux->l_fin[h]);
+      }
+    }
+    // (2) the peer's half has landed in this CTA's ring
+    cluster_sync();
+    if (tid < 32) {
+      const int h = 32 * r + tid;
+      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = aux->peer_ml[2 * tid], lp = aux->peer_ml[2 * tid + 1];
+      const float m0 = r == 0 ? mo : mp, l0 = r == 0 ? lo : lp, m1 = r == 0 ? mp : mo, l1 = r == 0 ? lp : lo;
+      const float sk = a.sink[h] * kLog2e;
+      const float Mx = fmaxf(fmaxf(m0, m1), sk);
+      const float w0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - Mx);
+      const float w1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - Mx);
+      const float L = l0 * w0 + l1 * w1 + exp2f(sk - Mx);
+      aux->coef[0][tid] = w0 / L;
+      aux->coef[1][tid] = w1 / L;
+      if (a.lse) a.lse[int64_t(mrow) * H + h] = (Mx + log2f(L)) * kLn2;
+    }
+    __syncthreads();
+    {
+      float own[32], peer[32];
+      if (n > 0) {
+        tc::tmem_ld32(tl + kColO + H * jb + 32 * r, own);
+        tc::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) own[i] = 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t addr = sRing + row_off + ((uint32_t(c ^ (d & 7))) << 4);
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(peer[4 * c]), "=f"(peer[4 * c + 1]), "=f"(peer[4 * c + 2]), "=f"(peer[4 * c + 3])
+                     : "r"(addr));
+      }
+      __nv_bfloat16* om = a.out + int64_t(mrow) * H * D + int64_t(32 * r) * D + d;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float x0 = r == 0 ? own[i] : peer[i], x1 = r == 0 ? peer[i] : own[i];
+        om[i * D] = f2bf(fmaf(aux->coef[1][i], x1, aux->coef[0][i] * x0));
+      }
+    }
+  } else {
     const int sp = warp & 3, jb = warp >> 2;
     const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
     const int d = 128 * jb + 32 * sp + lane;
