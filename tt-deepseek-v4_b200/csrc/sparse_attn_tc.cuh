@@ -181,6 +181,8 @@ struct Aux {
   uint64_t p_full[2];
   uint64_t pv_done[2];
   uint64_t mma_done;
+  uint64_t pair_in;    // pair combine: the peer's half has landed here
+  uint64_t pair_done;  // pair combine: the peer has received this CTA's half
   uint32_t tmem_base;
   int abort;
 };
@@ -228,12 +230,46 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float x, float y, float z, float w) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y), "f"(z), "f"(w)
+// this CTA's shared memory -> the peer's (cluster addresses for dst and bar)
+__device__ __forceinline__ void bulk_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
-__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float x, float y) {
-  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
+// this CTA's shared memory -> global, then wait until the source has been read
+__device__ __forceinline__ void bulk_store_wait_read(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(src), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+// bounded wait with cluster-scope acquire (the peer's copy or arrival)
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int32_t* status, long long limit) {
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const long long t0 = clock64();
+  while (!try_wait()) {
+    if (clock64() - t0 > limit) {
+      if (status) atomicOr(status, kStatusTimeout);
+      return false;
+    }
+  }
+  return true;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a,
@@ -282,6 +318,8 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tc::mbar_init(smem_u32(&aux->pv_done[s]), 2);
     }
     tc::mbar_init(smem_u32(&aux->mma_done), 3);  // one commit from each issuer
+    tc::mbar_init(smem_u32(&aux->pair_in), 1);    // this CTA's expect_tx; the peer's copy completes it
+    tc::mbar_init(smem_u32(&aux->pair_done), 1);  // the peer's arrival once it has received
     tc::mbar_fence_init();
   }
   // the barriers are initialised before any thread arrives on them (the
@@ -640,20 +678,25 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   if (a.pair_combine) {
     // ------------------------------------------------------ pair combine
     // The row's splits 0 and 1 are this cluster's two CTAs (cluster rank =
-    // split).  CTA r finishes heads 32r..32r+31: it sends the other half of
-    // its O^T (thread = output dim d: 32 fp32, 128 B) and the (m, l) of those
-    // heads into the peer's idle ring, then combines its own half with the
-    // peer's: out = (w0 o0 + w1 o1) / L, w_s = 2^(m_s - M),
+    // split).  CTA r finishes heads 32r..32r+31.  It stages the other half
+    // of its O^T (thread = output dim d: 32 fp32 = one 128-B row, 16-B
+    // chunks swizzled by d % 8) and the (m, l) of those heads, and one bulk
+    // copy moves them into the peer's idle ring, completing on the peer's
+    // pair_in barrier.  Then out = (w0 o0 + w1 o1) / L, w_s = 2^(m_s - M),
     // L = l0 w0 + l1 w1 + 2^(sink - M), M = max(m0, m1, sink) - split 0's
     // partial first on both CTAs, so the result does not depend on which
-    // CTA finishes which half.
+    // CTA finishes which half - is staged as the 32 heads' contiguous bf16
+    // rows and leaves in one bulk store.  Ring use (idle since every MMA and
+    // copy completed): slot 0 receives the peer's rows, slot 1 its (m, l)
+    // (first 256 B) and the output (from 1 KB), slot 2 stages what is sent,
+    // its (m, l) in the first 256 B of the idle P buffers right after.
+    constexpr uint32_t kSendBytes = 512 * 128 + 256;
     const int r = split, pr = split ^ 1;
     const int sp = warp & 3, jb = warp >> 2;
     const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
     const int d = 128 * jb + 32 * sp + lane;
     const uint32_t row_off = uint32_t(d) * 128u;
-    // (1) both CTAs are past their last MMA and copy: the rings are idle
-    cluster_sync();
+    const uint32_t sRecv = sRing, sOut = sRing + kTileBytes + 1024, sSend = sRing + 2 * kTileBytes;
     {
       float o[32];
       if (n > 0) {
@@ -663,20 +706,35 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = 0.f;
       }
-      const uint32_t dst = mapa(sRing + row_off, uint32_t(pr));
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        st_cluster_v4(dst + ((uint32_t(c ^ (d & 7))) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t addr = sSend + row_off + ((uint32_t(c ^ (d & 7))) << 4);
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(o[4 * c]), "f"(o[4 * c + 1]),
+                     "f"(o[4 * c + 2]), "f"(o[4 * c + 3])
+                     : "memory");
+      }
       if (tid < 32) {
         const int h = 32 * pr + tid;
-        st_cluster_v2(mapa(smem_u32(&aux->peer_ml[2 * tid]), uint32_t(pr)), aux->m_fin[h], aux->l_fin[h]);
+        asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(sSend + 65536u + 8u * tid), "f"(aux->m_fin[h]),
+                     "f"(aux->l_fin[h])
+                     : "memory");
       }
     }
-    // (2) the peer's half has landed in this CTA's ring
+    if (tid == 0) tma::mbar_arrive_expect_tx(smem_u32(&aux->pair_in), kSendBytes);
+    tc::fence_proxy_async();  // the staged half is read by the copy engine
+    // both CTAs: rings idle, receive barrier armed, half staged
     cluster_sync();
+    if (tid == 0)
+      bulk_to_peer(mapa(sRecv, uint32_t(pr)), sSend, kSendBytes, mapa(smem_u32(&aux->pair_in), uint32_t(pr)));
+    // every thread: the peer's half has landed (bounded wait, cluster acquire)
+    mbar_wait_cluster(smem_u32(&aux->pair_in), 0, a.status, a.wait_limit);
+    // tell the peer its copy has landed (it may then release the shared
+    // memory the copy read)
+    if (tid == 0) mbar_arrive_remote(mapa(smem_u32(&aux->pair_done), uint32_t(pr)));
     if (tid < 32) {
       const int h = 32 * r + tid;
-      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = aux->peer_ml[2 * tid], lp = aux->peer_ml[2 * tid + 1];
+      const float* rml = reinterpret_cast<const float*>(smem + kOffRing + 65536) + 2 * tid;
+      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = rml[0], lp = rml[1];
       const float m0 = r == 0 ? mo : mp, l0 = r == 0 ? lo : lp, m1 = r == 0 ? mp : mo, l1 = r == 0 ? lp : lo;
       const float sk = a.sink[h] * kLog2e;
       const float Mx = fmaxf(fmaxf(m0, m1), sk);
@@ -687,29 +745,36 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       aux->coef[1][tid] = w1 / L;
       if (a.lse) a.lse[int64_t(mrow) * H + h] = (Mx + log2f(L)) * kLn2;
     }
+    float own[32], peer[32];
+    if (n > 0) {
+      tc::tmem_ld32(tl + kColO + H * jb + 32 * r, own);
+      tc::tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) own[i] = 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint32_t addr = sRecv + row_off + ((uint32_t(c ^ (d & 7))) << 4);
+      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(peer[4 * c]), "=f"(peer[4 * c + 1]), "=f"(peer[4 * c + 2]), "=f"(peer[4 * c + 3])
+                   : "r"(addr));
+    }
+    __syncthreads();  // coefficients
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float x0 = r == 0 ? own[i] : peer[i], x1 = r == 0 ? peer[i] : own[i];
+      const __nv_bfloat16 v = f2bf(fmaf(aux->coef[1][i], x1, aux->coef[0][i] * x0));
+      asm volatile("st.shared.b16 [%0], %1;" ::"r"(sOut + uint32_t(i * D + d) * 2u),
+                   "h"(*reinterpret_cast<const unsigned short*>(&v))
+                   : "memory");
+    }
+    tc::fence_proxy_async();
     __syncthreads();
-    {
-      float own[32], peer[32];
-      if (n > 0) {
-        tc::tmem_ld32(tl + kColO + H * jb + 32 * r, own);
-        tc::tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) own[i] = 0.f;
-      }
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t addr = sRing + row_off + ((uint32_t(c ^ (d & 7))) << 4);
-        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(peer[4 * c]), "=f"(peer[4 * c + 1]), "=f"(peer[4 * c + 2]), "=f"(peer[4 * c + 3])
-                     : "r"(addr));
-      }
-      __nv_bfloat16* om = a.out + int64_t(mrow) * H * D + int64_t(32 * r) * D + d;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float x0 = r == 0 ? own[i] : peer[i], x1 = r == 0 ? peer[i] : own[i];
-        om[i * D] = f2bf(fmaf(aux->coef[1][i], x1, aux->coef[0][i] * x0));
-      }
+    if (tid == 0) {
+      bulk_store_wait_read(a.out + (int64_t(mrow) * H + 32 * r) * D, sOut, 32 * D * 2);
+      // this CTA's outgoing copy has been received before its shared memory goes
+      mbar_wait_cluster(smem_u32(&aux->pair_done), 0, a.status, a.wait_limit);
     }
   } else {
     const int sp = warp & 3, jb = warp >> 2;
