@@ -248,20 +248,26 @@ static int sparse_attn_run(const void* q, const void* kv, int64_t kv_bstride, in
   float* ws_ml = nullptr;
   __nv_bfloat16* ws_o = nullptr;
   // two key splits with a final output: the splits of a row run as one
-  // cluster and combine over distributed shared memory (no partials, no
-  // combine launch); the workspace goes unused
+  // cluster and finish the row between them, exchanging half of each
+  // accumulator through the workspace (no combine launch)
   const bool pair = p.nsplit == 2 && final_mode;
-  if (pair) {
-    t.final_mode = 0;
-    t.pair_combine = 1;
-    t.out = static_cast<__nv_bfloat16*>(out);
-    t.lse = lse;
-  } else if (p.nsplit > 1) {
+  static_assert(2 * satc::kPairXFloats * sizeof(float) <= kSaH * (2 * sizeof(float) + kSaD * 2) * 2,
+                "the pair exchange fits the two-split workspace");
+  if (p.nsplit > 1) {
     const size_t need = ws_bytes_for(p, M);
     if (ws == nullptr || ws_bytes < need) {
       set_error("sparse_attn: needs %zu bytes of workspace (got %zu)", need, ws_bytes);
       return DSA_ERR_WORKSPACE;
     }
+  }
+  if (pair) {
+    DSA_CHECK_ARG(aligned(ws, 16), "sparse_attn: the workspace must be 16-byte aligned");
+    t.final_mode = 0;
+    t.pair_combine = 1;
+    t.pair_x = static_cast<float*>(ws);
+    t.out = static_cast<__nv_bfloat16*>(out);
+    t.lse = lse;
+  } else if (p.nsplit > 1) {
     ws_ml = static_cast<float*>(ws);
     ws_o = reinterpret_cast<__nv_bfloat16*>(ws_ml + size_t(p.nsplit) * M * kSaH * 2);
     t.final_mode = 0;

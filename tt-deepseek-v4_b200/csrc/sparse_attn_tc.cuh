@@ -105,6 +105,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0;     // O^T: 4 blocks of [128 dims x 64 heads]
 constexpr uint32_t kColQ = 256;   // Q': 128 rows x 256 bf16 (128 columns)
 constexpr uint32_t kColS = 384;   // S: [128 Q' rows x 128 tile rows] fp32
+// pair combine exchange per (row, receiving CTA): 32 heads' O^T as
+// [8 chunks][512 dims][4] fp32, then (m, l) of the 32 heads
+constexpr int kPairXFloats = 8 * D * 4 + 64;
 constexpr uint32_t kIdescS = tc::idesc_bf16(128, 128, false, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 64, true, false);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -140,8 +143,10 @@ struct Args {
   int final_mode;
   // the row's two key splits run as one thread-block cluster and finish
   // the row between them (see the pair combine at the end of the kernel):
-  // out / lse are written, no partials
+  // out / lse are written; pair_x (M x 2 x kPairXFloats fp32) carries the
+  // halves they exchange
   int pair_combine;
+  float* pair_x;
   long long wait_limit;  // spin budget of every bounded wait, SM cycles
   long long* trace;  // optional: per-tile clock64 stamps of CTA (0, 0), see kTr*
 };
@@ -181,8 +186,6 @@ struct Aux {
   uint64_t p_full[2];
   uint64_t pv_done[2];
   uint64_t mma_done;
-  uint64_t pair_in;    // pair combine: the peer's half has landed here
-  uint64_t pair_done;  // pair combine: the peer has received this CTA's half
   uint32_t tmem_base;
   int abort;
 };
@@ -220,56 +223,11 @@ __device__ __forceinline__ void q_part_to_tmem(uint32_t sq, uint32_t tmem, int w
   tc::mbar_arrive(smem_u32(q_full));
 }
 
-// distributed shared memory of the pair combine (plain remote stores)
-__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
+// the pair combine's cluster barrier: release / acquire at cluster scope
+// orders each CTA's exchange writes before the peer's reads
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// this CTA's shared memory -> the peer's (cluster addresses for dst and bar)
-__device__ __forceinline__ void bulk_to_peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   dst),
-               "r"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
-// this CTA's shared memory -> global, then wait until the source has been read
-__device__ __forceinline__ void bulk_store_wait_read(void* dst, uint32_t src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
-               "r"(src), "r"(bytes)
-               : "memory");
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
-}
-// bounded wait with cluster-scope acquire (the peer's copy or arrival)
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int32_t* status, long long limit) {
-  auto try_wait = [&]() {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-  };
-  if (try_wait()) return true;
-  const long long t0 = clock64();
-  while (!try_wait()) {
-    if (clock64() - t0 > limit) {
-      if (status) atomicOr(status, kStatusTimeout);
-      return false;
-    }
-  }
-  return true;
 }
 
 __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a,
@@ -318,8 +276,6 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       tc::mbar_init(smem_u32(&aux->pv_done[s]), 2);
     }
     tc::mbar_init(smem_u32(&aux->mma_done), 3);  // one commit from each issuer
-    tc::mbar_init(smem_u32(&aux->pair_in), 1);    // this CTA's expect_tx; the peer's copy completes it
-    tc::mbar_init(smem_u32(&aux->pair_done), 1);  // the peer's arrival once it has received
     tc::mbar_fence_init();
   }
   // the barriers are initialised before any thread arrives on them (the
@@ -678,25 +634,22 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   if (a.pair_combine) {
     // ------------------------------------------------------ pair combine
     // The row's splits 0 and 1 are this cluster's two CTAs (cluster rank =
-    // split).  CTA r finishes heads 32r..32r+31.  It stages the other half
-    // of its O^T (thread = output dim d: 32 fp32 = one 128-B row, 16-B
-    // chunks swizzled by d % 8) and the (m, l) of those heads, and one bulk
-    // copy moves them into the peer's idle ring, completing on the peer's
-    // pair_in barrier.  Then out = (w0 o0 + w1 o1) / L, w_s = 2^(m_s - M),
+    // split).  CTA r finishes heads 32r..32r+31: it writes the other half
+    // of its O^T (thread = output dim d, 32 fp32) and the (m, l) of those
+    // heads to the peer's slot of pair_x (L2-resident; coalesced 16-B
+    // stores), the cluster barrier orders those writes before the peer's
+    // reads, and each CTA combines its own half with the peer's:
+    // out = (w0 o0 + w1 o1) / L, w_s = 2^(m_s - M),
     // L = l0 w0 + l1 w1 + 2^(sink - M), M = max(m0, m1, sink) - split 0's
     // partial first on both CTAs, so the result does not depend on which
-    // CTA finishes which half - is staged as the 32 heads' contiguous bf16
-    // rows and leaves in one bulk store.  Ring use (idle since every MMA and
-    // copy completed): slot 0 receives the peer's rows, slot 1 its (m, l)
-    // (first 256 B) and the output (from 1 KB), slot 2 stages what is sent,
-    // its (m, l) in the first 256 B of the idle P buffers right after.
-    constexpr uint32_t kSendBytes = 512 * 128 + 256;
+    // CTA finishes which half.  (Distributed shared memory moves ~28 GB/s
+    // per SM here; the L2 round trip is faster.)
     const int r = split, pr = split ^ 1;
     const int sp = warp & 3, jb = warp >> 2;
     const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
     const int d = 128 * jb + 32 * sp + lane;
-    const uint32_t row_off = uint32_t(d) * 128u;
-    const uint32_t sRecv = sRing, sOut = sRing + kTileBytes + 1024, sSend = sRing + 2 * kTileBytes;
+    float* x_out = a.pair_x + (int64_t(mrow) * 2 + pr) * kPairXFloats;
+    const float* x_in = a.pair_x + (int64_t(mrow) * 2 + r) * kPairXFloats;
     {
       float o[32];
       if (n > 0) {
@@ -707,34 +660,18 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         for (int i = 0; i < 32; ++i) o[i] = 0.f;
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t addr = sSend + row_off + ((uint32_t(c ^ (d & 7))) << 4);
-        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(o[4 * c]), "f"(o[4 * c + 1]),
-                     "f"(o[4 * c + 2]), "f"(o[4 * c + 3])
-                     : "memory");
-      }
+      for (int c = 0; c < 8; ++c)
+        reinterpret_cast<float4*>(x_out)[c * D + d] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
       if (tid < 32) {
         const int h = 32 * pr + tid;
-        asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(sSend + 65536u + 8u * tid), "f"(aux->m_fin[h]),
-                     "f"(aux->l_fin[h])
-                     : "memory");
+        reinterpret_cast<float2*>(x_out + 8 * D * 4)[tid] = make_float2(aux->m_fin[h], aux->l_fin[h]);
       }
     }
-    if (tid == 0) tma::mbar_arrive_expect_tx(smem_u32(&aux->pair_in), kSendBytes);
-    tc::fence_proxy_async();  // the staged half is read by the copy engine
-    // both CTAs: rings idle, receive barrier armed, half staged
     cluster_sync();
-    if (tid == 0)
-      bulk_to_peer(mapa(sRecv, uint32_t(pr)), sSend, kSendBytes, mapa(smem_u32(&aux->pair_in), uint32_t(pr)));
-    // every thread: the peer's half has landed (bounded wait, cluster acquire)
-    mbar_wait_cluster(smem_u32(&aux->pair_in), 0, a.status, a.wait_limit);
-    // tell the peer its copy has landed (it may then release the shared
-    // memory the copy read)
-    if (tid == 0) mbar_arrive_remote(mapa(smem_u32(&aux->pair_done), uint32_t(pr)));
     if (tid < 32) {
       const int h = 32 * r + tid;
-      const float* rml = reinterpret_cast<const float*>(smem + kOffRing + 65536) + 2 * tid;
-      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = rml[0], lp = rml[1];
+      const float2 pml = __ldcg(reinterpret_cast<const float2*>(x_in + 8 * D * 4) + tid);
+      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = pml.x, lp = pml.y;
       const float m0 = r == 0 ? mo : mp, l0 = r == 0 ? lo : lp, m1 = r == 0 ? mp : mo, l1 = r == 0 ? lp : lo;
       const float sk = a.sink[h] * kLog2e;
       const float Mx = fmaxf(fmaxf(m0, m1), sk);
@@ -755,26 +692,28 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     }
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const uint32_t addr = sRecv + row_off + ((uint32_t(c ^ (d & 7))) << 4);
-      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                   : "=f"(peer[4 * c]), "=f"(peer[4 * c + 1]), "=f"(peer[4 * c + 2]), "=f"(peer[4 * c + 3])
-                   : "r"(addr));
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(x_in) + c * D + d);
+      peer[4 * c] = v.x;
+      peer[4 * c + 1] = v.y;
+      peer[4 * c + 2] = v.z;
+      peer[4 * c + 3] = v.w;
     }
     __syncthreads();  // coefficients
+    // out[h][d]: lanes d, d ^ 1 trade one value per head pair so that each
+    // store writes two adjacent dims (even lane: head i, odd lane: head i + 1)
+    __nv_bfloat16* om = a.out + (int64_t(mrow) * H + 32 * r) * D;
+    const bool odd = lane & 1;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float x0 = r == 0 ? own[i] : peer[i], x1 = r == 0 ? peer[i] : own[i];
-      const __nv_bfloat16 v = f2bf(fmaf(aux->coef[1][i], x1, aux->coef[0][i] * x0));
-      asm volatile("st.shared.b16 [%0], %1;" ::"r"(sOut + uint32_t(i * D + d) * 2u),
-                   "h"(*reinterpret_cast<const unsigned short*>(&v))
-                   : "memory");
-    }
-    tc::fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-      bulk_store_wait_read(a.out + (int64_t(mrow) * H + 32 * r) * D, sOut, 32 * D * 2);
-      // this CTA's outgoing copy has been received before its shared memory goes
-      mbar_wait_cluster(smem_u32(&aux->pair_done), 0, a.status, a.wait_limit);
+    for (int i = 0; i < 32; i += 2) {
+      const float x0a = r == 0 ? own[i] : peer[i], x1a = r == 0 ? peer[i] : own[i];
+      const float x0b = r == 0 ? own[i + 1] : peer[i + 1], x1b = r == 0 ? peer[i + 1] : own[i + 1];
+      const float va = fmaf(aux->coef[1][i], x1a, aux->coef[0][i] * x0a);
+      const float vb = fmaf(aux->coef[1][i + 1], x1b, aux->coef[0][i + 1] * x0b);
+      const float got = __shfl_xor_sync(0xffffffffu, odd ? va : vb, 1);
+      if (odd)
+        *reinterpret_cast<uint32_t*>(om + (i + 1) * D + d - 1) = pack_bf16x2(got, vb);
+      else
+        *reinterpret_cast<uint32_t*>(om + i * D + d) = pack_bf16x2(va, got);
     }
   } else {
     const int sp = warp & 3, jb = warp >> 2;
