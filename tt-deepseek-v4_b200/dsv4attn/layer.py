@@ -279,13 +279,16 @@ class DecodePath:
     def replay(self) -> None:
         self.graph.replay()
 
-    kernels_per_layer = 8  # launches per layer when the split-K combine is not needed
+    kernels_per_layer = 8  # launches per layer without a split-K combine launch
 
     def launches_per_step(self) -> int:
-        n = 0
         L0 = self.layers[0]
-        extra = 1 if ops.lib().dsa_sparse_attn_workspace_size(self.B, 1, self.args.n_heads, self.args.head_dim,
-                                                                L0.win + L0.k) else 0
+        H, D = self.args.n_heads, self.args.head_dim
+        ws = int(ops.lib().dsa_sparse_attn_workspace_size(self.B, 1, H, D, L0.win + L0.k))
+        nsplit = ws // (self.B * H * (2 * 4 + D * 2)) if ws else 1
+        # a row's two key splits combine inside the attention; more need the
+        # combine launch
+        extra = 1 if nsplit > 2 else 0
         topk2 = 1 if ops.lib().dsa_indexer_topk_workspace_size(self.B, L0.T_max, L0.k) else 0
         n = len(self.layers) * (self.kernels_per_layer + extra + topk2)
         return n + 2  # + the position advance and t_prev
