@@ -395,15 +395,17 @@ def test_sparse_attn_ex_rejects_bad_lead(cuda_dev):
     assert rc != 0 and "lead_cols" in _lib.last_error()
 
 
+@pytest.mark.parametrize("B", [24, 80])
 @pytest.mark.parametrize("kind", ["gauss", "ties", "const_rows", "wide", "nan", "short"])
-def test_topk_position_order_equals_sorted_selection(cuda_dev, kind):
+def test_topk_position_order_equals_sorted_selection(cuda_dev, kind, B):
     # the position-order top-k (one row per CTA, its own first level) and
     # the sorted top-k (the general select) pick exactly the same indices:
     # the k largest, ties to the lowest positions -- no near-tie allowance.
-    # Rows the position-order kernel hands to the general select (constant
-    # rows, huge ranges, NaN, fewer than k live entries) included.
+    # Rows the position-order kernels hand to the general select (constant
+    # rows, huge ranges, NaN, fewer than k live entries) included; 24 rows
+    # run two CTAs per row (a cluster pair), 80 rows one CTA per row.
     from dsv4attn import ops
-    B, T, k, W = 24, 9216, 2048, 128
+    T, k, W = 9216, 2048, 128
     g = torch.Generator().manual_seed(hash(kind) % 1000)
     s = torch.randn(B, T, generator=g) * (0.8 + torch.rand(B, 1, generator=g)) + 3 * (torch.rand(B, 1, generator=g) - .5)
     if kind == "ties":

@@ -753,6 +753,277 @@ __global__ void __launch_bounds__(kTopkThreads) topk_row_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// One row per 2-CTA cluster (the decode step's case with few rows: 2 B CTAs
+// fit the SMs).  CTA c of the pair takes positions [c * half, ...) of the
+// row, in the warp-contiguous register layout of topk_row_kernel, so each
+// CTA bins, gathers and emits half the keys; the two exchange only small
+// values through distributed shared memory: (min, max, live count), the
+// first level's 255-bin histogram, the threshold bin's keys (at most
+// kRankMax in all) and, for the compaction, their counts of keys above and
+// equal to the threshold.  Both CTAs then hold the same histogram and the
+// same survivors, find the same threshold, and write their own keys'
+// slots - the lower half's first: the same output as topk_row_kernel.
+// Rows the first level cannot settle take the general select over the whole
+// row in both CTAs.
+struct PairExchange {
+  uint32_t mm[3];              // the peer's (min, max, live count)
+  uint32_t ncand;              // the peer's keys in the threshold bin
+  uint32_t tot[2];             // the peer's keys above / equal to the threshold
+  uint32_t hist[256];          // the peer's first-level histogram
+  uint32_t cand[kRankMax];     // the peer's keys in the threshold bin
+};
+
+__device__ __forceinline__ uint32_t cl_mapa(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cl_st(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void cl_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cl_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cl_sync() {
+  cl_arrive();
+  cl_wait();
+}
+
+__global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
+    const float* __restrict__ score, int64_t ld_score, const int32_t* __restrict__ t_active, int n, int k, int win,
+    int mask_mode, int32_t* __restrict__ out_idx, float* __restrict__ out_score, int64_t ld_out) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ SelectScratch s;
+  __shared__ PairExchange px;
+  __shared__ uint32_t rank_gt[kRankMax], rank_ge[kRankMax];
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);  // this CTA's keys by local position; the whole row on fallback
+  uint8_t* bins = smem + kTopkMaxN * 4;
+  uint32_t* cand = reinterpret_cast<uint32_t*>(smem + kTopkMaxN * 8);
+  const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t peer = uint32_t(c ^ 1);
+  const int half = min(n, (((n + 1) >> 1) + 31) & ~31);
+  const int p0 = c ? half : 0, cnt_pos = c ? n - half : half;  // this CTA's positions [p0, p0 + cnt_pos)
+  const int per = (cnt_pos + kTopkThreads - 1) / kTopkThreads;
+  const int base = warp * 32 * per + lane;  // local position of r[j]: base + 32 j
+  if (tid < 256) s.hist[tid] = 0;
+  if (tid < kRankMax) {
+    rank_gt[tid] = 0;
+    rank_ge[tid] = 0;
+  }
+  if (tid == 0) s.ncand = 0;
+  // both CTAs have started before either writes the other's shared memory
+  cl_arrive();
+  pdl_wait();
+  pdl_launch_dependents();
+  const int ta = t_active[b];
+  const float* row = score + int64_t(b) * ld_score;
+  uint32_t r[kKeysPerThread];
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    const int i = base + 32 * j;
+    r[j] = (j < per && i < cnt_pos) ? __float_as_uint(__ldg(row + p0 + i)) : 0u;
+  }
+  const uint32_t kfloor = float_key(-INFINITY);
+  auto mask_key = [&](int pos, float v) {
+    return float_key(pos < ta ? v : (mask_mode ? -INFINITY : __fsub_rn(v, 1.0e4f)));
+  };
+  uint32_t lo = 0xffffffffu, hi = 0u, cnt = 0;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= per) break;
+    const int i = base + 32 * j;
+    if (i < cnt_pos) {
+      const uint32_t key = mask_key(p0 + i, __uint_as_float(r[j]));
+      r[j] = key;
+      keys[i] = key;
+      if (key > kfloor) {
+        ++cnt;
+        lo = min(lo, key);
+        hi = max(hi, key);
+      }
+    }
+  }
+  uint32_t mn, mx, n_live;
+  block_minmax_sum(lo, hi, cnt, &s, mn, mx, n_live);
+  cl_wait();
+  if (tid == 0) {
+    const uint32_t dst = cl_mapa(smem_u32(&px.mm[0]), peer);
+    cl_st(dst, mn);
+    cl_st(dst + 4, mx);
+    cl_st(dst + 8, n_live);
+  }
+  cl_sync();
+  mn = min(mn, px.mm[0]);
+  mx = max(mx, px.mm[1]);
+  n_live += px.mm[2];
+  const float vmin = key_float(mn), vmax = key_float(mx);
+  const float scale = 254.99f / (vmax - vmin);
+  // uniform across both CTAs: every input to it was exchanged
+  bool fast = n_live >= uint32_t(k) && mx != mn && isfinite(vmin) && isfinite(vmax) && isfinite(scale) &&
+              scale > 0.f;
+  uint32_t thr = 0;
+  if (fast) {
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      if (j >= per) break;
+      const int i = base + 32 * j;
+      uint32_t bin = kRowNoBin;
+      if (i < cnt_pos && r[j] > kfloor) {
+        const float d = key_float(r[j]) - vmin;
+        bin = min(__float_as_uint(fmaf(d, scale, kRoundMagic)) - __float_as_uint(kRoundMagic), 254u);
+      }
+      if (i < cnt_pos) bins[i] = uint8_t(bin);
+      const uint32_t lead = __shfl_sync(0xffffffffu, bin, 0);
+      const unsigned same = __ballot_sync(0xffffffffu, bin == lead);
+      if (bin == lead) {
+        if (lane == __ffs(same) - 1 && lead != kRowNoBin) atomicAdd(&s.hist[lead], uint32_t(__popc(same)));
+      } else if (bin != kRowNoBin) {
+        atomicAdd(&s.hist[bin], 1u);
+      }
+    }
+    __syncthreads();
+    if (tid < 256) cl_st(cl_mapa(smem_u32(&px.hist[tid]), peer), s.hist[tid]);
+    cl_sync();
+    if (tid < 256) s.hist[tid] += px.hist[tid];
+    __syncthreads();
+    pick_bin(k, &s);
+    const uint32_t bin = s.prefix;
+    const uint32_t kl = uint32_t(k) - s.kgt;
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      if (j >= per) break;
+      const int i = base + 32 * j;
+      const bool hit = i < cnt_pos && bins[i] == bin;
+      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (m) {
+        uint32_t o = 0;
+        if (lane == 0) o = atomicAdd(&s.ncand, uint32_t(__popc(m)));
+        o = __shfl_sync(0xffffffffu, o, 0);
+        if (hit) cand[o + __popc(m & ((1u << lane) - 1u))] = r[j];
+      }
+    }
+    __syncthreads();
+    const int nc_own = int(s.ncand);
+    if (tid == 0) cl_st(cl_mapa(smem_u32(&px.ncand), peer), uint32_t(nc_own));
+    if (nc_own <= kRankMax && tid < nc_own) cl_st(cl_mapa(smem_u32(&px.cand[tid]), peer), cand[tid]);
+    cl_sync();
+    const int nc_peer = int(px.ncand);
+    const int nc = nc_own + nc_peer;
+    if (nc_own <= kRankMax && nc_peer <= kRankMax && nc <= kRankMax) {
+      // the union of both halves' survivors (same multiset on both CTAs)
+      if (tid < nc_peer) cand[nc_own + tid] = px.cand[tid];
+      __syncthreads();
+      const int ci = tid & (kRankMax - 1), qt = tid / kRankMax;
+      constexpr int kParts = kTopkThreads / kRankMax;
+      if (ci < nc) {
+        const uint32_t cv = cand[ci];
+        const int u0 = (nc * qt) / kParts, u1 = (nc * (qt + 1)) / kParts;
+        uint32_t gt = 0, ge = 0;
+        for (int u = u0; u < u1; ++u) {
+          const uint32_t x = cand[u];
+          gt += x > cv;
+          ge += x >= cv;
+        }
+        if (u1 > u0) {
+          atomicAdd(&rank_gt[ci], gt);
+          atomicAdd(&rank_ge[ci], ge);
+        }
+      }
+      __syncthreads();
+      if (tid < nc && rank_gt[tid] < kl && kl <= rank_ge[tid]) s.prefix = cand[tid];
+      __syncthreads();
+      thr = s.prefix;
+    } else {
+      fast = false;
+    }
+  }
+  if (!fast) {
+    // the general select over the whole row, in both CTAs
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      const int i = tid + j * kTopkThreads;
+      r[j] = i < n ? mask_key(i, __ldg(row + i)) : 0u;
+      if (i < n) keys[i] = r[j];
+    }
+    __syncthreads();
+    kth_key_select(r, keys, n, k, &s, cand);
+    thr = s.prefix;
+#pragma unroll
+    for (int j = 0; j < kKeysPerThread; ++j) {
+      const int i = base + 32 * j;
+      r[j] = (j < per && i < cnt_pos) ? keys[p0 + i] : 0u;
+    }
+  }
+  // compaction: this CTA's keys above thr, then the lowest-position keys
+  // equal to it; the lower half's counts come first
+  uint32_t ca = 0, ce = 0;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= per) break;
+    const bool valid = base + 32 * j < cnt_pos;
+    ca += __popc(__ballot_sync(0xffffffffu, valid && r[j] > thr));
+    ce += __popc(__ballot_sync(0xffffffffu, valid && r[j] == thr));
+  }
+  if (lane == 0) {
+    s.warp_cnt[0][warp] = ca;
+    s.warp_cnt[1][warp] = ce;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t wa = s.warp_cnt[0][lane], we = s.warp_cnt[1][lane];
+    uint32_t xa = wa, xe = we;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t va = __shfl_up_sync(0xffffffffu, xa, o), ve = __shfl_up_sync(0xffffffffu, xe, o);
+      if (lane >= o) {
+        xa += va;
+        xe += ve;
+      }
+    }
+    s.warp_cnt[0][lane] = xa - wa;
+    s.warp_cnt[1][lane] = xe - we;
+    if (lane == 31) {
+      const uint32_t dst = cl_mapa(smem_u32(&px.tot[0]), peer);
+      cl_st(dst, xa);
+      cl_st(dst + 4, xe);
+      s.part[0][0] = xa;
+      s.part[0][1] = xe;
+    }
+  }
+  cl_sync();  // also the last access of either CTA's shared memory by the other
+  const uint32_t a0 = c ? px.tot[0] : s.part[0][0], a1 = c ? s.part[0][0] : px.tot[0];
+  const uint32_t e0 = c ? px.tot[1] : 0u;
+  const int n_above = int(a0 + a1);  // < k by the choice of thr
+  const int n_eq_take = k - n_above;
+  uint32_t oa = s.warp_cnt[0][warp] + (c ? a0 : 0u), oe = s.warp_cnt[1][warp] + e0;
+  const uint32_t lt = (1u << lane) - 1u;
+  int32_t* orow = out_idx + int64_t(b) * ld_out;
+  float* srow = out_score ? out_score + int64_t(b) * ld_out : nullptr;
+#pragma unroll
+  for (int j = 0; j < kKeysPerThread; ++j) {
+    if (j >= per) break;
+    const int i = base + 32 * j;
+    const bool valid = i < cnt_pos;
+    const bool above = valid && r[j] > thr, eq = valid && r[j] == thr;
+    const uint32_t ma = __ballot_sync(0xffffffffu, above), me = __ballot_sync(0xffffffffu, eq);
+    int slot = -1;
+    if (above) {
+      slot = int(oa + __popc(ma & lt));
+    } else if (eq) {
+      const int re = int(oe + __popc(me & lt));
+      if (re < n_eq_take) slot = n_above + re;
+    }
+    oa += __popc(ma);
+    oe += __popc(me);
+    if (slot >= 0) {
+      const float f = key_float(r[j]);
+      orow[slot] = f >= -1000.0f ? p0 + i + win : -1;
+      if (srow) srow[slot] = f;
+    }
+  }
+}
+
 __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ idx, int64_t ld,
                                       int B, int win) {
   pdl_wait();
@@ -813,7 +1084,29 @@ static int topk_launch(const float* score, int64_t ld_score, const int32_t* t_ac
     cudaFuncSetAttribute(topk_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk_smem());
     cudaFuncSetAttribute(topk_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, merge_smem());
     cudaFuncSetAttribute(topk_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk_smem());
+    cudaFuncSetAttribute(topk_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk_smem());
     attr_dev = dev;
+  }
+  if (T <= kTopkMaxN && !sort_desc && fq == nullptr && 2 * B <= num_sms()) {
+    // few rows: two CTAs per row (a cluster pair)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, B);
+    cfg.blockDim = dim3(kTopkThreads);
+    cfg.dynamicSmemBytes = chunk_smem();
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, topk_pair_kernel, score, ld_score, t_active, T, k, win, mask_mode, out_idx, out_score,
+                       ld_out);
+    DSA_CHECK_LAUNCH("indexer_topk");
+    return DSA_OK;
   }
   if (T <= kTopkMaxN && !sort_desc) {
     launch_pdl(topk_row_kernel, dim3(B), dim3(kTopkThreads), chunk_smem(), st, score, ld_score, t_active, T, k, win,
