@@ -242,10 +242,14 @@ def time_kernels(path, inputs, outs, reps=3):
                                                     t_valid=path.t_active) for L, x in zip(path.layers, inputs)])
     run("indexer_topk", lambda: [ops.indexer_topk(L.score, path.t_active, L.k, L.win, T=L.T_max, mask_mode=1,
                                                   out=L.idx[:, L.win:], ws=L.ws) for L in path.layers])
-    # the newest row's score: the step runs it on the compressor's branch,
-    # beside indexer_score
-    run("indexer_score_newest", lambda: [ops.indexer_score_newest(x.iq, L.idx_cache, x.iw, path.t_active, L.T_max,
-                                                                  out=L.score) for L, x in zip(path.layers, inputs)])
+    # the layer's small stages in one launch (the step runs it beside the
+    # indexer score; timed alone here)
+    a = path.args
+    run("layer_prologue", lambda: [ops.layer_prologue(
+        (x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, L.idx_cache),
+        (x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, L.kv_cache), path.cos, path.sin, path.pos,
+        path.t_active, x.iq, x.iw, L.score, L.T_max, x.kv, L.idx, L.win, L.ratio, eps=a.norm_eps,
+        rope_dim=a.rope_head_dim) for L, x in zip(path.layers, inputs)])
     return res
 
 

@@ -190,6 +190,50 @@ int dsa_compressor_step(const void* kv_row, const void* score_row, int64_t ld_ro
                         int overlap, int rotate, int write_state, float eps,
                         dsa_stream_t stream);
 
+/* One compressor's arguments, as for dsa_compressor_step (the state is
+ * always written; no emitted flags). */
+typedef struct dsa_compressor_args {
+  const void* kv_row;
+  const void* score_row;
+  int64_t ld_row;
+  const float* ape;
+  float* kv_state;
+  float* score_state;
+  const float* gamma;
+  void* kv_cache;
+  int64_t cache_bstride;
+  int64_t cache_rows;
+  int slot_offset;
+  int d, rope_dim, ratio, overlap, rotate;
+} dsa_compressor_args;
+
+/* A decode layer's small per-sequence stages in one launch, B sequences:
+ *   dsa_compressor_step(*icmp) then dsa_indexer_score_newest on its cache
+ *     (icmp->kv_cache [B, >= T, 128], q iq [B, 64, 128] bf16, w iw [B, 64]
+ *     fp32, score [B, ld_score] fp32, t_active);
+ *   dsa_kv_window_write(kv [B, D] bf16 into cmp->kv_cache's ring rows,
+ *     kv_scales may be NULL, win), dsa_window_indices(idx[:, 0:win]) and
+ *     dsa_compressor_step(*cmp) on the same cache;
+ * cos/sin [n_pos, rope_dim/2], pos [B] and eps shared (inference.py:
+ * 4938-5097, 5997-6006, 6020-6026, 5260-5275).  Same results as those five
+ * calls.  DSA_BESIDE_PREVIOUS: the caller guarantees that every input was
+ * complete when the previous kernel on the stream began and that the
+ * previous kernel neither writes what this call reads nor reads or writes
+ * what it writes (in a decode step: the indexer score, which covers rows
+ * [0, t_active - 1) while this call writes row t_active - 1 of the indexer
+ * cache and of score).  The kernel then runs beside that kernel, letting the
+ * next kernel launch early, and waits for it only before completing, so a
+ * successor that waits for this call also sees the previous kernel's
+ * writes.  No counterpart as one call in the reference (five device
+ * chains). */
+enum { DSA_BESIDE_PREVIOUS = 1 };
+int dsa_layer_prologue(const dsa_compressor_args* icmp, const dsa_compressor_args* cmp,
+                       const float* cos_tab, const float* sin_tab, int n_pos, float eps,
+                       const int32_t* pos, const int32_t* t_active, const void* iq, const float* iw,
+                       float* score, int64_t ld_score, int T, const void* kv, float* kv_scales, int D,
+                       int rope_dim, int win, int32_t* idx, int64_t ld_idx, int B, unsigned flags,
+                       dsa_stream_t stream);
+
 /* ------------------------------------------------------------- attn.topk */
 
 /* Window ring indices for B sequences: idx[b, i] for i < win is the

@@ -32,14 +32,9 @@ __global__ void __launch_bounds__(256) indexer_score_newest_kernel(
     const float* __restrict__ w, const int32_t* __restrict__ t_active, float* __restrict__ score, int64_t ld_score,
     int T) {
   __shared__ float s_dot[kRowHeads];
-  const int b = blockIdx.x;
   pdl_wait();
   pdl_launch_dependents();
-  const int t = min(t_active[b], T) - 1;
-  if (t < 0) return;  // uniform across the block
-  const float sc = indexer_row_score(q + int64_t(b) * kRowHeads * kRowDim, k + int64_t(b) * k_bstride +
-                                     int64_t(t) * kRowDim, w + int64_t(b) * kRowHeads, s_dot);
-  if (threadIdx.x == 0) score[int64_t(b) * ld_score + t] = sc;
+  score_newest_row(q, k, k_bstride, w, t_active, score, ld_score, T, blockIdx.x, s_dot);
 }
 
 }  // namespace dsa

@@ -41,4 +41,19 @@ __device__ __forceinline__ float indexer_row_score(const __nv_bfloat16* __restri
   return sc;
 }
 
+// The score of sequence b's newest live row, t = min(t_active[b], T) - 1,
+// into score[b, t] (nothing when t < 0): indexer_score_newest_kernel
+// (indexer.cu) and the decode layer's prologue kernel (prologue.cu).
+__device__ __forceinline__ void score_newest_row(const __nv_bfloat16* __restrict__ q,
+                                                 const __nv_bfloat16* __restrict__ k, int64_t k_bstride,
+                                                 const float* __restrict__ w, const int32_t* __restrict__ t_active,
+                                                 float* __restrict__ score, int64_t ld_score, int T, int b,
+                                                 float* s_dot) {
+  const int t = min(t_active[b], T) - 1;
+  if (t < 0) return;  // uniform across the block
+  const float sc = indexer_row_score(q + int64_t(b) * kRowHeads * kRowDim, k + int64_t(b) * k_bstride +
+                                     int64_t(t) * kRowDim, w + int64_t(b) * kRowHeads, s_dot);
+  if (threadIdx.x == 0) score[int64_t(b) * ld_score + t] = sc;
+}
+
 }  // namespace dsa

@@ -22,6 +22,7 @@
 // (dsa_topk_merge), which is also the cross-GPU merge of the sequence split.
 #include "common.cuh"
 #include "indexer_row.cuh"
+#include "window_rows.cuh"
 
 namespace dsa {
 
@@ -1028,14 +1029,7 @@ __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* 
                                       int B, int win) {
   pdl_wait();
   pdl_launch_dependents();
-  const int b = blockIdx.x;
-  const int p = pos[b];
-  for (int i = threadIdx.x; i < win; i += blockDim.x) {
-    int v;
-    if (p < win) v = (i <= p) ? i : -1;
-    else v = (p % win + 1 + i) % win;
-    idx[int64_t(b) * ld + i] = v;
-  }
+  window_indices_row(pos, idx, ld, win, blockIdx.x);
 }
 
 }  // namespace dsa

@@ -27,6 +27,17 @@ I64 = ctypes.c_int64
 F32 = ctypes.c_float
 SZ = ctypes.c_size_t
 
+DSA_BESIDE_PREVIOUS = 1  # dsa_layer_prologue flag
+
+
+class CompressorArgs(ctypes.Structure):
+    """dsa_compressor_args (include/dsv4attn.h)."""
+    _fields_ = [("kv_row", P), ("score_row", P), ("ld_row", I64), ("ape", P), ("kv_state", P),
+                ("score_state", P), ("gamma", P), ("kv_cache", P), ("cache_bstride", I64), ("cache_rows", I64),
+                ("slot_offset", I32), ("d", I32), ("rope_dim", I32), ("ratio", I32), ("overlap", I32),
+                ("rotate", I32)]
+
+
 # name -> (restype, argtypes); must match include/dsv4attn.h
 PROTOTYPES = {
     "dsa_version": (I32, []),
@@ -47,6 +58,8 @@ PROTOTYPES = {
     "dsa_window_indices": (I32, [P, P, I64, I32, I32, P]),
     "dsa_indexer_score": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, P]),
     "dsa_indexer_score_ex": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, I32, P]),
+    "dsa_layer_prologue": (I32, [ctypes.POINTER(CompressorArgs), ctypes.POINTER(CompressorArgs), P, P, I32, F32, P,
+                                  P, P, P, P, I64, I32, P, P, I32, I32, I32, P, I64, I32, ctypes.c_uint, P]),
     "dsa_indexer_score_newest": (I32, [P, P, I64, P, P, P, I64, I32, I32, P]),
     "dsa_indexer_topk": (I32, [P, I64, P, P, P, I64, I32, I32, I32, I32, I32, I32, P]),
     "dsa_indexer_topk_workspace_size": (SZ, [I32, I32, I32]),

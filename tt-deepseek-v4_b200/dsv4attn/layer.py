@@ -16,25 +16,26 @@ allocate in the reference, inference.py:4757-4813, 5460-5580):
 ``DecodePath`` runs one decode step over a stack of layers in the
 reference's order (inference.py:5888-6093):
 
-    attn.kv          kv_window_write      act_quant(nope) + ring write
-    attn.topk        window_indices       ring slots of the window
-                     compressor_step      indexer compressor (emit on device)
-                     indexer_score_newest the newest row's score (side branch)
-                     indexer_score        relu-weighted multi-head scores
-                     indexer_topk         k best compressed rows (+W, -1)
-    attn.compress    compressor_step      attention compressor (emit on device)
+    attn.topk        indexer_score        relu-weighted multi-head scores
+    (prologue)       layer_prologue       the indexer compressor (emit on
+                                          device) and the newest row's score;
+                                          attn.kv act_quant(nope) + ring
+                                          write; the window's ring slots;
+                                          attn.compress (emit on device)
+    attn.topk        indexer_topk         k best compressed rows (+W, -1)
     attn.sparse      sparse_attn          gather + sink softmax attention
 
 and then advances the device-resident positions, so a captured CUDA graph
 of the whole step can be replayed without any host work (the reference
 needs two traces and host staging per step, inference.py:7498-7543).  The
-window write, the attention compressor and the indexer compressor run on a
-side stream in parallel with the indexer score (a parallel branch of the
-captured graph): the score covers the compressed rows before the newest,
-the side branch scores the newest row after its compressor
-(dsa_indexer_score_newest), and the top-k runs after the join -- the same
-selection as scoring after the compressor, with the compressor and the
-newest row's score off the critical path.
+four kernels of a layer form one chain of programmatic dependent launches
+on one stream.  The score covers the compressed rows before the newest;
+the prologue (dsa_layer_prologue), which writes at most the newest row and
+that row's score, runs beside it and completes after it; the top-k then
+finds every live score in place -- the same selection as scoring after the
+compressor, with the compressors and the small stages off the critical
+path.  (Side streams joined before the top-k and the attention turned
+those programmatic launches into full dependencies, ~4 us each.)
 """
 
 from __future__ import annotations
@@ -188,16 +189,11 @@ class DecodePath:
         self.pos = torch.zeros(self.B, dtype=I32, device=self.device)
         self.t_active = torch.zeros(self.B, dtype=I32, device=self.device)
         # t_active - 1: the indexer scores the rows before the newest, which
-        # the indexer compressor may write in the same step (the top-k
-        # recomputes that one row after the join)
+        # the indexer compressor may write in the same step (the prologue
+        # scores that one row after its compressor)
         self.t_prev = torch.zeros(self.B, dtype=I32, device=self.device)
         self.status = torch.zeros(1, dtype=I32, device=self.device)
         self.graph = None
-        # the window write and the attention compressor depend on nothing of
-        # the indexer chain: they run on a side stream, joined before attention
-        self.side = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
-        # the indexer compressor: its own branch, joined before the top-k
-        self.side_idx = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
 
     def set_positions(self, pos) -> None:
         """Stage the current decode position(s) (pre_stage_decode,
@@ -210,46 +206,32 @@ class DecodePath:
     def layer_step(self, L: DecodeLayer, x: LayerInputs, out: torch.Tensor) -> None:
         a = self.args
         W, r = L.win, L.ratio
-        main = torch.cuda.current_stream(self.device)
-        side = self.side
-        # side branch 1: the indexer's compressor (joined before the top-k)
-        side_idx = self.side_idx
-        side_idx.wait_stream(main)
-        with torch.cuda.stream(side_idx):
-            ops.compressor_step(x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, self.cos,
-                                self.sin, L.idx_cache, 0, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
-                                rope_dim=a.rope_head_dim)
-            # the newest live row's score (t_active - 1), after the
-            # compressor that may have written that row; the main branch
-            # scores the rows before it
-            ops.indexer_score_newest(x.iq, L.idx_cache, x.iw, self.t_active, L.T_max, out=L.score)
-        # side branch 2: attn.kv window write, the window ring indices and
-        # attn.compress (all three only feed the attention)
-        side.wait_stream(main)
-        with torch.cuda.stream(side):
-            ops.kv_window_write(x.kv, L.kv_cache, self.pos, W, rope_dim=a.rope_head_dim)
-            ops.window_indices(self.pos, W, out=L.idx[:, :W])
-            ops.compressor_step(x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, self.cos, self.sin,
-                                L.kv_cache, W, self.pos, r, overlap=True, rotate=False, eps=a.norm_eps,
-                                rope_dim=a.rope_head_dim)
-        # main branch: attn.topk.  The score covers the rows before the
-        # newest (t_prev = t_active - 1), which the indexer compressor may be
-        # writing meanwhile; the compressor's branch scores that row after
-        # it, and the top-k runs after joining it.  The top-k writes
-        # idx[:, W:], disjoint from the window columns.
-        # keys_ready: the key rows scored here were written by earlier steps
-        # and t_prev before the first layer, so from the second layer on the
-        # kernel's first key tiles may be requested before the previous
-        # layer's last kernel ends (the first layer may directly follow the
-        # kernel that writes t_prev)
+        # One stream, every hand-over a programmatic dependent launch:
+        #   indexer score -> prologue -> top-k -> attention.
+        # attn.topk's score covers the compressed rows before the newest
+        # (t_prev = t_active - 1).  keys_ready: the rows it scores were
+        # written by earlier steps and t_prev before the first layer, so from
+        # the second layer on its first key tiles are requested before the
+        # previous layer's last kernel ends (the first layer may directly
+        # follow the kernel that writes t_prev).
         ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_prev,
                           keys_ready=L is not self.layers[0])
-        main.wait_stream(side_idx)
+        # The prologue: the indexer compressor (it may write row t_active - 1
+        # of the indexer cache) and that row's score, the window-ring KV
+        # write (attn.kv), the window indices and attn.compress.  None of it
+        # touches what the score reads or writes, so it runs beside the
+        # score and waits for it only before completing: the top-k, which
+        # waits for the prologue, sees every live score in place.
+        ops.layer_prologue((x.icmp_kv, x.icmp_score, L.iape, L.icmp_kv, L.icmp_sc, L.igamma, L.idx_cache),
+                           (x.cmp_kv, x.cmp_score, L.ape, L.cmp_kv, L.cmp_sc, L.gamma, L.kv_cache),
+                           self.cos, self.sin, self.pos, self.t_active, x.iq, x.iw, L.score, L.T_max, x.kv, L.idx,
+                           W, r, eps=a.norm_eps, rope_dim=a.rope_head_dim, beside_previous=True)
+        # the top-k writes idx[:, W:], disjoint from the window columns
         ops.indexer_topk(L.score, self.t_active, L.k, W, T=L.T_max, mask_mode=1, out=L.idx[:, W:], ws=L.ws)
-        main.wait_stream(side)
-        # the window columns of idx, q and the window rows were written before
-        # the top-k began (side branch, inputs): each key split requests its
-        # window tile before waiting for the top-k
+        # the window columns of idx, q and the window rows were complete when
+        # the attention was launched (the top-k lets it launch only after its
+        # own wait, i.e. after the prologue completed): each key split
+        # requests its window tile before waiting for the top-k
         ops.sparse_attn(x.q, L.kv_cache, L.idx, L.sink, self.scale, out=out, ws=L.ws, status=self.status,
                         lead_cols=W, lead_ready=True)
 
@@ -279,7 +261,7 @@ class DecodePath:
     def replay(self) -> None:
         self.graph.replay()
 
-    kernels_per_layer = 8  # launches per layer without a split-K combine launch
+    kernels_per_layer = 4  # launches per layer without a split-K combine launch
 
     def launches_per_step(self) -> int:
         L0 = self.layers[0]

@@ -8,8 +8,11 @@ all buffers persistent (CUDA-graph capture); nothing here synchronises.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
+from . import _lib
 from ._lib import DSA_KEYS_READY, check, lib
 
 BF16 = torch.bfloat16
@@ -349,6 +352,66 @@ def compressor_step(kv_row, score_row, ape, kv_state, score_state, gamma, cos, s
                                     slot_offset, pos.data_ptr(), _ptr(emitted), B, d, rope_dim, ratio,
                                     int(overlap), int(rotate), int(write_state), eps, _stream(kv_state)),
           "compressor_step")
+
+
+def _cmp_args(kv_row, score_row, ape, kv_state, score_state, gamma, kv_cache, slot_offset: int, ratio: int,
+              overlap: bool, rotate: bool, rope_dim: int) -> "_lib.CompressorArgs":
+    for t, n in ((kv_state, "kv_state"), (score_state, "score_state"), (gamma, "gamma"), (ape, "ape")):
+        _need(t, n, F32)
+        _contig(t, n)
+    _need(kv_row, "kv_row", BF16)
+    _need(score_row, "score_row", BF16)
+    _need(kv_cache, "kv_cache", BF16)
+    B = kv_state.shape[0]
+    d = gamma.shape[0]
+    coff = 2 if overlap else 1
+    if tuple(kv_state.shape) != (B, coff * ratio, coff * d) or kv_state.shape != score_state.shape:
+        raise ValueError(f"state must be [B, {coff * ratio}, {coff * d}], got {tuple(kv_state.shape)}")
+    if kv_cache.dim() != 3 or kv_cache.shape[2] != d or kv_cache.stride(1) != d:
+        raise ValueError("kv_cache must be [B, rows, d] with contiguous rows")
+    if kv_row.shape[-1] != coff * d or kv_row.stride(-1) != 1 or score_row.stride() != kv_row.stride():
+        raise ValueError("kv_row/score_row must be [B, coff*d] with matching strides")
+    return _lib.CompressorArgs(kv_row.data_ptr(), score_row.data_ptr(), kv_row.stride(0), ape.data_ptr(),
+                               kv_state.data_ptr(), score_state.data_ptr(), gamma.data_ptr(), kv_cache.data_ptr(),
+                               kv_cache.stride(0), kv_cache.shape[1], slot_offset, d, rope_dim, ratio, int(overlap),
+                               int(rotate))
+
+
+def layer_prologue(icmp: tuple, cmp: tuple, cos, sin, pos, t_active, iq, iw, score, T: int, kv, idx, win: int,
+                   ratio: int, eps: float = 1e-6, rope_dim: int = 64, overlap: bool = True, rotate: bool = False,
+                   kv_scales=None, beside_previous: bool = False) -> None:
+    """A decode layer's small stages as one launch (dsa_layer_prologue):
+    ``compressor_step(*icmp, slot_offset=0)`` then ``indexer_score_newest``
+    on its cache, and ``kv_window_write(kv, cache)``, ``window_indices(pos,
+    win, out=idx[:, :win])``, ``compressor_step(*cmp, slot_offset=win)`` on
+    the attention cache.  icmp / cmp = (kv_row, score_row, ape, kv_state,
+    score_state, gamma, kv_cache).  ``beside_previous``: run beside the
+    previous kernel on the stream (DSA_BESIDE_PREVIOUS; see the header for
+    the caller's guarantee)."""
+    ia = _cmp_args(*icmp, 0, ratio, overlap, rotate, rope_dim)
+    ca = _cmp_args(*cmp, win, ratio, overlap, rotate, rope_dim)
+    for t, n in ((cos, "cos"), (sin, "sin")):
+        _need(t, n, F32)
+        _contig(t, n)
+    _need(pos, "pos", I32)
+    _need(t_active, "t_active", I32)
+    _need(iq, "iq", BF16)
+    _need(iw, "iw", F32)
+    _need(score, "score", F32)
+    _need(kv, "kv", BF16)
+    _need(idx, "idx", I32)
+    _contig(iq, "iq")
+    _contig(iw, "iw")
+    _contig(kv, "kv")
+    B, D = kv.shape
+    if iq.shape[1:] != (64, 128) or score.stride(1) != 1 or idx.stride(1) != 1:
+        raise ValueError("layer_prologue: iq [B,64,128], score and idx rows contiguous")
+    check(lib().dsa_layer_prologue(ctypes.byref(ia), ctypes.byref(ca), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+                                   eps, pos.data_ptr(), t_active.data_ptr(), iq.data_ptr(), iw.data_ptr(),
+                                   score.data_ptr(), score.stride(0), T, kv.data_ptr(), _ptr(kv_scales), D, rope_dim,
+                                   win, idx.data_ptr(), idx.stride(0), B,
+                                   _lib.DSA_BESIDE_PREVIOUS if beside_previous else 0, _stream(kv)),
+          "layer_prologue")
 
 
 # ---------------------------------------------------------------- attn.topk
