@@ -271,6 +271,22 @@ int dsa_indexer_score_ex(const void* q, const void* k, const float* w, float* sc
                          const int32_t* t_valid, int B, int H, int Di, int T,
                          int64_t k_bstride, int64_t ld_score, int flags, dsa_stream_t stream);
 
+/* dsa_indexer_score_ex with the per-sequence keys' work split dynamically:
+ * each of the persistent kernel's CTAs scores four fifths of an even share
+ * of the (sequence, 128-key tile) items and then claims further ones from
+ * counters
+ * (uint32 [2], 8-byte aligned device memory, zero before the first call;
+ * every call leaves them zero), so CTAs that start late - on SMs the
+ * previous kernel still held - take fewer and all finish together.  The
+ * same scores, bit for bit.  Calls that can overlap on the GPU (other
+ * streams) need their own counters; after a wait timed out, re-zero them.
+ * Needs k_bstride != 0 and B <= 4096.  Replaces the same reference stage
+ * (inference.py:5260-5275). */
+int dsa_indexer_score_dyn(const void* q, const void* k, const float* w, float* score,
+                          const int32_t* t_valid, int B, int H, int Di, int T,
+                          int64_t k_bstride, int64_t ld_score, int flags, uint32_t* counters,
+                          dsa_stream_t stream);
+
 /* The score of each sequence's newest live compressed row: for each b with
  * t = min(t_active[b], T) - 1 >= 0, score[b * ld_score + t] = sum_h w[b, h]
  * relu(q[b, h, :] . k[b * k_bstride + t * 128 + :]) (the score stage of

@@ -479,3 +479,27 @@ def test_sparse_attn_pair_combine_deterministic(cuda_dev):
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
     want = O.sparse_attn(q, kv, idx, sink, 512 ** -0.5)
     assert rel_err(a, want) < ATTN_REL
+
+
+@pytest.mark.parametrize("B,T,keys_ready", [(64, 9216, True), (64, 9216, False), (7, 3000, True), (130, 640, False)])
+def test_indexer_score_dynamic_split_equals_static(cuda_dev, B, T, keys_ready):
+    # claiming items from a counter changes which CTA scores which tile, not
+    # a score: equal bits to the static split, over repeated calls (the
+    # counters come back to zero) and ragged t_valid
+    from dsv4attn import ops
+    g = torch.Generator().manual_seed(B + T)
+    q = torch.randn(B, 64, 128, generator=g).to(torch.bfloat16).to(cuda_dev)
+    k = torch.randn(B, T, 128, generator=g).to(torch.bfloat16).to(cuda_dev)
+    w = (0.02 * torch.randn(B, 64, generator=g)).to(cuda_dev)
+    tv = torch.randint(0, T + 1, (B,), generator=g, dtype=torch.int32)
+    tv[0] = T
+    tvd = tv.to(cuda_dev)
+    ctr = torch.zeros(2, dtype=torch.int32, device=cuda_dev)
+    want = torch.full((B, T), 5.0, device=cuda_dev)
+    ops.indexer_score(q, k, w, T, out=want, t_valid=tvd)
+    for rep in range(3):
+        got = torch.full((B, T), 5.0, device=cuda_dev)
+        ops.indexer_score(q, k, w, T, out=got, t_valid=tvd, keys_ready=keys_ready, counters=ctr)
+        torch.cuda.synchronize()
+        assert torch.equal(got.cpu(), want.cpu()), f"call {rep}"
+        assert ctr.cpu().tolist() == [0, 0]

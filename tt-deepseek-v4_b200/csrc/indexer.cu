@@ -43,7 +43,7 @@ using namespace dsa;
 
 static int indexer_score_run(const void* q, const void* k, const float* w, float* score, const int32_t* t_valid,
                              int B, int H, int Di, int T, int64_t k_bstride, int64_t ld_score, int flags,
-                             dsa_stream_t stream) {
+                             dsa_stream_t stream, uint32_t* dyn = nullptr) {
   DSA_CHECK_ARG(q && k && w && score, "indexer_score: null pointer");
   DSA_CHECK_ARG(H == kIdxH && Di == kIdxD, "indexer_score: built for H=64, Di=128 (got H=%d Di=%d)", H, Di);
   DSA_CHECK_ARG(B >= 0 && T >= 0, "indexer_score: bad B/T");
@@ -56,11 +56,16 @@ static int indexer_score_run(const void* q, const void* k, const float* w, float
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    cudaFuncSetAttribute(idxtc::indexer_score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(idxtc::indexer_score_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         idxtc::kSmemBytes);
+    cudaFuncSetAttribute(idxtc::indexer_score_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          idxtc::kSmemBytes);
     attr_dev = dev;
   }
   const int nsm = num_sms();
+  DSA_CHECK_ARG(!dyn || (k_bstride != 0 && B <= idxtc::kMaxSeqBalanced && aligned(dyn, 8)),
+                "indexer_score: the dynamic split needs per-sequence keys, B <= %d and 8-byte aligned counters",
+                idxtc::kMaxSeqBalanced);
   if (k_bstride == 0 && B % idxpf::QG == 0) {
     // one key cache shared by all rows (a prefill chunk): 4 rows per MMA batch
     static int pf_attr_dev = -1;
@@ -118,8 +123,13 @@ static int indexer_score_run(const void* q, const void* k, const float* w, float
     a.balanced = B <= idxtc::kMaxSeqBalanced ? 1 : 0;
     a.keys_ready = (flags & DSA_KEYS_READY) ? 1 : 0;
     const int grid = a.balanced ? std::min(nsm, total) : (total + a.items_per_cta - 1) / a.items_per_cta;
-    launch_pdl(idxtc::indexer_score_tc_kernel, dim3(grid), dim3(idxtc::THREADS), idxtc::kSmemBytes,
-               reinterpret_cast<cudaStream_t>(stream), a, tm_k, tm_q);
+    a.dyn = dyn;
+    if (dyn)
+      launch_pdl(idxtc::indexer_score_tc_kernel<true>, dim3(grid), dim3(idxtc::THREADS), idxtc::kSmemBytes,
+                 reinterpret_cast<cudaStream_t>(stream), a, tm_k, tm_q);
+    else
+      launch_pdl(idxtc::indexer_score_tc_kernel<false>, dim3(grid), dim3(idxtc::THREADS), idxtc::kSmemBytes,
+                 reinterpret_cast<cudaStream_t>(stream), a, tm_k, tm_q);
   }
   DSA_CHECK_LAUNCH("indexer_score");
   return DSA_OK;
@@ -155,4 +165,13 @@ extern "C" int dsa_indexer_score_newest(const void* q, const void* k, int64_t k_
              score, ld_score, T);
   DSA_CHECK_LAUNCH("indexer_score_newest");
   return DSA_OK;
+}
+
+extern "C" int dsa_indexer_score_dyn(const void* q, const void* k, const float* w, float* score,
+                                     const int32_t* t_valid, int B, int H, int Di, int T, int64_t k_bstride,
+                                     int64_t ld_score, int flags, uint32_t* counters, dsa_stream_t stream) {
+  clear_error();
+  DSA_CHECK_ARG((flags & ~DSA_KEYS_READY) == 0, "indexer_score: unknown flags 0x%x", flags);
+  DSA_CHECK_ARG(counters != nullptr, "indexer_score: null counters");
+  return indexer_score_run(q, k, w, score, t_valid, B, H, Di, T, k_bstride, ld_score, flags, stream, counters);
 }

@@ -15,6 +15,18 @@
 //               K = 128 (8 x K16), into one of two TMEM accumulators.
 //   warps 2-5   epilogue: thread = key row (TMEM lane), 64 head scores in
 //               registers -> sum_h w_h relu(s_h) -> one fp32 score, coalesced.
+// Dynamic split (kDyn, a caller's counters): each CTA keeps a contiguous
+// four fifths of an even share (its first items still requested before the
+// dependency wait when keys_ready) and then claims items one at a time from
+// a global counter, one claim in flight ahead, so CTAs that start late -- on
+// SMs the previous kernel still held -- take fewer and the CTAs finish
+// together (79.1 against 80.5 us per decode layer at config 2, A/B; claiming
+// all but the first NS items lost 2.6 us: claim latency on the item path and
+// the epilogue reloading a sequence's head weights at almost every item).  The producer publishes every item it takes
+// (sequence and first key, or an end marker) in an 8-entry ring guarded by
+// mbarriers, which the MMA and epilogue warps follow; at most 6 items are in
+// flight between the producer and the epilogue, so 8 entries never wrap onto
+// an unread one.  The last CTA to finish claiming resets the counters.
 // The [H, T] score matrix never exists; HBM traffic is the key stream
 // (256 B per key) plus 4 B of score per key.
 #pragma once
@@ -36,7 +48,9 @@ constexpr int kQBytes = H * DI * 2;        // 16 KB: 2 k-blocks of [64 rows x 12
 constexpr int kStageBytes = kKeyBytes + kQBytes;
 constexpr int kOffAux = NS * kStageBytes;
 constexpr int kMaxSeqBalanced = 4096;      // sequences the live-tile prefix holds
-constexpr int kOffPre = kOffAux + 256;
+constexpr int kAuxBytes = 512;
+constexpr int kOffPre = kOffAux + kAuxBytes;
+constexpr int kInfo = 8;                   // dynamic split: published items ring
 constexpr int kSmemBytes = kOffPre + (kMaxSeqBalanced + 1) * 4 + 1024;
 constexpr uint32_t kTmemCols = 128;        // 2 accumulators x 64 columns
 constexpr uint32_t kIdesc = tc::idesc_bf16(128, 64, false, false);
@@ -46,10 +60,12 @@ struct Aux {
   uint64_t empty[NS];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
+  uint64_t info_full[kInfo];
+  int info_b[kInfo], info_t0[kInfo];  // sequence (-1: no more items) and first key
   uint32_t tmem_base;
   int wsum[THREADS / 32];
 };
-static_assert(sizeof(Aux) <= 256, "aux block");
+static_assert(sizeof(Aux) <= kAuxBytes, "aux block");
 
 struct Args {
   const float* w;
@@ -67,6 +83,7 @@ struct Args {
   int keys_ready;
   int64_t ld_score;
   int64_t k_row_stride;   // rows between consecutive sequences in the key map
+  uint32_t* dyn;          // dynamic split: [claimed items, CTAs done], zero on entry and on exit
 };
 
 __device__ __forceinline__ int seq_limit(const Args& a, int b) {
@@ -110,6 +127,7 @@ struct ItemWalk {
   }
 };
 
+template <bool kDyn>
 __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args a,
                                                                       const __grid_constant__ CUtensorMap tm_k,
                                                                       const __grid_constant__ CUtensorMap tm_q) {
@@ -132,6 +150,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
       tc::mbar_init(smem_u32(&aux->acc_full[s]), 1);
       tc::mbar_init(smem_u32(&aux->acc_empty[s]), 4);
     }
+    for (int s = 0; s < kInfo; ++s) tc::mbar_init(smem_u32(&aux->info_full[s]), 1);
     tc::mbar_fence_init();
   }
   tc::fence_before_sync();
@@ -141,6 +160,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
 
   ItemWalk walk{};
   walk.a = &a;
+  int total_live = 0;
   auto build_walk = [&]() {
     if (a.balanced) {
       // live tiles per sequence -> exclusive prefix (one block scan)
@@ -166,8 +186,12 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
       }
       if (tid == THREADS - 1) pre[a.B] = run;
       __syncthreads();
-      const int total_live = pre[a.B];
-      const int share = (total_live + gridDim.x - 1) / gridDim.x;
+      total_live = pre[a.B];
+      // dynamic split: about four fifths of an even share are each CTA's
+      // own (contiguous, so the epilogue's head weights change rarely); the
+      // rest is claimed
+      const int even = (total_live + gridDim.x - 1) / gridDim.x;
+      const int share = kDyn ? max(NS, even * 4 / 5) : even;
       walk.pre = pre;
       walk.l = min(total_live, int(blockIdx.x) * share);
       walk.l_end = min(total_live, walk.l + share);
@@ -191,7 +215,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
   // keys_ready: the work split (from t_valid) and the first NS key tiles
   // before the wait; each stage's q follows after it on the same barrier
   int npre = 0;
-  int qb[NS];
+  int qb[NS], qt0[NS];
   if (a.keys_ready) {
     build_walk();
     if (warp == 0 && lane == 0) {
@@ -204,6 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
         const int krow = int(int64_t(b) * a.k_row_stride + t0);
         tma::load_2d(st, &tm_k, 0, krow, fb);
         tma::load_2d(st + kKeyBytes / 2, &tm_k, 64, krow, fb);
+        qt0[npre] = t0;
         qb[npre++] = b;
       }
     }
@@ -227,18 +252,64 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
       }
       int it = npre;
       int b, t0, t_lim;
-      while (walk.next(b, t0, t_lim)) {
+      auto issue = [&](int b_, int t0_) {
         const int s = it % NS;
         if (it >= NS) tc::mbar_wait(smem_u32(&aux->empty[s]), ((it / NS) - 1) & 1, a.status, 2, a.wait_limit);
         const uint32_t st = sbase + s * kStageBytes;
         const uint32_t fb = smem_u32(&aux->full[s]);
         tma::mbar_arrive_expect_tx(fb, kStageBytes);
-        const int krow = int(int64_t(b) * a.k_row_stride + t0);
+        const int krow = int(int64_t(b_) * a.k_row_stride + t0_);
         tma::load_2d(st, &tm_k, 0, krow, fb);
         tma::load_2d(st + kKeyBytes / 2, &tm_k, 64, krow, fb);
-        tma::load_2d(st + kKeyBytes, &tm_q, 0, b * H, fb);
-        tma::load_2d(st + kKeyBytes + kQBytes / 2, &tm_q, 64, b * H, fb);
-        ++it;
+        tma::load_2d(st + kKeyBytes, &tm_q, 0, b_ * H, fb);
+        tma::load_2d(st + kKeyBytes + kQBytes / 2, &tm_q, 64, b_ * H, fb);
+      };
+      if constexpr (kDyn) {
+        // every item taken is published for the MMA and epilogue warps
+        auto publish = [&](int i, int b_, int t0_) {
+          aux->info_b[i % kInfo] = b_;
+          aux->info_t0[i % kInfo] = t0_;
+          tc::mbar_arrive(smem_u32(&aux->info_full[i % kInfo]));
+        };
+        for (int i = 0; i < npre; ++i) publish(i, qb[i], qt0[i]);
+        while (walk.next(b, t0, t_lim)) {
+          issue(b, t0);
+          publish(it, b, t0);
+          ++it;
+        }
+        const int* pre = reinterpret_cast<const int*>(smem + kOffPre);
+        const int even = (total_live + gridDim.x - 1) / gridDim.x;
+        const int first = int(gridDim.x) * max(NS, even * 4 / 5);
+        // one claim in flight ahead of the item being issued
+        int next = int(atomicAdd(a.dyn, 1u));
+        for (;;) {
+          const int l = first + next;
+          if (l >= total_live) break;
+          next = int(atomicAdd(a.dyn, 1u));
+          // the sequence holding live item l: the last b with pre[b] <= l
+          int lo = 0, hi = a.B - 1;
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pre[mid] <= l) lo = mid;
+            else hi = mid - 1;
+          }
+          t0 = (l - pre[lo]) * TILE;
+          issue(lo, t0);
+          publish(it, lo, t0);
+          ++it;
+        }
+        publish(it, -1, 0);
+        // every CTA has made its last claim once all have counted themselves
+        // here: the last one resets the counters for the next call
+        if (atomicAdd(a.dyn + 1, 1u) == gridDim.x - 1) {
+          atomicExch(a.dyn, 0u);
+          atomicExch(a.dyn + 1, 0u);
+        }
+      } else {
+        while (walk.next(b, t0, t_lim)) {
+          issue(b, t0);
+          ++it;
+        }
       }
     }
     __syncwarp();
@@ -247,7 +318,16 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
     if (lane == 0) {
       int it = 0;
       int b, t0, t_lim;
-      while (walk.next(b, t0, t_lim)) {
+      auto next_item = [&]() -> bool {
+        if constexpr (kDyn) {
+          if (!tc::mbar_wait(smem_u32(&aux->info_full[it % kInfo]), (it / kInfo) & 1, a.status, 2, a.wait_limit))
+            return false;
+          return aux->info_b[it % kInfo] >= 0;
+        } else {
+          return walk.next(b, t0, t_lim);
+        }
+      };
+      while (next_item()) {
         const int s = it % NS, acc = it & 1;
         tc::mbar_wait(smem_u32(&aux->full[s]), (it / NS) & 1, a.status, 2, a.wait_limit);
         if (it >= 2) tc::mbar_wait(smem_u32(&aux->acc_empty[acc]), ((it - 2) >> 1) & 1, a.status, 2, a.wait_limit);
@@ -275,7 +355,20 @@ __global__ void __launch_bounds__(THREADS, 1) indexer_score_tc_kernel(const Args
     int cur_b = -1;
     float wv[H];
     int b, t0, t_lim;
-    while (walk.next(b, t0, t_lim)) {
+    auto next_item = [&]() -> bool {
+      if constexpr (kDyn) {
+        if (!tc::mbar_wait(smem_u32(&aux->info_full[it % kInfo]), (it / kInfo) & 1, a.status, 2, a.wait_limit))
+          return false;
+        b = aux->info_b[it % kInfo];
+        t0 = aux->info_t0[it % kInfo];
+        if (b < 0) return false;
+        t_lim = seq_limit(a, b);
+        return true;
+      } else {
+        return walk.next(b, t0, t_lim);
+      }
+    };
+    while (next_item()) {
       const int acc = it & 1;
       if (b != cur_b) {
 #pragma unroll

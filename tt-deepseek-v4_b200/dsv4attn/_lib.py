@@ -58,6 +58,7 @@ PROTOTYPES = {
     "dsa_window_indices": (I32, [P, P, I64, I32, I32, P]),
     "dsa_indexer_score": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, P]),
     "dsa_indexer_score_ex": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, I32, P]),
+    "dsa_indexer_score_dyn": (I32, [P, P, P, P, P, I32, I32, I32, I32, I64, I64, I32, P, P]),
     "dsa_layer_prologue": (I32, [ctypes.POINTER(CompressorArgs), ctypes.POINTER(CompressorArgs), P, P, I32, F32, P,
                                   P, P, P, P, I64, I32, P, P, I32, I32, I32, P, I64, I32, ctypes.c_uint, P]),
     "dsa_indexer_score_newest": (I32, [P, P, I64, P, P, P, I64, I32, I32, P]),

@@ -193,6 +193,9 @@ class DecodePath:
         # scores that one row after its compressor)
         self.t_prev = torch.zeros(self.B, dtype=I32, device=self.device)
         self.status = torch.zeros(1, dtype=I32, device=self.device)
+        # the indexer score's dynamic work split (claimed items, CTAs done):
+        # zero, and left zero by every call; the layers run one at a time
+        self.score_counters = torch.zeros(2, dtype=I32, device=self.device)
         self.graph = None
 
     def set_positions(self, pos) -> None:
@@ -214,8 +217,10 @@ class DecodePath:
         # the second layer on its first key tiles are requested before the
         # previous layer's last kernel ends (the first layer may directly
         # follow the kernel that writes t_prev).
+        # The work split is dynamic: CTAs placed late, on SMs the previous
+        # layer's attention still held, take fewer items.
         ops.indexer_score(x.iq, L.idx_cache, x.iw, L.T_max, out=L.score, t_valid=self.t_prev,
-                          keys_ready=L is not self.layers[0])
+                          keys_ready=L is not self.layers[0], counters=self.score_counters)
         # The prologue: the indexer compressor (it may write row t_active - 1
         # of the indexer cache) and that row's score, the window-ring KV
         # write (attn.kv), the window indices and attn.compress.  None of it

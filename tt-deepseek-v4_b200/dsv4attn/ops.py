@@ -429,14 +429,16 @@ def window_indices(pos: torch.Tensor, win: int, out: torch.Tensor | None = None)
 
 def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: int,
                   out: torch.Tensor | None = None, t_valid: torch.Tensor | None = None,
-                  keys_ready: bool = False) -> torch.Tensor:
+                  keys_ready: bool = False, counters: torch.Tensor | None = None) -> torch.Tensor:
     """``s[b,t] = sum_h w[b,h] relu(q[b,h].k[b,t])`` for t < T
     (inference.py:5260-5275).  q [B,64,128] bf16, k_cache [B, >=T, 128] bf16
     (or [>=T, 128]: one cache shared by all B rows, the queries of a prefill
     chunk), w [B,64] fp32 -> [B, T] fp32.  ``keys_ready``: k_cache and
     t_valid were complete before the previous kernel on the stream started
     (DSA_KEYS_READY: the kernel requests its first key tiles before waiting
-    for that kernel)."""
+    for that kernel).  ``counters`` (int32 [2], zero; left zero): split the
+    work dynamically (dsa_indexer_score_dyn; one pair per stream that can
+    run it concurrently)."""
     _need(q, "q", BF16)
     _need(k_cache, "k_cache", BF16)
     _need(w, "w", F32)
@@ -453,6 +455,15 @@ def indexer_score(q: torch.Tensor, k_cache: torch.Tensor, w: torch.Tensor, T: in
         k_bstride = k_cache.stride(0)
     if out is None:
         out = torch.empty(B, T, dtype=F32, device=q.device)
+    if counters is not None:
+        _need(counters, "counters", I32)
+        if counters.numel() < 2:
+            raise ValueError("counters must hold 2 int32")
+        check(lib().dsa_indexer_score_dyn(q.data_ptr(), k_cache.data_ptr(), w.data_ptr(), out.data_ptr(),
+                                          _ptr(t_valid), B, H, Di, T, k_bstride, out.stride(0),
+                                          DSA_KEYS_READY if keys_ready else 0, counters.data_ptr(), _stream(q)),
+              "indexer_score")
+        return out
     check(lib().dsa_indexer_score_ex(q.data_ptr(), k_cache.data_ptr(), w.data_ptr(), out.data_ptr(),
                                      _ptr(t_valid), B, H, Di, T, k_bstride, out.stride(0),
                                      DSA_KEYS_READY if keys_ready else 0, _stream(q)), "indexer_score")
