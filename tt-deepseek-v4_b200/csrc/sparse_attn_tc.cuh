@@ -174,7 +174,8 @@ struct Aux {
   float alpha[H];                 // rescale factor of the last max update
   float f[H];                     // epilogue scale per head
   float m_fin[H], l_fin[H];       // pair combine: this split's (m, l) per head, m in log2 units
-  float peer_ml[H];               // pair combine: the peer split's (m, l) of the heads this CTA finishes
+  float peer_ml[H];               // pair combine: the peer split's (m, l) of the heads this CTA finishes,
+                                  // written by the peer through distributed shared memory
   float coef[2][H / 2];           // pair combine: weight / L of split 0 and split 1 per finished head
   uint32_t vmask[kIdxCap / 32];   // validity bits of the staged indices
   uint64_t q_tma;
@@ -221,6 +222,14 @@ __device__ __forceinline__ void q_part_to_tmem(uint32_t sq, uint32_t tmem, int w
   tc::tmem_wait_st();
   tc::fence_before_sync();
   tc::mbar_arrive(smem_u32(q_full));
+}
+
+// a 32-bit store into CTA `rank`'s shared memory at the address of `p` in
+// this CTA's (distributed shared memory)
+__device__ __forceinline__ void st_peer_f32(const void* p, uint32_t rank, float v) {
+  uint32_t addr;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(smem_u32(p)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 // the pair combine's cluster barrier: release / acquire at cluster scope
@@ -328,6 +337,21 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     const uint32_t bits = __ballot_sync(0xffffffffu, id >= 0);
     if (lane == 0) aux->vmask[e >> 5] = bits;
   };
+  const uint32_t tmem = aux->tmem_base;
+  auto wait = [&](const uint64_t* bar, uint32_t parity) {
+    if (*abort_flag) return;
+    if (!tc::mbar_wait(smem_u32(bar), parity, a.status, kStatusTimeout, a.wait_limit)) *abort_flag = 1;
+  };
+  // whole-warp wait with one polling lane
+  auto warp_wait = [&](const uint64_t* bar, uint32_t parity) {
+    if (lane == 0) wait(bar, parity);
+    __syncwarp();
+  };
+  // every warp moves its part of Q' once the TMA copy has landed
+  auto q_part = [&]() {
+    warp_wait(&aux->q_tma, 0);
+    q_part_to_tmem(sQstage, tmem, warp, lane, &aux->q_full);
+  };
   if (early_lead) {
     // before the dependency wait: q and the lead tile
     load_q();
@@ -337,6 +361,10 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   } else if (a.early) {
     load_q();
   }
+  // q is ready before the dependency wait: Q' goes into tensor memory now,
+  // so the first score MMA and the third tile's copies (into the slot that
+  // staged q) need not wait for it once the index list is in
+  if (a.early) q_part();
   pdl_wait();
   pdl_launch_dependents();
   if (!a.early) load_q();
@@ -361,24 +389,8 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t tmem = aux->tmem_base;
   if (tid == 0) SA_TRACE(kTrMisc, 5);
-
-  auto wait = [&](const uint64_t* bar, uint32_t parity) {
-    if (*abort_flag) return;
-    if (!tc::mbar_wait(smem_u32(bar), parity, a.status, kStatusTimeout, a.wait_limit)) *abort_flag = 1;
-  };
-  // whole-warp wait with one polling lane
-  auto warp_wait = [&](const uint64_t* bar, uint32_t parity) {
-    if (lane == 0) wait(bar, parity);
-    __syncwarp();
-  };
-
-  // every warp moves its part of Q' once the TMA copy has landed
-  auto q_part = [&]() {
-    warp_wait(&aux->q_tma, 0);
-    q_part_to_tmem(sQstage, tmem, warp, lane, &aux->q_full);
-  };
+  const bool q_late = !a.early;  // Q' still to be moved (q was loaded after the wait)
 
   if (is_producer_warp(warp)) {
     // ------------------------------------------------------------ producers
@@ -387,18 +399,18 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     const int pw = producer_index(warp);
     for (int t = early_lead ? 1 : 0; t < n; ++t) {
       if (t == NT - 1) {
-        q_part();
+        if (q_late) q_part();
         warp_wait(&aux->q_full, 0);
       }
       if (t >= NT) warp_wait(&aux->empty[t % NT], ((t / NT) - 1) & 1);
       issue_tile(t, pw);
     }
-    if (n < NT) q_part();
+    if (n < NT && q_late) q_part();
     cp_async_wait<0>();
   } else if (warp == kMmaWarp || warp == 12) {
     // ------------------------------------------------------------ PV issuers
     // warp 4: output dims 0-255 (O^T blocks 0, 1), warp 12: dims 256-511
-    q_part();
+    if (q_late) q_part();
     const int jb0 = warp == kMmaWarp ? 0 : 2;
     if (lane == 0 && n > 0) {
       const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
@@ -434,7 +446,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     __syncwarp();
   } else if (warp < 4) {
     // ------------------------------------------------------------ softmax warps 0-3
-    q_part();
+    if (q_late) q_part();
     if (tid == 0) SA_TRACE(kTrMisc, 6);
     // Heads 16w..16w+15: first-half partials in TMEM lanes 32w..32w+15,
     // second-half partials in lanes 32w+16..32w+31.  Keys 16q..16q+15 are S
@@ -594,7 +606,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------ S issuer
-    q_part();
+    if (q_late) q_part();
     if (lane == 0 && n > 0) {
       const uint32_t hi = tc::desc_hi(1024, tc::kLayoutSw128);
       const uint32_t k_lo = tc::desc_lo(sRing, 16);  // K-major: LBO unused
@@ -635,21 +647,26 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
     // ------------------------------------------------------ pair combine
     // The row's splits 0 and 1 are this cluster's two CTAs (cluster rank =
     // split).  CTA r finishes heads 32r..32r+31: it writes the other half
-    // of its O^T (thread = output dim d, 32 fp32) and the (m, l) of those
-    // heads to the peer's slot of pair_x (L2-resident; coalesced 16-B
-    // stores), the cluster barrier orders those writes before the peer's
-    // reads, and each CTA combines its own half with the peer's:
+    // of its O^T (thread = output dim d, 32 heads rounded to bf16, four
+    // 16-B stores) to the peer's slot of pair_x (L2-resident) and the
+    // (m, l) of those heads into the peer's shared memory, the cluster
+    // barrier orders those writes before the peer's reads, and each CTA
+    // combines its own half (fp32, from tensor memory) with the peer's:
     // out = (w0 o0 + w1 o1) / L, w_s = 2^(m_s - M),
     // L = l0 w0 + l1 w1 + 2^(sink - M), M = max(m0, m1, sink) - split 0's
     // partial first on both CTAs, so the result does not depend on which
-    // CTA finishes which half.  (Distributed shared memory moves ~28 GB/s
-    // per SM here; the L2 round trip is faster.)
+    // CTA runs first.  The tail is bound by the SM's traffic to L2 (the
+    // exchange out, the peer's half in, the output rows): bf16 halves the
+    // exchange (the split-K drain of other row shapes stores its partials
+    // in bf16 as well).  Distributed shared memory moved only ~28 GB/s per
+    // SM here, so it carries just the 64 (m, l) values.
     const int r = split, pr = split ^ 1;
     const int sp = warp & 3, jb = warp >> 2;
     const uint32_t tl = tmem + ((uint32_t)(32 * sp) << 16);
     const int d = 128 * jb + 32 * sp + lane;
-    float* x_out = a.pair_x + (int64_t(mrow) * 2 + pr) * kPairXFloats;
-    const float* x_in = a.pair_x + (int64_t(mrow) * 2 + r) * kPairXFloats;
+    // [4 groups of 8 heads][D dims] x 16 B of bf16
+    uint4* x_out = reinterpret_cast<uint4*>(a.pair_x + (int64_t(mrow) * 2 + pr) * kPairXFloats);
+    const uint4* x_in = reinterpret_cast<const uint4*>(a.pair_x + (int64_t(mrow) * 2 + r) * kPairXFloats);
     {
       float o[32];
       if (n > 0) {
@@ -660,18 +677,22 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         for (int i = 0; i < 32; ++i) o[i] = 0.f;
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        reinterpret_cast<float4*>(x_out)[c * D + d] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      for (int c = 0; c < 4; ++c)
+        x_out[c * D + d] = make_uint4(pack_bf16x2(o[8 * c], o[8 * c + 1]), pack_bf16x2(o[8 * c + 2], o[8 * c + 3]),
+                                      pack_bf16x2(o[8 * c + 4], o[8 * c + 5]), pack_bf16x2(o[8 * c + 6], o[8 * c + 7]));
       if (tid < 32) {
         const int h = 32 * pr + tid;
-        reinterpret_cast<float2*>(x_out + 8 * D * 4)[tid] = make_float2(aux->m_fin[h], aux->l_fin[h]);
+        st_peer_f32(&aux->peer_ml[2 * tid], uint32_t(pr), aux->m_fin[h]);
+        st_peer_f32(&aux->peer_ml[2 * tid + 1], uint32_t(pr), aux->l_fin[h]);
       }
     }
-    cluster_sync();
+    cluster_sync();  // the last access of either CTA's shared memory by the other
+    uint4 xp[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) xp[c] = __ldcg(x_in + c * D + d);
     if (tid < 32) {
       const int h = 32 * r + tid;
-      const float2 pml = __ldcg(reinterpret_cast<const float2*>(x_in + 8 * D * 4) + tid);
-      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = pml.x, lp = pml.y;
+      const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = aux->peer_ml[2 * tid], lp = aux->peer_ml[2 * tid + 1];
       const float m0 = r == 0 ? mo : mp, l0 = r == 0 ? lo : lp, m1 = r == 0 ? mp : mo, l1 = r == 0 ? lp : lo;
       const float sk = a.sink[h] * kLog2e;
       const float Mx = fmaxf(fmaxf(m0, m1), sk);
@@ -691,12 +712,13 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       for (int i = 0; i < 32; ++i) own[i] = 0.f;
     }
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(x_in) + c * D + d);
-      peer[4 * c] = v.x;
-      peer[4 * c + 1] = v.y;
-      peer[4 * c + 2] = v.z;
-      peer[4 * c + 3] = v.w;
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t w[4] = {xp[c].x, xp[c].y, xp[c].z, xp[c].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        peer[8 * c + 2 * e] = __uint_as_float(w[e] << 16);
+        peer[8 * c + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      }
     }
     __syncthreads();  // coefficients
     // out[h][d]: lanes d, d ^ 1 trade one value per head pair so that each
