@@ -863,14 +863,20 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
   bool fast = n_live >= uint32_t(k) && mx != mn && isfinite(vmin) && isfinite(vmax) && isfinite(scale) &&
               scale > 0.f;
   uint32_t thr = 0;
+  // After the loads, the per-key loops are not unrolled and read the keys
+  // back from shared memory: in the decode step this kernel starts on SMs
+  // whose instruction cache holds the indexer's code, and unrolled copies
+  // cost more in instruction fetch than they save in issue (same box, A/B:
+  // 75.8 against 77.5 us per layer, although the kernel timed back to back
+  // with itself, warm, runs 10.7 against 9.5 us).
   if (fast) {
-#pragma unroll
-    for (int j = 0; j < kKeysPerThread; ++j) {
-      if (j >= per) break;
+#pragma unroll 1
+    for (int j = 0; j < per; ++j) {
       const int i = base + 32 * j;
       uint32_t bin = kRowNoBin;
-      if (i < cnt_pos && r[j] > kfloor) {
-        const float d = key_float(r[j]) - vmin;
+      const uint32_t x = i < cnt_pos ? keys[i] : 0u;
+      if (i < cnt_pos && x > kfloor) {
+        const float d = key_float(x) - vmin;
         bin = min(__float_as_uint(fmaf(d, scale, kRoundMagic)) - __float_as_uint(kRoundMagic), 254u);
       }
       if (i < cnt_pos) bins[i] = uint8_t(bin);
@@ -890,9 +896,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
     pick_bin(k, &s);
     const uint32_t bin = s.prefix;
     const uint32_t kl = uint32_t(k) - s.kgt;
-#pragma unroll
-    for (int j = 0; j < kKeysPerThread; ++j) {
-      if (j >= per) break;
+#pragma unroll 1
+    for (int j = 0; j < per; ++j) {
       const int i = base + 32 * j;
       const bool hit = i < cnt_pos && bins[i] == bin;
       const unsigned m = __ballot_sync(0xffffffffu, hit);
@@ -900,7 +905,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
         uint32_t o = 0;
         if (lane == 0) o = atomicAdd(&s.ncand, uint32_t(__popc(m)));
         o = __shfl_sync(0xffffffffu, o, 0);
-        if (hit) cand[o + __popc(m & ((1u << lane) - 1u))] = r[j];
+        if (hit) cand[o + __popc(m & ((1u << lane) - 1u))] = keys[i];
       }
     }
     __syncthreads();
@@ -950,21 +955,19 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
     __syncthreads();
     kth_key_select(r, keys, n, k, &s, cand);
     thr = s.prefix;
-#pragma unroll
-    for (int j = 0; j < kKeysPerThread; ++j) {
-      const int i = base + 32 * j;
-      r[j] = (j < per && i < cnt_pos) ? keys[p0 + i] : 0u;
-    }
   }
   // compaction: this CTA's keys above thr, then the lowest-position keys
   // equal to it; the lower half's counts come first
   uint32_t ca = 0, ce = 0;
-#pragma unroll
-  for (int j = 0; j < kKeysPerThread; ++j) {
-    if (j >= per) break;
+  // this CTA's keys by local position (the general select left the whole
+  // row in shared memory)
+  const uint32_t* lkeys = keys + (fast ? 0 : p0);
+#pragma unroll 1
+  for (int j = 0; j < per; ++j) {
     const bool valid = base + 32 * j < cnt_pos;
-    ca += __popc(__ballot_sync(0xffffffffu, valid && r[j] > thr));
-    ce += __popc(__ballot_sync(0xffffffffu, valid && r[j] == thr));
+    const uint32_t x = valid ? lkeys[base + 32 * j] : 0u;
+    ca += __popc(__ballot_sync(0xffffffffu, valid && x > thr));
+    ce += __popc(__ballot_sync(0xffffffffu, valid && x == thr));
   }
   if (lane == 0) {
     s.warp_cnt[0][warp] = ca;
@@ -1001,12 +1004,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
   const uint32_t lt = (1u << lane) - 1u;
   int32_t* orow = out_idx + int64_t(b) * ld_out;
   float* srow = out_score ? out_score + int64_t(b) * ld_out : nullptr;
-#pragma unroll
-  for (int j = 0; j < kKeysPerThread; ++j) {
-    if (j >= per) break;
+#pragma unroll 1
+  for (int j = 0; j < per; ++j) {
     const int i = base + 32 * j;
     const bool valid = i < cnt_pos;
-    const bool above = valid && r[j] > thr, eq = valid && r[j] == thr;
+    const uint32_t x = valid ? lkeys[i] : 0u;
+    const bool above = valid && x > thr, eq = valid && x == thr;
     const uint32_t ma = __ballot_sync(0xffffffffu, above), me = __ballot_sync(0xffffffffu, eq);
     int slot = -1;
     if (above) {
@@ -1018,7 +1021,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
     oa += __popc(ma);
     oe += __popc(me);
     if (slot >= 0) {
-      const float f = key_float(r[j]);
+      const float f = key_float(x);
       orow[slot] = f >= -1000.0f ? p0 + i + win : -1;
       if (srow) srow[slot] = f;
     }
