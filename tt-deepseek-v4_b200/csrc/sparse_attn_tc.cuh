@@ -572,9 +572,9 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       if (tid == 0) SA_TRACE(kTrPDone, t);
     }
     // ---------------------------------------------------------------- epilogue
-    if (n > 0) warp_wait(&aux->pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1);
-    tc::fence_after_sync();
-    if (tid == 0) SA_TRACE(kTrMisc, 2);
+    // (m, l) per head while the last PV still runs: the quad shuffles and
+    // the stores below took ~1K cycles here, measured, when they came
+    // after the wait for it
     // l per head: this thread's partial sums over its keys, then the 4 lanes
     // of the quad
     l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
@@ -604,6 +604,9 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         }
       }
     }
+    if (n > 0) warp_wait(&aux->pv_done[(n - 1) & 1], ((n - 1) >> 1) & 1);
+    tc::fence_after_sync();
+    if (tid == 0) SA_TRACE(kTrMisc, 2);
   } else if (warp == 8) {
     // ------------------------------------------------------------ S issuer
     if (q_late) q_part();
