@@ -689,6 +689,17 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
         st_peer_f32(&aux->peer_ml[2 * tid + 1], uint32_t(pr), aux->l_fin[h]);
       }
     }
+    // this CTA's own half and the sinks are read while the partner may
+    // still be on its last tiles
+    float own[32], peer[32];
+    if (n > 0) {
+      tc::tmem_ld32(tl + kColO + H * jb + 32 * r, own);
+      tc::tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) own[i] = 0.f;
+    }
+    const float sink_h = tid < 32 ? a.sink[32 * r + tid] : 0.f;
     cluster_sync();  // the last access of either CTA's shared memory by the other
     uint4 xp[4];
 #pragma unroll
@@ -697,7 +708,7 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       const int h = 32 * r + tid;
       const float mo = aux->m_fin[h], lo = aux->l_fin[h], mp = aux->peer_ml[2 * tid], lp = aux->peer_ml[2 * tid + 1];
       const float m0 = r == 0 ? mo : mp, l0 = r == 0 ? lo : lp, m1 = r == 0 ? mp : mo, l1 = r == 0 ? lp : lo;
-      const float sk = a.sink[h] * kLog2e;
+      const float sk = sink_h * kLog2e;
       const float Mx = fmaxf(fmaxf(m0, m1), sk);
       const float w0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - Mx);
       const float w1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - Mx);
@@ -705,14 +716,6 @@ __global__ void __launch_bounds__(THREADS, 1) sparse_attn_tc_kernel(const Args a
       aux->coef[0][tid] = w0 / L;
       aux->coef[1][tid] = w1 / L;
       if (a.lse) a.lse[int64_t(mrow) * H + h] = (Mx + log2f(L)) * kLn2;
-    }
-    float own[32], peer[32];
-    if (n > 0) {
-      tc::tmem_ld32(tl + kColO + H * jb + 32 * r, own);
-      tc::tmem_wait_ld();
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) own[i] = 0.f;
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
