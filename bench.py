@@ -482,7 +482,9 @@ def main():
     # per-kernel CUDA-event timings -> dominant kernel roofline
     log(f"timed: {ms_step:.3f} ms/step; per-kernel timings")
     kt = time_kernels(path, inputs, outs)
-    dom = max(kt, key=kt.get)
+    # the dominant kernel among those the workload's byte count covers (the
+    # layer prologue is latency-bound, with no roofline of its own)
+    dom = max((k for k in kt if k in ab), key=kt.get)
     achieved = ab[dom] / (kt[dom] * 1e-3) / 1e9
     # ncu DRAM bytes of this workload's dominant kernel (None where no capture
     # of that workload is committed)

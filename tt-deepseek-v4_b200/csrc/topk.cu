@@ -768,6 +768,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_row_kernel(
 // Rows the first level cannot settle take the general select over the whole
 // row in both CTAs.
 struct PairExchange {
+  uint64_t bar[4];             // arrivals of the peer's values: mm, hist, cand + ncand, tot
   uint32_t mm[3];              // the peer's (min, max, live count)
   uint32_t ncand;              // the peer's keys in the threshold bin
   uint32_t tot[2];             // the peer's keys above / equal to the threshold
@@ -775,19 +776,35 @@ struct PairExchange {
   uint32_t cand[kRankMax];     // the peer's keys in the threshold bin
 };
 
-__device__ __forceinline__ uint32_t cl_mapa(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cl_st(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
 __device__ __forceinline__ void cl_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cl_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-__device__ __forceinline__ void cl_sync() {
-  cl_arrive();
-  cl_wait();
+// One value into the peer CTA's copy of `field`, counted on the peer's copy
+// of mbarrier `bar` (st.async ... complete_tx): the receiver waits for
+// exactly the bytes it expects, and neither side stops at a cluster-wide
+// barrier, whose release fence stalled every exchange (ncu: membar 1.5
+// stall cycles per issued instruction with four cluster barriers).
+__device__ __forceinline__ void px_send(const void* field, uint32_t rank, uint32_t v, const uint64_t* bar) {
+  uint32_t dst, rbar;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_u32(field)), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(smem_u32(bar)), "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst), "r"(v),
+               "r"(rbar)
+               : "memory");
+}
+// bounded wait for the peer's values (phase 0: each barrier is used once);
+// past about a second it gives up rather than hang
+__device__ __forceinline__ void px_wait(const uint64_t* bar) {
+  const uint32_t a = smem_u32(bar);
+  const long long t0 = clock64();
+  uint32_t ok = 0;
+  do {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(a)
+        : "memory");
+  } while (!ok && clock64() - t0 < 2000000000LL);
 }
 
 __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
@@ -811,8 +828,20 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
     rank_gt[tid] = 0;
     rank_ge[tid] = 0;
   }
-  if (tid == 0) s.ncand = 0;
-  // both CTAs have started before either writes the other's shared memory
+  if (tid == 0) {
+    s.ncand = 0;
+    const uint32_t bytes[4] = {3 * 4, 256 * 4, 4 + kRankMax * 4, 2 * 4};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&px.bar[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&px.bar[i])), "r"(bytes[i])
+                   : "memory");
+  }
+  // both CTAs have started (and set up their barriers) before either
+  // writes the other's shared memory
   cl_arrive();
   pdl_wait();
   pdl_launch_dependents();
@@ -848,12 +877,11 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
   block_minmax_sum(lo, hi, cnt, &s, mn, mx, n_live);
   cl_wait();
   if (tid == 0) {
-    const uint32_t dst = cl_mapa(smem_u32(&px.mm[0]), peer);
-    cl_st(dst, mn);
-    cl_st(dst + 4, mx);
-    cl_st(dst + 8, n_live);
+    px_send(&px.mm[0], peer, mn, &px.bar[0]);
+    px_send(&px.mm[1], peer, mx, &px.bar[0]);
+    px_send(&px.mm[2], peer, n_live, &px.bar[0]);
   }
-  cl_sync();
+  px_wait(&px.bar[0]);
   mn = min(mn, px.mm[0]);
   mx = max(mx, px.mm[1]);
   n_live += px.mm[2];
@@ -889,8 +917,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
       }
     }
     __syncthreads();
-    if (tid < 256) cl_st(cl_mapa(smem_u32(&px.hist[tid]), peer), s.hist[tid]);
-    cl_sync();
+    if (tid < 256) px_send(&px.hist[tid], peer, s.hist[tid], &px.bar[1]);
+    px_wait(&px.bar[1]);
     if (tid < 256) s.hist[tid] += px.hist[tid];
     __syncthreads();
     pick_bin(k, &s);
@@ -910,9 +938,12 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
     }
     __syncthreads();
     const int nc_own = int(s.ncand);
-    if (tid == 0) cl_st(cl_mapa(smem_u32(&px.ncand), peer), uint32_t(nc_own));
-    if (nc_own <= kRankMax && tid < nc_own) cl_st(cl_mapa(smem_u32(&px.cand[tid]), peer), cand[tid]);
-    cl_sync();
+    if (tid == 0) px_send(&px.ncand, peer, uint32_t(nc_own), &px.bar[2]);
+    // a fixed kRankMax entries (the receiver's byte count); those past the
+    // count are not read
+    if (tid < kRankMax) px_send(&px.cand[tid], peer, cand[tid], &px.bar[2]);
+    px_wait(&px.bar[2]);
+    __syncthreads();  // every thread has sent its cand entry before any is overwritten below
     const int nc_peer = int(px.ncand);
     const int nc = nc_own + nc_peer;
     if (nc_own <= kRankMax && nc_peer <= kRankMax && nc <= kRankMax) {
@@ -988,14 +1019,14 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
     s.warp_cnt[0][lane] = xa - wa;
     s.warp_cnt[1][lane] = xe - we;
     if (lane == 31) {
-      const uint32_t dst = cl_mapa(smem_u32(&px.tot[0]), peer);
-      cl_st(dst, xa);
-      cl_st(dst + 4, xe);
+      px_send(&px.tot[0], peer, xa, &px.bar[3]);
+      px_send(&px.tot[1], peer, xe, &px.bar[3]);
       s.part[0][0] = xa;
       s.part[0][1] = xe;
     }
   }
-  cl_sync();  // also the last access of either CTA's shared memory by the other
+  __syncthreads();
+  px_wait(&px.bar[3]);
   const uint32_t a0 = c ? px.tot[0] : s.part[0][0], a1 = c ? s.part[0][0] : px.tot[0];
   const uint32_t e0 = c ? px.tot[1] : 0u;
   const int n_above = int(a0 + a1);  // < k by the choice of thr
@@ -1026,6 +1057,10 @@ __global__ void __launch_bounds__(kTopkThreads) topk_pair_kernel(
       if (srow) srow[slot] = f;
     }
   }
+  // neither CTA exits while a value it sent may still be in flight to the
+  // other (no data: a relaxed arrive)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  cl_wait();
 }
 
 __global__ void window_indices_kernel(const int32_t* __restrict__ pos, int32_t* __restrict__ idx, int64_t ld,
