@@ -74,8 +74,10 @@ def _exit_worker(rank, world, port, result_dir, leave_rank, leave_step):
     from oracle_backend import OracleOps
     from seqsplit_case import load_shard, make_case
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    # the rendezvous store lives in the test process, so the rank that
+    # leaves (rank 0 included) takes no store down with it
+    store = dist.TCPStore("127.0.0.1", port, is_master=False, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world, timeout=timedelta(seconds=5))
     res = "ok"
     t0 = time.time()
     try:
@@ -106,7 +108,9 @@ def test_seq_split_rank_exit_fails_the_others(tmp_path, world, leave_rank):
     next exchange raise (within the process-group timeout), not hang and not
     return a wrong result."""
     ctx = mp.get_context("spawn")
-    port = _free_port()
+    from datetime import timedelta
+    store = dist.TCPStore("127.0.0.1", 0, is_master=True, wait_for_workers=False, timeout=timedelta(seconds=60))
+    port = store.port
     procs = [ctx.Process(target=_exit_worker, args=(r, world, port, str(tmp_path), leave_rank, 2))
              for r in range(world)]
     for p in procs:
